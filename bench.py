@@ -1,0 +1,382 @@
+"""Benchmark: the int4 decode weight stream on B200.
+
+One step = one decode token's full weight stream: for each of the 48 layers the
+q, k, v, o, gate, up and down int4 GEMVs, then lm_head -- 337 GEMVs reading
+6,617,825,280 bytes of packed weights + f16 scales (6,250,168,320 with
+``--scales fp8``), each with its own f16 N(0, 1) activation vector and f16
+output.  Weights are N(0, 0.02) quantised exactly as the engine's quant()
+does, on the GPU.  The working set (6.6 GB) is ~50x the 126 MB L2, so every
+step streams from HBM; no L2 flush is needed.
+
+Reported (one JSON line from rank 0):
+  value      whole-job GB/s (algorithmic bytes / device time), step replayed
+             as one CUDA graph with the inputs resident in HBM
+  e2e        the same metric through the public API with host buffers: each
+             step copies its activations from pinned host memory and the
+             outputs back, inside the timed region
+  roofline   the GEMV kernel's achieved GB/s (algorithmic bytes of its launches
+             / their CUDA-event durations, one eager pass of the timed steps)
+             against the measured HBM copy bandwidth
+  cpu_baseline  the CPU oracle (oracle/g4b_oracle.c) on the host cores, on a
+             bounded sample of the same stream (rank 0, N=1)
+
+``--impl reference`` times the reference's path on the host cores instead (the
+oracle restatement of the shaders; the shaders themselves need a Vulkan stack
+that these machines do not have).
+
+Multi-GPU (torchrun, one rank per GPU): every rank streams its own copy of the
+model for its own token (independent decode streams, no data-path
+collective), so the per-GPU work is fixed: "scaling": "weak".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "gemma4-12b-snapdragonx2elite_b200"))
+
+HIDDEN, FFN, LAYERS, VOCAB = 3840, 15360, 48, 262144
+NQ, NKV = 16 * 256, 8 * 256
+LAYER_SHAPES = [("q", NQ, HIDDEN), ("k", NKV, HIDDEN), ("v", NKV, HIDDEN), ("o", HIDDEN, NQ),
+                ("gate", FFN, HIDDEN), ("up", FFN, HIDDEN), ("down", HIDDEN, FFN)]
+LM_HEAD = ("lm_head", VOCAB, HIDDEN)
+
+
+def stream_shapes(layers=LAYERS):
+    out = []
+    for li in range(layers):
+        out += [(f"L{li}.{n}", N, K) for (n, N, K) in LAYER_SHAPES]
+    out.append(LM_HEAD)
+    return out
+
+
+def weight_bytes(N, K, fp8):
+    return N * K // 2 + (K // 32) * N * (1 if fp8 else 2)
+
+
+def gemv_bytes(N, K, fp8):
+    """Algorithmic bytes of one GEMV: packed weights + scales + f16 x + f16 y."""
+    return weight_bytes(N, K, fp8) + 2 * K + 2 * N
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            self.path = f"/tmp/g4b_clocks_{os.getpid()}.csv"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        except Exception:
+            return None
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------- model setup
+def build_model(torch, ops, qz, device, fp8, layers):
+    """Quantise N(0, 0.02) weights on the GPU into the engine's packed layout."""
+    model = []
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    for name, N, K in stream_shapes(layers):
+        W = torch.randn((N, K), generator=gen, device=device, dtype=torch.float32).mul_(0.02)
+        model.append((name, qz.quant_device(W, pf=False, fp8=fp8, prefill_i8=False)))
+        del W
+    return model
+
+
+def run_cpu_baseline(model_host_fn, fp8, seconds, oracle):
+    """Oracle GEMVs over the stream in order until `seconds` have elapsed."""
+    done = 0
+    t0 = time.perf_counter()
+    n = 0
+    for name, N, K, wp, sc, inv in model_host_fn():
+        x = np.random.default_rng(n).standard_normal(K).astype(np.float16).astype(np.float32)
+        oracle.gemv(x, wp, sc, 1 if fp8 else 0, inv, N, K, 1)
+        done += gemv_bytes(N, K, fp8)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return done / dt / 1e9, n, done, dt
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--scales", default="f16", choices=["f16", "fp8"])
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    fp8 = args.scales == "fp8"
+    metric = "int4 GEMV HBM GB/s (decode weight stream, 48 layers + lm_head, batch 1)"
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    config = {"workload": "configs[1]: decode weight stream, 48 layers + lm_head, batch 1",
+              "scales": args.scales, "layers": args.layers, "activations": "f16 N(0,1) per GEMV",
+              "weights": "N(0,0.02) -> int4, 32-blocks", "l2": "working set 6.6 GB > 126 MB L2, no flush needed",
+              "parallelism": f"replicas{world}"}
+
+    if args.impl == "reference":
+        return run_reference_arm(args, metric, config, rank, world, fp8)
+
+    import torch
+    import torch.distributed as dist
+    from g4b import _lib as L
+    from g4b import ops
+    from g4b import quant_gpu as qz
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    L.load()
+
+    model = build_model(torch, ops, qz, device, fp8, args.layers)
+    shapes = [(name, w.N, w.K) for name, w in model]
+    step_bytes = sum(gemv_bytes(N, K, fp8) for _, N, K in shapes)
+    # per-GEMV activations (f16 N(0,1)) and outputs, resident in HBM
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1 + rank)
+    xs = [torch.randn((w.K,), generator=gen, device=device).to(torch.float16) for _, w in model]
+    ys = [torch.empty((w.N,), device=device, dtype=torch.float16) for _, w in model]
+    stream = torch.cuda.Stream(device)
+    ws = torch.zeros(max(ops.gemv_workspace_bytes(1, w.N, w.K, 0) for _, w in model) + 256,
+                     dtype=torch.uint8, device=device)
+
+    def step():
+        for (_, w), x, y in zip(model, xs, ys):
+            ops.gemv_i4(x, w, out=y, stream=stream, workspace=ws)
+
+    # warm-up and graph capture
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- timed region: K graph replays
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    launches0 = L.launches()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record(stream)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    ms = max_over_ranks(ms)
+    launches_per_step = len(model)
+    ms_step = ms / args.steps
+    value = world * step_bytes / (ms_step / 1e3) / 1e9
+
+    # ---- roofline pass: the same steps launched eagerly, CUDA events per GEMV
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in model]
+    kern_ms = 0.0
+    kern_bytes = 0
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            for i, ((_, w), x, y) in enumerate(zip(model, xs, ys)):
+                evs[i][0].record(stream)
+                ops.gemv_i4(x, w, out=y, stream=stream, workspace=ws)
+                evs[i][1].record(stream)
+            stream.synchronize()
+            kern_ms += sum(a.elapsed_time(b) for a, b in evs)
+            kern_bytes += step_bytes
+    kern_gbs = kern_bytes / (kern_ms / 1e3) / 1e9
+    peak = None
+    peak_src = "of fallback"
+    try:
+        peak = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["hbm_gbs"])
+        peak_src = "of measured"
+    except Exception:
+        peak = 6650.0
+    roofline = {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(kern_gbs / peak, 4), "traffic": None, "peak_source": peak_src,
+                "kernel": "gemv_i4_kernel", "launches_timed": args.steps * len(model),
+                "avg_launch_us": round(kern_ms * 1e3 / (args.steps * len(model)), 2)}
+    tp = os.path.join(REPO, "profiles", "gemv_traffic.json")
+    if os.path.exists(tp):
+        try:
+            t = json.load(open(tp))
+            roofline["traffic"] = t.get("bytes_per_launch_scaled")
+            roofline["traffic_note"] = t.get("note")
+        except Exception:
+            pass
+
+    # ---- e2e: host buffers through the public API, copies inside the timed region
+    xs_h = [x.cpu().pin_memory() for x in xs]
+    ys_h = [torch.empty(y.shape, dtype=y.dtype).pin_memory() for y in ys]
+    h2d = sum(x.numel() * 2 for x in xs)
+    d2h = sum(y.numel() * 2 for y in ys)
+
+    def e2e_step():
+        for xh, x in zip(xs_h, xs):
+            x.copy_(xh, non_blocking=True)
+        step()
+        for yh, y in zip(ys_h, ys):
+            yh.copy_(y, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+        stream.synchronize()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+            stream.synchronize()            # the caller reads its result every step
+        e2e_s = time.perf_counter() - t0
+    e2e_s = max_over_ranks(e2e_s)
+    e2e_val = world * step_bytes * args.steps / e2e_s / 1e9
+
+    # ---- CPU baseline: rank 0 at N = 1 only
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle as O
+
+        def host_model():
+            for name, w in model:
+                wp = w.wp.cpu().numpy().view(np.uint32)
+                sc = w.scales.cpu().numpy()
+                sc = sc.view(np.uint16) if not fp8 else sc
+                yield name, w.N, w.K, wp, sc, w.inv
+
+        gbs, n, done, dt = run_cpu_baseline(host_model, fp8, args.cpu_seconds, O)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"oracle gemv over the first {n} GEMVs of the stream in order "
+                         f"({done / 1e9:.2f} GB in {dt:.1f} s, OpenMP over output columns)"}
+
+    if rank == 0:
+        out = {"metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+               "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+               "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+               "dtype": "int4 x f16 -> f32 acc", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+               "config": config, "roofline": roofline, "cpu_baseline": cpu,
+               "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                       "d2h_bytes_per_step": d2h},
+               "gpu_launches": launches_per_step * args.steps, "clocks": clk,
+               "bytes_per_step": step_bytes}
+        print(json.dumps(out), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference_arm(args, metric, config, rank, world, fp8):
+    """The reference's path on the host cores: the oracle restatement of
+    vk/gemv.comp (+ reduce.comp) over one layer's seven GEMVs per step."""
+    if rank != 0:
+        return
+    import oracle as O
+
+    layer = []
+    for name, N, K in LAYER_SHAPES:
+        W = (np.random.default_rng(len(layer)).standard_normal((N, K)) * 0.02).astype(np.float32)
+        r = O.pack_reference(W, fp8=fp8)
+        layer.append((name, N, K, r["wp"], r["scales"], r["inv"], r["split"]))
+        del W
+    xs = [np.random.default_rng(100 + i).standard_normal(K).astype(np.float16).astype(np.float32)
+          for i, (_, N, K, *_r) in enumerate(layer)]
+    step_bytes = sum(gemv_bytes(N, K, fp8) for _, N, K, *_r in layer)
+
+    def step():
+        for (name, N, K, wp, sc, inv, split), x in zip(layer, xs):
+            O.gemv(x, wp, sc, 1 if fp8 else 0, inv, N, K, split)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = time.perf_counter() - t0
+    val = step_bytes * args.steps / dt / 1e9
+    out = {"metric": metric, "value": round(val, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "int4 x f32 -> f32 acc", "data": "synthetic",
+           "config": config, "impl": "reference",
+           "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+                            "sample": "one layer's seven GEMVs per step (q,k,v,o,gate,up,down; "
+                                      f"{step_bytes / 1e6:.1f} MB), oracle restatement of vk/gemv.comp + "
+                                      "vk/reduce.comp with the reference split"},
+           "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "note": "the reference's GLSL shaders need a Vulkan stack (unavailable on this box); its CPU "
+                   "path for this op is timed through the oracle port"}
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

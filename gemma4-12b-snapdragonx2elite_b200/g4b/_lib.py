@@ -1,0 +1,128 @@
+"""ctypes binding of the C ABI declared in ``include/g4b.h``.
+
+The library is ``libg4b.so`` next to this file, built in-tree by
+``g4b._build``.  If it is missing it is built on first use when nvcc is
+available; otherwise loading fails loudly -- there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+
+from . import _build
+
+# status codes (include/g4b.h)
+G4B_OK = 0
+G4B_E_SHAPE = -1
+G4B_E_ALIGN = -2
+G4B_E_ARCH = -3
+G4B_E_CUDA = -4
+G4B_E_FAULT_INJECTED = -5
+G4B_E_ARG = -6
+G4B_E_WORKSPACE = -7
+G4B_E_TIMEOUT = -8
+
+DT_F32 = 0
+DT_F16 = 1
+SCALE_F16 = 0
+SCALE_E4M3 = 1
+
+Q_VERSION = 0
+Q_DEVICE_OK = 1
+Q_SM_COUNT = 2
+Q_LAUNCHES = 3
+Q_FAULT_COUNTER = 4
+
+_STATUS_NAMES = {
+    G4B_E_SHAPE: "G4B_E_SHAPE", G4B_E_ALIGN: "G4B_E_ALIGN", G4B_E_ARCH: "G4B_E_ARCH",
+    G4B_E_CUDA: "G4B_E_CUDA", G4B_E_FAULT_INJECTED: "G4B_E_FAULT_INJECTED", G4B_E_ARG: "G4B_E_ARG",
+    G4B_E_WORKSPACE: "G4B_E_WORKSPACE", G4B_E_TIMEOUT: "G4B_E_TIMEOUT",
+}
+
+# The entry points declared in include/g4b.h: name -> (restype, argtypes)
+_P = C.c_void_p
+_I = C.c_int
+_F = C.c_float
+_Z = C.c_size_t
+SIGNATURES = {
+    "g4b_last_error": (C.c_char_p, []),
+    "g4b_version": (_I, []),
+    "g4b_query": (C.c_longlong, [_I]),
+    "g4b_stream_wait": (_I, [_P, _I]),
+    "g4b_gemv_workspace_bytes": (_Z, [_I, _I, _I, _I]),
+    "g4b_gemv_i4": (_I, [_P, _I, _I, _P, _P, _I, _F, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "g4b_reduce_partials": (_I, [_P, _P, _I, _I, _P]),
+    "g4b_dequant_i4": (_I, [_P, _P, _I, _F, _P, _I, _I, _I, _P]),
+    "g4b_cast": (_I, [_P, _I, _P, _I, _Z, _P]),
+    "g4b_cast_i8": (_I, [_P, _I, _P, _P, _I, _I, _P]),
+    "g4b_quant_i4": (_I, [_P, _I, _I, _P, _P, _P, _P, _P]),
+    "g4b_quant_e4m3": (_I, [_P, _I, _I, _I, _P, _P]),
+    "g4b_quant_w8a8": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
+}
+
+
+class G4BError(RuntimeError):
+    """A g4b entry point returned a negative status."""
+
+    def __init__(self, op: str, code: int, msg: str):
+        super().__init__(f"{op} failed with {_STATUS_NAMES.get(code, code)}: {msg}")
+        self.op = op
+        self.code = code
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib_path() -> str:
+    return _build.LIB_PATH
+
+
+def load(build_if_missing: bool = True):
+    """Load (building if needed) the CUDA library and bind its signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB_PATH
+        if not os.path.exists(path) or (build_if_missing and not _build.up_to_date()
+                                        and _nvcc_available()):
+            if not build_if_missing:
+                raise ImportError(f"g4b CUDA library not built: {path} is missing")
+            _build.build()
+        L = C.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _nvcc_available() -> bool:
+    try:
+        _build.nvcc_path()
+        return True
+    except RuntimeError:
+        return False
+
+
+def last_error() -> str:
+    return load().g4b_last_error().decode(errors="replace")
+
+
+def check(op: str, status: int) -> None:
+    if status != G4B_OK:
+        raise G4BError(op, status, last_error())
+
+
+def query(what: int) -> int:
+    return int(load().g4b_query(what))
+
+
+def launches() -> int:
+    """Kernels launched through the library by this process so far."""
+    return query(Q_LAUNCHES)

@@ -1,0 +1,169 @@
+"""torch-tensor front end of the g4b CUDA library.
+
+PyTorch provides device memory, streams and the tensors' pointers; every
+computation runs in the CUDA library through its C ABI (``include/g4b.h``).
+If the library cannot be loaded these functions raise -- there is no CPU or
+PyTorch fallback.
+"""
+from __future__ import annotations
+
+import threading
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .pack import PackedWeight, w4a8_ratio
+
+_DT = {torch.float32: L.DT_F32, torch.float16: L.DT_F16}
+
+
+def _stream_handle(stream: Optional[torch.cuda.Stream], device: torch.device) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return int(s.cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else int(t.data_ptr())
+
+
+def _need(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+@dataclass
+class DeviceWeight:
+    """One packed linear layer resident in HBM (the reference's Buf set for a layer)."""
+    N: int
+    K: int
+    nblk: int
+    split: int
+    scale_fmt: int
+    inv: float
+    wp: torch.Tensor                      # [K, N/8] int32 (bit pattern of the uint32 words)
+    scales: torch.Tensor                  # [nblk, N] float16 or uint8
+    scales16: torch.Tensor                # [nblk, N] float16
+    w8: Optional[torch.Tensor] = None     # [K, N] int8
+    sw8: Optional[torch.Tensor] = None    # [N] float16
+    ratio16: Optional[torch.Tensor] = None  # [nblk, N] float16 (W4A8)
+
+    @property
+    def weight_bytes(self) -> int:
+        return self.wp.numel() * 4 + self.scales.numel() * self.scales.element_size()
+
+
+def to_device(pw: PackedWeight, device="cuda", w4a8: bool = False) -> DeviceWeight:
+    dev = torch.device(device)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    dw = DeviceWeight(N=pw.N, K=pw.K, nblk=pw.nblk, split=pw.split, scale_fmt=pw.scale_fmt, inv=pw.inv,
+                      wp=t(pw.wp.view(np.int32)), scales=t(pw.scales), scales16=t(pw.scales16))
+    if pw.w8 is not None:
+        dw.w8 = t(pw.w8)
+        dw.sw8 = t(pw.sw8)
+        if w4a8 and pw.sw_f32 is not None and pw.sc_f32 is not None:
+            dw.ratio16 = t(w4a8_ratio(pw.sc_f32, pw.sw_f32))
+    return dw
+
+
+# ------------------------------------------------------------------ workspace
+class _Workspaces:
+    """Zero-filled scratch per (device, stream), grown on demand (never on a hot
+    path once warmed up: the same size is reused)."""
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self._bufs: dict = {}
+
+    def get(self, device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+        key = (device.index, stream)
+        with self._lock:
+            buf = self._bufs.get(key)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                self._bufs[key] = buf
+            return buf
+
+
+WORKSPACES = _Workspaces()
+
+
+# ----------------------------------------------------------------------- ops
+def gemv_workspace_bytes(M: int, N: int, K: int, split: int = 0) -> int:
+    return int(L.load().g4b_gemv_workspace_bytes(M, N, K, split))
+
+
+def gemv_i4(x: torch.Tensor, w: DeviceWeight, split: int = 0, out: Optional[torch.Tensor] = None,
+            out_dtype: torch.dtype = torch.float32, stream: Optional[torch.cuda.Stream] = None,
+            workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ dequant(W).T for x [K] or [M, K] (M <= 8 per kernel; larger M loops)."""
+    _need(x, "x")
+    squeeze = x.dim() == 1
+    x2 = x.view(1, -1) if squeeze else x
+    M, K = x2.shape
+    if K != w.K:
+        raise ValueError(f"gemv_i4: x has K={K}, weight has K={w.K}")
+    if out is None:
+        out = torch.empty((M, w.N), dtype=out_dtype, device=x.device)
+    _need(out, "out")
+    sh = _stream_handle(stream, x.device)
+    lib = L.load()
+    need = lib.g4b_gemv_workspace_bytes(M, w.N, w.K, split)
+    ws = workspace
+    if need and ws is None:
+        ws = WORKSPACES.get(x.device, sh, need)
+    L.check("g4b_gemv_i4", lib.g4b_gemv_i4(
+        _ptr(x2), _DT[x2.dtype], M, _ptr(w.wp), _ptr(w.scales), w.scale_fmt, w.inv,
+        _ptr(out), _DT[out.dtype], w.N, w.K, split, _ptr(ws), ws.numel() if ws is not None else 0, sh))
+    return out.view(-1) if squeeze else out
+
+
+def reduce_partials(partial: torch.Tensor, split: int, out: Optional[torch.Tensor] = None,
+                    stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    _need(partial, "partial")
+    N = partial.numel() // split
+    if out is None:
+        out = torch.empty((N,), dtype=torch.float32, device=partial.device)
+    L.check("g4b_reduce_partials", L.load().g4b_reduce_partials(
+        _ptr(partial), _ptr(out), N, split, _stream_handle(stream, partial.device)))
+    return out
+
+
+def dequant_i4(w: DeviceWeight, out_dtype: torch.dtype = torch.float16,
+               stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    out = torch.empty((w.K, w.N), dtype=out_dtype, device=w.wp.device)
+    L.check("g4b_dequant_i4", L.load().g4b_dequant_i4(
+        _ptr(w.wp), _ptr(w.scales), w.scale_fmt, w.inv, _ptr(out), _DT[out_dtype], w.N, w.K,
+        _stream_handle(stream, out.device)))
+    return out
+
+
+def cast(x: torch.Tensor, dtype: torch.dtype, out: Optional[torch.Tensor] = None,
+         stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    _need(x, "x")
+    if out is None:
+        out = torch.empty(x.shape, dtype=dtype, device=x.device)
+    L.check("g4b_cast", L.load().g4b_cast(_ptr(x), _DT[x.dtype], _ptr(out), _DT[out.dtype], x.numel(),
+                                          _stream_handle(stream, x.device)))
+    return out
+
+
+def cast_i8(X: torch.Tensor, stream: Optional[torch.cuda.Stream] = None):
+    """Per-token int8 quantisation -> (A8 [M, K] int8, sa [M] f32)."""
+    _need(X, "X")
+    M, K = X.shape
+    A8 = torch.empty((M, K), dtype=torch.int8, device=X.device)
+    sa = torch.empty((M,), dtype=torch.float32, device=X.device)
+    L.check("g4b_cast_i8", L.load().g4b_cast_i8(_ptr(X), _DT[X.dtype], _ptr(A8), _ptr(sa), M, K,
+                                                _stream_handle(stream, X.device)))
+    return A8, sa
+
+
+def stream_wait(stream: Optional[torch.cuda.Stream] = None, timeout_ms: int = 0) -> None:
+    """Bounded wait for a stream (the engine's fence wait with a timeout)."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    L.check("g4b_stream_wait", L.load().g4b_stream_wait(_stream_handle(stream, dev), int(timeout_ms)))

@@ -1,0 +1,173 @@
+/*
+ * g4b.h -- C ABI of the B200 (sm_100a) int4/int8 quantized-weight matmul library.
+ *
+ * Drop-in for the quantized-weight dispatches of gemma4-adreno's Vulkan engine
+ * (src/vk_engine.py).  The reference binds these kernels through Vulkan
+ * descriptor sets plus a std140 uniform; each entry point below replaces one
+ * such dispatch (or dispatch pair) and takes the same buffers and sizes as plain
+ * device pointers.  Every reference citation is file:line within the reference
+ * project.
+ *
+ * Conventions (all entry points):
+ *   - All array pointers are DEVICE pointers owned by the caller.  Calls are
+ *     stream-ordered and asynchronous on `stream` (NULL = the legacy default
+ *     stream); none synchronises the device or allocates device memory.
+ *   - Return 0 (G4B_OK) on success, a negative G4B_E_* code otherwise.  On
+ *     error nothing was launched and g4b_last_error() (per host thread) says why.
+ *   - Layouts are the reference's packing layout (src/vk_engine.py:125-159):
+ *       wp      [K, N/8] uint32, nibble j of word (k, g) = column 8g+j, value q in
+ *               [0,15] standing for the weight (q - 8) * scale
+ *       scales  [K/32, N] f16 (G4B_SCALE_F16) or e4m3 bytes (G4B_SCALE_E4M3)
+ *       int8 W  [K, N] int8, row-major (the W8A8 prefill weights)
+ *     Activations are row-major [M, K]; outputs row-major [M, N].
+ *   - Pointers must be 16-byte aligned; N % 16 == 0; K % 32 == 0 (one scale
+ *     block), as the reference requires (src/vk_engine.py:126, 219).
+ *   - Thread safety: calls on distinct streams from distinct host threads are
+ *     safe; a workspace must not be shared by calls that can overlap on the GPU.
+ */
+#ifndef G4B_H
+#define G4B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* exported symbols (the library is built with hidden visibility otherwise) */
+#if defined(G4B_BUILDING) && defined(__GNUC__)
+#define G4B_API __attribute__((visibility("default")))
+#else
+#define G4B_API
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers */
+typedef struct CUstream_st* g4b_stream_t;
+
+/* ----------------------------------------------------------------- status */
+#define G4B_OK                 0
+#define G4B_E_SHAPE           -1  /* unsupported or inconsistent sizes          */
+#define G4B_E_ALIGN           -2  /* a pointer is not 16-byte aligned            */
+#define G4B_E_ARCH            -3  /* current device is not an sm_100 GPU         */
+#define G4B_E_CUDA            -4  /* a CUDA runtime call failed                  */
+#define G4B_E_FAULT_INJECTED  -5  /* G4B_FAULT asked this call to fail           */
+#define G4B_E_ARG             -6  /* bad enum value or NULL pointer              */
+#define G4B_E_WORKSPACE       -7  /* workspace missing or too small              */
+#define G4B_E_TIMEOUT         -8  /* g4b_stream_wait gave up                     */
+
+/* ------------------------------------------------------------- enumerations */
+#define G4B_DT_F32  0
+#define G4B_DT_F16  1
+
+#define G4B_SCALE_F16   0   /* scales [K/32, N] f16: the reference's default          */
+#define G4B_SCALE_E4M3  1   /* scales [K/32, N] float8 e4m3fn bytes (GEMV_FP8=1)       */
+
+/* g4b_query() selectors */
+#define G4B_Q_VERSION        0  /* library version, major*10000 + minor*100 + patch */
+#define G4B_Q_DEVICE_OK      1  /* 1 if the current device can run the kernels     */
+#define G4B_Q_SM_COUNT       2  /* streaming multiprocessors on the current device */
+#define G4B_Q_LAUNCHES       3  /* kernels this process has launched through g4b   */
+#define G4B_Q_FAULT_COUNTER  4  /* calls seen by the fault injector                */
+
+/* --------------------------------------------------------------- utilities */
+/* Message for the last failing call on this host thread ("" if none). */
+G4B_API const char* g4b_last_error(void);
+
+/* Library version as major*10000 + minor*100 + patch. */
+G4B_API int g4b_version(void);
+
+/* Integer facts about the library and the current device (G4B_Q_*); -1 on error. */
+G4B_API long long g4b_query(int what);
+
+/* Wait for all work queued on `stream` with a host-side time limit, the
+ * counterpart of the engine's fence wait with GEMMA4_FENCE_TIMEOUT_MS
+ * (src/vk_engine.py:294-302).  timeout_ms <= 0 waits without limit.
+ * Returns G4B_E_TIMEOUT (work still running) or G4B_E_CUDA (the stream failed). */
+G4B_API int g4b_stream_wait(g4b_stream_t stream, int timeout_ms);
+
+/* ------------------------------------------------------------ decode GEMV */
+/* Bytes of workspace g4b_gemv_i4 needs for these sizes.  `split` as passed to
+ * g4b_gemv_i4 (0 = the library chooses).  0 means no workspace is needed. */
+G4B_API size_t g4b_gemv_workspace_bytes(int M, int N, int K, int split);
+
+/* int4 block-scaled GEMV (M = 1) or small-batch GEMM (M <= 8 tokens):
+ *     y[m, n] = sum_k x[m, k] * (q[k, n] - 8) * scale[k/32, n]   (* inv for e4m3)
+ * Replaces one gemv (+ reduce) dispatch pair recorded by gemv() with the
+ * descriptor set from gemv_ds() (src/vk_engine.py:214-226, 270-272): the
+ * shaders vk/gemv.comp:11-33, vk/gemv_fp8.comp:20-40 and vk/reduce.comp:8-12.
+ *   x        [M, K] f32 or f16 (x_dtype)
+ *   scales   f16 or e4m3 per scale_fmt; inv is the e4m3 scales' 2^-shift
+ *            (ignored for f16 scales), the uniform's e.x in the reference
+ *   y        [M, N] f32 or f16 (y_dtype); f32 accumulation throughout
+ *   split    number of K-slices (must divide K/32), the reference's `split`
+ *            from quant(); 0 lets the library pick one for the B200's SMs
+ *   workspace  device scratch of g4b_gemv_workspace_bytes() bytes (NULL if that
+ *            is 0), zero-filled once when allocated: it holds the K-slice
+ *            partial sums and per-tile arrival counters, and every call leaves
+ *            the counters at zero again.
+ * The K-slice partials are summed in slice order, so results are deterministic. */
+G4B_API int g4b_gemv_i4(const void* x, int x_dtype, int M,
+                const uint32_t* wp, const void* scales, int scale_fmt, float inv,
+                void* y, int y_dtype, int N, int K, int split,
+                void* workspace, size_t ws_bytes, g4b_stream_t stream);
+
+/* Split-K partial reduction, vk/reduce.comp:8-12:
+ *     y[n] = sum_{c=0}^{split-1} partial[c*N + n]   (c ascending, f32)
+ * Exposed on its own for parity with the reference's reduce dispatch
+ * (src/vk_engine.py:223-226, 272); g4b_gemv_i4 performs it internally. */
+G4B_API int g4b_reduce_partials(const float* partial, float* y, int N, int split, g4b_stream_t stream);
+
+/* Dequantise packed int4 weights to a dense [K, N] matrix:
+ *   out_dtype F16, scale_fmt F16 : f16((q - 8) * f32(scale))  -- bit-exact the
+ *       tile vk/coopgemm_i4h.comp:19-25 writes to shared memory
+ *   out_dtype F32                : (q - 8) * f32(scale), exact in f32
+ * With scale_fmt E4M3 the scale is decoded as vk/gemv_fp8.comp:14-18 and the
+ * product is multiplied by inv (a power of two, so still exact). */
+G4B_API int g4b_dequant_i4(const uint32_t* wp, const void* scales, int scale_fmt, float inv,
+                   void* out, int out_dtype, int N, int K, g4b_stream_t stream);
+
+/* ------------------------------------------------------------ weight packing */
+/* The engine's int4 packing, quant() (src/vk_engine.py:126-131), on the GPU,
+ * bit-exact to the host packer:  W [N, K] f32 (row-major, HF layout) ->
+ *   scale[n, b] = max(max_{k in block b} |W[n,k]| / 7, 1e-8)           (f32)
+ *   q = clip(round_half_even(W / scale) + 8, 0, 15) packed into wp [K, N/8]
+ *   scales_f16 [K/32, N] = f16(scale)
+ * scales_f32 (nullable) receives the f32 scales as [N, K/32] (the input of
+ * g4b_quant_e4m3 / g4b_quant_w8a8); amax_bits (nullable, initialised by the
+ * caller to 0) receives atomicMax of the scales' f32 bit patterns: the
+ * tensor-wide max scale the e4m3 shift is computed from.  N % 8, K % 32. */
+G4B_API int g4b_quant_i4(const float* W, int N, int K, uint32_t* wp, uint16_t* scales_f16,
+                         float* scales_f32, uint32_t* amax_bits, g4b_stream_t stream);
+
+/* e4m3 scales for GEMV_FP8 (src/vk_engine.py:133-137): with the caller's
+ * shift = floor(log2(256 / max scale)) (inv = 2^-shift),
+ *   scales_e4m3[b, n] = e4m3_rne(clip(scale[n, b] * 2^shift, 0, 448))
+ * scales_f32 is the [N, K/32] output of g4b_quant_i4. */
+G4B_API int g4b_quant_e4m3(const float* scales_f32, int N, int K, int shift, uint8_t* scales_e4m3,
+                           g4b_stream_t stream);
+
+/* W8A8 prefill weights (src/vk_engine.py:152-157) from the packed int4 ones:
+ *   deq = (q - 8) * scale (f32);  s_w[n] = max(max_k |deq[n,k]| / 127, 1e-12)
+ *   w8 [K, N] int8 = clip(round_half_even(deq / s_w), -127, 127);  sw_f16 = f16(s_w)
+ * sw_f32 (nullable) receives s_w; ratio_f16 (nullable, [K/32, N]) receives the
+ * W4A8 requant ratio f16(scale / s_w) (benchmarks/coopgemm_w4a8.py:84). */
+G4B_API int g4b_quant_w8a8(const uint32_t* wp, const float* scales_f32, int N, int K, int8_t* w8,
+                           uint16_t* sw_f16, float* sw_f32, uint16_t* ratio_f16, g4b_stream_t stream);
+
+/* ------------------------------------------------------------ prefill path */
+/* Element-wise f32 <-> f16 conversion (round-to-nearest-even), the engine's
+ * vk/cast_dn.comp:7 (f32 -> f16) and vk/cast_up.comp:7 (f16 -> f32) dispatches
+ * around each prefill GEMM (src/vk_engine.py:398-400). */
+G4B_API int g4b_cast(const void* src, int src_dtype, void* dst, int dst_dtype, size_t n, g4b_stream_t stream);
+
+/* Per-token int8 activation quantiser, vk/cast_i8.comp:11-19 (dispatched by
+ * gmm() under PREFILL_I8, src/vk_engine.py:392-394):
+ *     s = max(max_k |X[m,k]| / 127, 1e-12);  inv = 1/s  (both correctly rounded)
+ *     A8[m,k] = clamp(round_half_even(X[m,k] * inv), -127, 127);  sa[m] = s   */
+G4B_API int g4b_cast_i8(const void* X, int x_dtype, int8_t* A8, float* sa, int M, int K, g4b_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* G4B_H */
