@@ -67,6 +67,35 @@ def gemv_bytes(N, K, fp8):
     return weight_bytes(N, K, fp8) + 2 * K + 2 * N
 
 
+# ------------------------------------------------------ per-kernel CUDA events
+class GraphEvents:
+    """CUDA events recorded as event-record nodes inside a captured graph
+    (cudaEventRecordWithFlags(..., cudaEventRecordExternal)), so each kernel's
+    duration is measured on its own stream without the host in the loop."""
+
+    def __init__(self, n):
+        import ctypes
+        self.C = ctypes
+        self.rt = ctypes.CDLL("libcudart.so.12")
+        self.ev = []
+        for _ in range(2 * n):
+            e = ctypes.c_void_p()
+            assert self.rt.cudaEventCreateWithFlags(ctypes.byref(e), 0) == 0
+            self.ev.append(e)
+
+    def record(self, i, stream_handle):
+        assert self.rt.cudaEventRecordWithFlags(self.ev[i], self.C.c_void_p(stream_handle), 1) == 0
+
+    def elapsed_ms(self, i, j):
+        ms = self.C.c_float()
+        assert self.rt.cudaEventElapsedTime(self.C.byref(ms), self.ev[i], self.ev[j]) == 0
+        return ms.value
+
+    def close(self):
+        for e in self.ev:
+            self.rt.cudaEventDestroy(e)
+
+
 # ----------------------------------------------------------------- clocks
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled during the timed region."""
@@ -129,20 +158,21 @@ def build_model(torch, ops, qz, device, fp8, layers):
     return model
 
 
-def run_cpu_baseline(model_host_fn, fp8, seconds, oracle):
-    """Oracle GEMVs over the stream in order until `seconds` have elapsed."""
+def run_cpu_baseline(host_entries, fp8, seconds, oracle):
+    """Oracle GEMVs cycling over `host_entries` (the stream's first matrices, in
+    order) until `seconds` of CPU time have elapsed."""
     done = 0
-    t0 = time.perf_counter()
     n = 0
-    for name, N, K, wp, sc, inv in model_host_fn():
-        x = np.random.default_rng(n).standard_normal(K).astype(np.float16).astype(np.float32)
-        oracle.gemv(x, wp, sc, 1 if fp8 else 0, inv, N, K, 1)
-        done += gemv_bytes(N, K, fp8)
-        n += 1
-        if time.perf_counter() - t0 >= seconds:
-            break
-    dt = time.perf_counter() - t0
-    return done / dt / 1e9, n, done, dt
+    t0 = time.perf_counter()
+    while True:
+        for name, N, K, wp, sc, inv in host_entries:
+            x = np.random.default_rng(n).standard_normal(K).astype(np.float16).astype(np.float32)
+            oracle.gemv(x, wp, sc, 1 if fp8 else 0, inv, N, K, 1)
+            done += gemv_bytes(N, K, fp8)
+            n += 1
+            if time.perf_counter() - t0 >= seconds:
+                dt = time.perf_counter() - t0
+                return done / dt / 1e9, n, done, dt
 
 
 def main():
@@ -155,6 +185,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="stream", choices=["stream", "gemv"],
+                    help="stream: configs[1] decode weight stream (default); gemv: configs[0] single GEMV")
     args = ap.parse_args()
     fp8 = args.scales == "fp8"
     metric = "int4 GEMV HBM GB/s (decode weight stream, 48 layers + lm_head, batch 1)"
@@ -183,7 +215,23 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     L.load()
 
-    model = build_model(torch, ops, qz, device, fp8, args.layers)
+    if args.workload == "gemv":
+        # one [15360, 3840] GEMV; R weight copies rotated so that
+        # successive launches read different HBM (R * 33 MB > 126 MB L2)
+        R = 8
+        gen = torch.Generator(device=device)
+        gen.manual_seed(0)
+        model = []
+        for r in range(R):
+            W = torch.randn((FFN, HIDDEN), generator=gen, device=device).mul_(0.02)
+            model.append((f"gate.copy{r}", qz.quant_device(W, pf=False, fp8=fp8, prefill_i8=False)))
+            del W
+        config.update({"workload": "configs[0]: one int4 GEMV W[15360, 3840], batch 1, f16 x/y",
+                       "l2": f"{R} weight copies rotated per launch ({R * 33.2:.0f} MB > 126 MB L2)"})
+        config.pop("layers", None)
+        metric = "int4 GEMV HBM GB/s (W[15360, 3840], batch 1)"
+    else:
+        model = build_model(torch, ops, qz, device, fp8, args.layers)
     shapes = [(name, w.N, w.K) for name, w in model]
     step_bytes = sum(gemv_bytes(N, K, fp8) for _, N, K in shapes)
     # per-GEMV activations (f16 N(0,1)) and outputs, resident in HBM
@@ -192,14 +240,19 @@ def main():
     xs = [torch.randn((w.K,), generator=gen, device=device).to(torch.float16) for _, w in model]
     ys = [torch.empty((w.N,), device=device, dtype=torch.float16) for _, w in model]
     stream = torch.cuda.Stream(device)
+    sh = int(stream.cuda_stream)
     ws = torch.zeros(max(ops.gemv_workspace_bytes(1, w.N, w.K, 0) for _, w in model) + 256,
                      dtype=torch.uint8, device=device)
 
-    def step():
-        for (_, w), x, y in zip(model, xs, ys):
-            ops.gemv_i4(x, w, out=y, stream=stream, workspace=ws)
+    def step(gev=None):
+        for i, ((_, w), x, y) in enumerate(zip(model, xs, ys)):
+            if gev is not None:
+                gev.record(2 * i, sh)
+            ops.gemv_i4(x, w, out=y, stream=stream, workspace=ws, pdl=True)
+            if gev is not None:
+                gev.record(2 * i + 1, sh)
 
-    # warm-up and graph capture
+    # warm-up and graph capture (the reference records one command buffer per token)
     with torch.cuda.stream(stream):
         for _ in range(max(1, args.warmup)):
             step()
@@ -207,8 +260,14 @@ def main():
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
-    for _ in range(args.warmup):
-        graph.replay()
+    gev = GraphEvents(len(model))
+    graph_ev = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_ev, stream=stream):
+        step(gev)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+            graph_ev.replay()
     torch.cuda.synchronize()
 
     def barrier():
@@ -223,55 +282,61 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- timed region: K graph replays
+    # ---- timed region: K graph replays on the launching stream
     clocks = ClockSampler(local_rank)
     clocks.start()
-    launches0 = L.launches()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        graph.replay()
-    e1.record(stream)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
     barrier()
     ms = e0.elapsed_time(e1)
-    clk = clocks.stop()
     ms = max_over_ranks(ms)
     launches_per_step = len(model)
     ms_step = ms / args.steps
     value = world * step_bytes / (ms_step / 1e3) / 1e9
 
-    # ---- roofline pass: the same steps launched eagerly, CUDA events per GEMV
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in model]
+    # ---- roofline: the same step with an event-record node around every kernel
     kern_ms = 0.0
     kern_bytes = 0
+    per_shape = {}
     with torch.cuda.stream(stream):
         for _ in range(args.steps):
-            for i, ((_, w), x, y) in enumerate(zip(model, xs, ys)):
-                evs[i][0].record(stream)
-                ops.gemv_i4(x, w, out=y, stream=stream, workspace=ws)
-                evs[i][1].record(stream)
+            graph_ev.replay()
             stream.synchronize()
-            kern_ms += sum(a.elapsed_time(b) for a, b in evs)
-            kern_bytes += step_bytes
+            for i, (name, N, K) in enumerate(shapes):
+                d = gev.elapsed_ms(2 * i, 2 * i + 1)
+                kern_ms += d
+                kern_bytes += gemv_bytes(N, K, fp8)
+                key = f"{N}x{K}"
+                a = per_shape.setdefault(key, [0.0, 0, gemv_bytes(N, K, fp8)])
+                a[0] += d
+                a[1] += 1
+    clk = clocks.stop()
+    gev.close()
     kern_gbs = kern_bytes / (kern_ms / 1e3) / 1e9
     peak = None
-    peak_src = "of fallback"
+    peak_src = "of measured"
     try:
         peak = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["hbm_gbs"])
-        peak_src = "of measured"
     except Exception:
         peak = 6650.0
+        peak_src = "of fallback"
     roofline = {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(kern_gbs / peak, 4), "traffic": None, "peak_source": peak_src,
                 "kernel": "gemv_i4_kernel", "launches_timed": args.steps * len(model),
-                "avg_launch_us": round(kern_ms * 1e3 / (args.steps * len(model)), 2)}
+                "avg_launch_us": round(kern_ms * 1e3 / (args.steps * len(model)), 3),
+                "per_shape_gbs": {k: round(v[2] * v[1] / (v[0] / 1e3) / 1e9, 1) for k, v in per_shape.items()},
+                "graph_vs_kernels": round(ms_step / (kern_ms / args.steps), 4)}
     tp = os.path.join(REPO, "profiles", "gemv_traffic.json")
     if os.path.exists(tp):
         try:
             t = json.load(open(tp))
-            roofline["traffic"] = t.get("bytes_per_launch_scaled")
+            roofline["traffic"] = t.get("bytes_per_launch_scaled", {}).get(args.workload)
             roofline["traffic_note"] = t.get("note")
         except Exception:
             pass
@@ -307,17 +372,19 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle as O
 
-        def host_model():
-            for name, w in model:
-                wp = w.wp.cpu().numpy().view(np.uint32)
-                sc = w.scales.cpu().numpy()
-                sc = sc.view(np.uint16) if not fp8 else sc
-                yield name, w.N, w.K, wp, sc, w.inv
-
-        gbs, n, done, dt = run_cpu_baseline(host_model, fp8, args.cpu_seconds, O)
+        host_entries = []
+        budget = 2 * 10 ** 9                    # host copies of the stream's first ~2 GB of weights
+        for name, w in model:
+            if budget <= 0:
+                break
+            wp = w.wp.cpu().numpy().view(np.uint32)
+            sc = w.scales.cpu().numpy()
+            host_entries.append((name, w.N, w.K, wp, sc.view(np.uint16) if not fp8 else sc, w.inv))
+            budget -= weight_bytes(w.N, w.K, fp8)
+        gbs, n, done, dt = run_cpu_baseline(host_entries, fp8, args.cpu_seconds, O)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
-               "sample": f"oracle gemv over the first {n} GEMVs of the stream in order "
-                         f"({done / 1e9:.2f} GB in {dt:.1f} s, OpenMP over output columns)"}
+               "sample": f"oracle gemv, {n} GEMVs cycling over the workload's first {len(host_entries)} "
+                         f"matrices in order ({done / 1e9:.2f} GB in {dt:.1f} s, OpenMP over output columns)"}
 
     if rank == 0:
         out = {"metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,

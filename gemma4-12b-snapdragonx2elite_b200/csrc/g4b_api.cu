@@ -9,7 +9,10 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <unordered_map>
 #include <vector>
+
+#include <cudaTypedefs.h>
 
 #include "g4b_common.cuh"
 
@@ -107,6 +110,59 @@ int check_device(int* sm_count) {
     return G4B_OK;
 }
 
+// ------------------------------------------------------------- tensor maps
+struct TmapKey {
+    uintptr_t base;
+    uint64_t dim0, dim1, stride1;
+    uint32_t box0, box1, dtype, swizzle;
+    bool operator==(const TmapKey& o) const {
+        return base == o.base && dim0 == o.dim0 && dim1 == o.dim1 && stride1 == o.stride1 && box0 == o.box0 &&
+               box1 == o.box1 && dtype == o.dtype && swizzle == o.swizzle;
+    }
+};
+struct TmapKeyHash {
+    size_t operator()(const TmapKey& k) const {
+        size_t h = std::hash<uint64_t>()(k.base);
+        for (uint64_t v : {k.dim0, k.dim1, k.stride1, (uint64_t)k.box0 << 32 | k.box1, (uint64_t)k.dtype << 8 | k.swizzle})
+            h = h * 1000003u ^ std::hash<uint64_t>()(v);
+        return h;
+    }
+};
+static std::mutex g_tmap_mu;
+static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> g_tmaps;
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
+                  uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle) {
+    TmapKey key{(uintptr_t)base, dim0, dim1, stride1_bytes, box0, box1, (uint32_t)dtype, (uint32_t)swizzle};
+    std::lock_guard<std::mutex> lk(g_tmap_mu);
+    auto it = g_tmaps.find(key);
+    if (it != g_tmaps.end()) {
+        *out = it->second;
+        return G4B_OK;
+    }
+    if (!g_encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+            return fail(G4B_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+        g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint64_t dims[2] = {dim0, dim1};
+    const cuuint64_t strides[1] = {stride1_bytes};
+    const cuuint32_t box[2] = {box0, box1};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap m;
+    CUresult r = g_encode(&m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(G4B_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    if (g_tmaps.size() > 8192) g_tmaps.clear();
+    g_tmaps.emplace(key, m);
+    *out = m;
+    return G4B_OK;
+}
+
 }  // namespace g4b
 
 extern "C" {
@@ -125,6 +181,10 @@ long long g4b_query(int what) {
         }
         case G4B_Q_LAUNCHES: return g4b::g_launches.load();
         case G4B_Q_FAULT_COUNTER: return g4b::g_fault_calls.load();
+        case G4B_Q_KERNEL_STATUS: {
+            if (g4b::check_device(nullptr) != G4B_OK) return -1;
+            return (long long)g4b::read_status_gemv();
+        }
         default: return -1;
     }
 }

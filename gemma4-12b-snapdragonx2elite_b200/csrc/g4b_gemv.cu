@@ -27,15 +27,45 @@
 //     them in slice order (deterministic), scales by inv and writes y -- the
 //     reduce.comp dispatch fused into the GEMV.
 #include <algorithm>
+#include <utility>
 
 #include "g4b_common.cuh"
 
 namespace g4b {
 
+// Launch flags of the current host call (set by g4b_gemv_i4_ex for its duration).
+static thread_local bool t_pdl = false;
+
+// Launch `kern` on `s`, with programmatic dependent launch when t_pdl is set:
+// the grid may then start while the previous kernel in the stream is still
+// running (every kernel here waits with griddepcontrol.wait before it reads
+// activations or writes outputs and workspace).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    if (t_pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 constexpr int kGemvWarps = 4;
 constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kGemvTileN = 256;
 constexpr int kGemvMaxTok = 8;
+// The workspace starts with a fixed region of per-tile arrival counters (so a
+// call never lands its counters on another call's partials), then the partials.
+constexpr int kGemvMaxTiles = 4096;
+constexpr size_t kGemvCounterBytes = kGemvMaxTiles * sizeof(unsigned);
 
 struct GemvArgs {
     const void* x;        // [M, K] f32 or f16
@@ -232,6 +262,8 @@ __device__ __forceinline__ void compute_stage(const Stage<XF32, SFMT, NT>& st, f
 
 template <bool XF32, int SFMT, int NT, bool WIDE, bool YF32>
 __global__ void __launch_bounds__(kGemvThreads, NT == 1 ? 3 : 2) gemv_i4_kernel(GemvArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, q = lane & 3;
     const int tile = blockIdx.x, slice = blockIdx.y;
@@ -315,6 +347,788 @@ __global__ void __launch_bounds__(kGemvThreads, NT == 1 ? 3 : 2) gemv_i4_kernel(
     if (tid == 0) a.counters[tile] = 0u;  // the workspace is ready for the next call
 }
 
+// ============================================================ streaming GEMV
+// A persistent grid (two CTAs per SM).  A producer warp streams weight tiles of
+// [128 rows (4 scale blocks) x 256 columns] into a shared-memory ring with one
+// 2-D TMA load each (plus one TMA load of their 4 x 256 scales), a second
+// producer warp copies the matching activation rows, and 4 consumer warps
+// each run compute_stage() on one of the tile's 32-row blocks.  Work = the
+// (column tile, block quad) items in tile-major order, split into equal
+// contiguous ranges per CTA.  A CTA's share of a tile is reduced across its 4
+// warps in shared memory (in warp order); a tile shared by several CTAs is
+// summed by the last CTA to arrive (per-tile counter), in CTA order, so the
+// result is deterministic.  With a caller-given split the ranges are exactly
+// the reference's K-slices.
+constexpr int kStTN = 256;
+constexpr int kStRows = 128;                         // rows per stage = 4 scale blocks
+constexpr int kStWBytes = kStRows * (kStTN / 2);     // 16 KB of packed weights
+constexpr int kStThreads = 192;                      // warps 0-3 consumers, 4 weights, 5 activations
+constexpr int kStMaxStages = 8;
+
+static __device__ unsigned g_gemv_status;
+
+struct StreamArgs {
+    const void* x;
+    void* y;
+    float* partial;      // [G * maxseg, M, kStTN]
+    unsigned* counters;  // [ntiles]
+    float inv;
+    int M, N, K, nquad, ntiles, L, maxseg, stages, stage_bytes, s_bytes;
+    long long total;
+};
+
+template <bool XF32, int SFMT, int NT, bool YF32>
+__global__ void __launch_bounds__(kStThreads, 2) gemv_i4_stream_kernel(const StreamArgs a,
+                                                                      const __grid_constant__ CUtensorMap wmap,
+                                                                      const __grid_constant__ CUtensorMap smap) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bars[2 * kStMaxStages];
+    __shared__ unsigned s_last;
+    __shared__ int s_issued;
+    __shared__ int s_abort;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    volatile int* abort_flag = &s_abort;
+    const int S = a.stages;
+    const uint32_t smem0 = smem_u32(smem);
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kStMaxStages + s); };
+    const long long ibeg = (long long)blockIdx.x * a.L;
+    const long long iend = min(ibeg + (long long)a.L, a.total);
+    constexpr int esz = XF32 ? 4 : 2;
+    constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
+    // per-warp reduction area after the stages: [4 warps][NT*4 tokens][8][33] f32
+    float (*red)[NT * 4][8][33] = reinterpret_cast<float (*)[NT * 4][8][33]>(smem + (size_t)S * a.stage_bytes);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 4);
+        }
+        s_abort = 0;
+        s_issued = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == 4) {
+        // ---------------- weight + scale producer: one TMA box of each per stage
+        if (lane == 0) {
+            prefetch_tensor_map(&wmap);
+            prefetch_tensor_map(&smap);
+            const uint64_t pol = l2_evict_first_policy();
+            int i = 0;
+            for (long long it = ibeg; it < iend; ++it, ++i) {
+                const int s = i % S;
+                if (i >= S && !mbar_wait(empty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status)) break;
+                const int t = (int)(it / a.nquad), qd = (int)(it % a.nquad);
+                // full boxes always land (out-of-range columns are zero-filled)
+                mbar_arrive_expect_tx(full_bar(s), kStWBytes + a.s_bytes + (uint32_t)(a.M * kStRows * esz));
+                const uint32_t st = smem0 + (uint32_t)s * a.stage_bytes;
+                tma_load_2d(st, &wmap, t * (kStTN / 8), qd * kStRows, full_bar(s), pol);
+                tma_load_2d(st + kStWBytes, &smap, t * (kStTN * ssz / 8), qd * 4, full_bar(s), pol);
+            }
+            s_issued = i;
+        }
+    } else if (warp == 5) {
+        // ---------------- activation producer (waits for the previous grid)
+        pdl_wait();
+        int i = 0;
+        for (long long it = ibeg; it < iend; ++it, ++i) {
+            const int s = i % S;
+            if (i >= S && !mbar_wait(empty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status)) break;
+            const int qd = (int)(it % a.nquad);
+            if (lane < a.M)
+                bulk_g2s_nohint(smem0 + (uint32_t)s * a.stage_bytes + kStWBytes + a.s_bytes + lane * kStRows * esz,
+                                reinterpret_cast<const uint8_t*>(a.x) + ((size_t)lane * a.K + qd * kStRows) * esz,
+                                kStRows * esz, full_bar(s));
+        }
+    } else {
+        // ---------------- consumers: warp w takes the tile's block w
+        pdl_wait();  // outputs and workspace may still be read by the previous grid
+        const int g = lane >> 2, q = lane & 3, ctid = tid;
+        float acc[NT][16][2];
+        long long cur_t = -1;
+        const float inv = SFMT == G4B_SCALE_E4M3 ? a.inv : 1.0f;
+
+        auto flush = [&](long long t) {
+            // 1. the 4 warps' sums into shared memory (padded rows: conflict-free)
+            #pragma unroll
+            for (int t2 = 0; t2 < NT; t2++)
+                #pragma unroll
+                for (int u = 0; u < 4; u++)
+                    #pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        red[warp][4 * t2 + q][g][8 * u + j] = acc[t2][u * 4 + j][0];
+                        red[warp][4 * t2 + q][g][8 * u + j + 4] = acc[t2][u * 4 + j][1];
+                    }
+            named_bar_sync(1, 128);
+            const int c = blockIdx.x;
+            const long long c_first = (t * a.nquad) / a.L, c_last = ((t + 1) * a.nquad - 1) / a.L;
+            const bool single = c_first == c_last;
+            const bool ok = !*abort_flag;
+            const int n_base = (int)t * kStTN;
+            const long long slot = (long long)c * a.maxseg + (t - ((long long)c * a.L) / a.nquad);
+            // 2. warp-ordered sum, then y (tile owned by this CTA alone) or a partial
+            for (int e = ctid; e < a.M * kStTN && ok; e += 128) {
+                const int tok = e / kStTN, col = e % kStTN, n = n_base + col;
+                const int gg = col >> 5, cc = col & 31;
+                const float v = ((red[0][tok][gg][cc] + red[1][tok][gg][cc]) + red[2][tok][gg][cc]) + red[3][tok][gg][cc];
+                if (single) {
+                    if (n < a.N) {
+                        if (YF32) ((float*)a.y)[(size_t)tok * a.N + n] = v * inv;
+                        else ((__half*)a.y)[(size_t)tok * a.N + n] = __float2half_rn(v * inv);
+                    }
+                } else {
+                    a.partial[((size_t)slot * a.M + tok) * kStTN + col] = v;
+                }
+            }
+            if (!single) {
+                __threadfence();
+                named_bar_sync(1, 128);
+                if (ctid == 0) s_last = ok && (atomicAdd(&a.counters[t], 1u) == (unsigned)(c_last - c_first)) ? 1u : 0u;
+                named_bar_sync(1, 128);
+                if (s_last) {
+                    __threadfence();
+                    const int nseg = (int)(c_last - c_first + 1);
+                    for (int e = ctid; e < a.M * kStTN; e += 128) {
+                        const int tok = e / kStTN, col = e % kStTN, n = n_base + col;
+                        float v = 0.f;
+                        // 8 independent loads in flight, summed in CTA order
+                        for (int k0 = 0; k0 < nseg; k0 += 8) {
+                            float pv[8];
+                            #pragma unroll
+                            for (int k = 0; k < 8; k++) {
+                                const long long cc = c_first + k0 + k;
+                                pv[k] = 0.f;
+                                if (k0 + k < nseg) {
+                                    const long long sl = cc * a.maxseg + (t - (cc * a.L) / a.nquad);
+                                    pv[k] = __ldcg(&a.partial[((size_t)sl * a.M + tok) * kStTN + col]);
+                                }
+                            }
+                            #pragma unroll
+                            for (int k = 0; k < 8; k++)
+                                if (k0 + k < nseg) v += pv[k];
+                        }
+                        if (n < a.N) {
+                            if (YF32) ((float*)a.y)[(size_t)tok * a.N + n] = v * inv;
+                            else ((__half*)a.y)[(size_t)tok * a.N + n] = __float2half_rn(v * inv);
+                        }
+                    }
+                    if (ctid == 0) a.counters[t] = 0u;  // ready for the next call
+                }
+            }
+            named_bar_sync(1, 128);  // red[] is reused by the next flush
+        };
+
+        int i = 0;
+        for (long long it = ibeg; it < iend; ++it, ++i) {
+            const long long t = it / a.nquad;
+            if (t != cur_t) {
+                if (cur_t >= 0) flush(cur_t);
+                #pragma unroll
+                for (int t2 = 0; t2 < NT; t2++)
+                    #pragma unroll
+                    for (int k = 0; k < 16; k++) acc[t2][k][0] = acc[t2][k][1] = 0.f;
+                cur_t = t;
+            }
+            const int s = i % S;
+            if (mbar_wait(full_bar(s), (i / S) & 1, abort_flag, &g_gemv_status)) {
+                const uint8_t* st = smem + (size_t)s * a.stage_bytes;
+                const int row0 = 32 * warp + 8 * q;
+                Stage<XF32, SFMT, NT> sg;
+                #pragma unroll
+                for (int r = 0; r < 8; r++)
+                    sg.w[r] = *reinterpret_cast<const uint4*>(st + (row0 + r) * (kStTN / 2) + 16 * g);
+                if constexpr (SFMT == G4B_SCALE_F16) {
+                    #pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        sg.s.v[k] = *reinterpret_cast<const uint4*>(st + kStWBytes + (warp * kStTN + 32 * g + 8 * k) * 2);
+                } else {
+                    #pragma unroll
+                    for (int k = 0; k < 2; k++)
+                        sg.s.v[k] = *reinterpret_cast<const uint4*>(st + kStWBytes + warp * kStTN + 32 * g + 16 * k);
+                }
+                const uint8_t* xs = st + kStWBytes + a.s_bytes;
+                #pragma unroll
+                for (int t2 = 0; t2 < NT; t2++) {
+                    const int tok = 4 * t2 + (g >> 1);
+                    const bool live = tok < a.M && (XF32 || (g & 1) == 0);
+                    if constexpr (XF32) {
+                        const float4* xp = reinterpret_cast<const float4*>(xs + (tok * kStRows + row0) * 4);
+                        sg.x.v[t2][0] = live ? xp[0] : make_float4(0, 0, 0, 0);
+                        sg.x.v[t2][1] = live ? xp[1] : make_float4(0, 0, 0, 0);
+                    } else {
+                        sg.x.v[t2] = live ? *reinterpret_cast<const uint4*>(xs + (tok * kStRows + row0) * 2)
+                                          : make_uint4(0, 0, 0, 0);
+                    }
+                }
+                compute_stage<XF32, SFMT, NT>(sg, acc, g);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar(s));
+        }
+        if (cur_t >= 0) flush(cur_t);
+    }
+
+    __syncthreads();
+    if (tid == 0 && *abort_flag) {
+        // drain: let every TMA load this CTA issued land before the CTA exits
+        const int issued = s_issued;
+        for (int i = max(0, issued - S); i < issued; i++) {
+            const uint64_t t0 = global_ns();
+            while (!mbar_try_wait(full_bar(i % S), (i / S) & 1) && global_ns() - t0 < kWaitLimitNs) {
+            }
+        }
+    }
+}
+
+// ====================================================== streaming GEMV, M = 1
+// The decode case (one token) gets its own consumer arithmetic and layout:
+//  * nibble -> f16 with a single AND: (w & 0x000F000F) is the f16 pair
+//    (q * 2^-24, q' * 2^-24) exactly (subnormals; the tensor core keeps them),
+//    and (w & 0x00F000F0) is (q * 2^-20, ...).  The 2^24 / 2^20 and the -8
+//    offset are applied per block in f32:  sum (q - 8) x = 2^E * C - 8 * X
+//    with X = the sum of the block's x.
+//  * block-diagonal B: the 8 columns of one m16n8k16 B operand hold x masked
+//    to 8 different 32-row blocks (f16 x; 4 blocks x {hi, lo} pieces for f32
+//    x), so every accumulator element is a useful per-block dot product and
+//    the per-block scale is applied once per stage.
+//  * the A fragments come straight from ldmatrix.x4.trans: for a 16-bit
+//    column g (4 weight columns) it hands lane (g, q) rows 2q and 2q+1 packed
+//    in one register -- the k-pair layout m16n8k16 wants -- so one
+//    instruction feeds 4 mma operands.  The weight tile lands 128-byte
+//    swizzled and the 8 rows of each 8x8 matrix are rotated per lane so they
+//    fall on 8 different swizzle phases: conflict-free.
+//  * work: a stage of [256 rows (8 blocks) x 256 columns] goes to one of 2
+//    warp groups (item i -> group i % 2), each of its 8 warps taking one
+//    16-byte column segment (32 columns); one ldmatrix.x4 feeds two mma
+//    steps.  Each group owns 2 stages (double buffering); a barrier is only
+//    ever waited on by the group that consumes it, in order, so the parity of
+//    the phase it waits for can never alias an older, still-pending phase.
+constexpr int kM1Rows = 256;
+constexpr int kM1WBytes = kM1Rows * (kStTN / 2);  // 32 KB
+constexpr int kM1Groups = 2;
+constexpr int kM1PerGroup = 2;                     // private stages per group
+constexpr int kM1Stages = kM1Groups * kM1PerGroup;
+constexpr int kM1WarpsPerGroup = 8;
+constexpr int kM1Consumers = 32 * kM1WarpsPerGroup * kM1Groups;  // 512
+constexpr int kM1Threads = kM1Consumers + 64;      // + TMA producer warp + activation producer warp
+
+// item i of a CTA -> its group, shared-memory stage and barrier phase parity
+__device__ __forceinline__ int m1_group(int i) { return i % kM1Groups; }
+__device__ __forceinline__ int m1_stage(int i) { return i % kM1Groups + kM1Groups * ((i / kM1Groups) % kM1PerGroup); }
+__device__ __forceinline__ uint32_t m1_parity(int i) { return (uint32_t)((i / kM1Groups) / kM1PerGroup) & 1u; }
+
+struct M1Args {
+    const void* x;
+    void* y;
+    float* partial;      // [G * maxseg, kStTN]
+    unsigned* counters;  // [ntiles]
+    float inv;
+    int N, K, noct, ntiles, G, maxseg, stage_bytes, s_bytes;
+    long long total;
+};
+
+__device__ __forceinline__ uint32_t nib_sub(uint32_t P, int j) {
+    const uint32_t src = (j >= 2) ? (P >> 8) : P;
+    return src & ((j & 1) ? 0x00F000F0u : 0x000F000Fu);
+}
+
+// byte offset of 32-bit word `word` (0..31) of row `row` in a 128-byte-swizzled tile
+__device__ __forceinline__ int swz128(int row, int word) {
+    return row * 128 + ((((word >> 2) ^ (row & 7)) << 4) | ((word & 3) << 2));
+}
+
+template <bool XF32, int SFMT, bool YF32>
+__global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args a,
+                                                                  const __grid_constant__ CUtensorMap wmap,
+                                                                  const __grid_constant__ CUtensorMap smap) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ uint64_t bars[2 * kM1Stages];
+    __shared__ float red[2][kM1Groups][kStTN];  // double-buffered: consecutive flushes never share it
+    __shared__ unsigned s_last;
+    __shared__ long long s_pending;              // shared tile this CTA must still reduce (-1: none)
+    __shared__ int s_issued;
+    __shared__ int s_abort;
+    __shared__ __align__(16) uint32_t s_zero[32];  // B-fragment source for lanes that feed zeros
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    volatile int* abort_flag = &s_abort;
+    constexpr int esz = XF32 ? 4 : 2;
+    constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
+    // the swizzle pattern repeats every 1024 bytes: align the stages to it
+    const uint32_t raw0 = smem_u32(smem_raw);
+    const uint32_t smem0 = (raw0 + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (smem0 - raw0);
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kM1Stages + s); };
+    // balanced contiguous item ranges: CTA c owns [c*T/G, (c+1)*T/G)
+    const long long ibeg = (long long)blockIdx.x * a.total / a.G;
+    const long long iend = (long long)(blockIdx.x + 1) * a.total / a.G;
+    const int pw = kM1Consumers / 32;  // first producer warp
+
+    if (tid == 0) {
+        for (int s = 0; s < kM1Stages; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), kM1WarpsPerGroup);
+        }
+        s_abort = 0;
+        s_issued = 0;
+        s_pending = -1;
+        fence_mbar_init();
+    }
+    if (tid < 32) s_zero[tid] = 0u;
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == pw) {
+        if (lane == 0) {
+            prefetch_tensor_map(&wmap);
+            prefetch_tensor_map(&smap);
+            const uint64_t pol = l2_evict_first_policy();
+            int i = 0;
+            for (long long it = ibeg; it < iend; ++it, ++i) {
+                const int s = m1_stage(i);
+                if (i >= kM1Stages && !mbar_wait(empty_bar(s), m1_parity(i) ^ 1u, abort_flag, &g_gemv_status)) break;
+                const int t = (int)(it / a.noct), o = (int)(it % a.noct);
+                mbar_arrive_expect_tx(full_bar(s), kM1WBytes + a.s_bytes + kM1Rows * esz);
+                const uint32_t st = smem0 + (uint32_t)s * a.stage_bytes;
+                tma_load_2d(st, &wmap, t * (kStTN / 8), o * kM1Rows, full_bar(s), pol);
+                tma_load_2d(st + kM1WBytes, &smap, t * (kStTN * ssz / 8), o * 8, full_bar(s), pol);
+            }
+            s_issued = i;
+        }
+    } else if (warp == pw + 1) {
+        pdl_wait();
+        if (lane == 0) {
+            int i = 0;
+            for (long long it = ibeg; it < iend; ++it, ++i) {
+                const int s = m1_stage(i);
+                if (i >= kM1Stages && !mbar_wait(empty_bar(s), m1_parity(i) ^ 1u, abort_flag, &g_gemv_status)) break;
+                const int o = (int)(it % a.noct);
+                bulk_g2s_nohint(smem0 + (uint32_t)s * a.stage_bytes + kM1WBytes + a.s_bytes,
+                                reinterpret_cast<const uint8_t*>(a.x) + (size_t)o * kM1Rows * esz, kM1Rows * esz,
+                                full_bar(s));
+            }
+        }
+    } else {
+        pdl_wait();
+        const int g = lane >> 2, q = lane & 3, ctid = tid;
+        const int grp = warp / kM1WarpsPerGroup, seg = warp % kM1WarpsPerGroup;  // 16-byte column segment
+        const int colA = 32 * seg + 4 * g;  // this lane's columns: colA + j (j = 0, 1) and colA + 2 + j
+        // ldmatrix.x4: lane L addresses row L%8 of matrix L/8; matrix m = (step p + m/2, k-pair m%2)
+        const int lm = lane >> 3, lrr = lane & 7, lq = lrr >> 1, le = lrr & 1;
+        const int lds = lm >> 1, lh = lm & 1;
+        const float inv = SFMT == G4B_SCALE_E4M3 ? a.inv : 1.0f;
+        constexpr int NPASS = XF32 ? 2 : 1;   // f32 x: two passes of 4 blocks
+        constexpr int NSTEP = XF32 ? 8 : 16;  // mma steps per pass
+        constexpr int RMUL = XF32 ? 4 : 2;    // rows advanced per step
+        float acc[2][2];
+        const long long t_first = ibeg / a.noct, t_last = iend > ibeg ? (iend - 1) / a.noct : t_first - 1;
+        // Sum a shared tile's partials in CTA order (deterministic) and write y.
+        auto reduce_tile = [&](long long t) {
+            const long long c_first = ((t * a.noct + 1) * a.G - 1) / a.total;
+            const long long c_last = (((t + 1) * a.noct) * a.G - 1) / a.total;
+            const int nseg = (int)(c_last - c_first + 1);
+            if (ctid < kStTN) {
+                const int col = ctid;
+                float v = 0.f;
+                for (int k0 = 0; k0 < nseg; k0 += 8) {
+                    float pv[8];
+                    #pragma unroll
+                    for (int k = 0; k < 8; k++) {
+                        pv[k] = 0.f;
+                        if (k0 + k < nseg) {
+                            const long long cc = c_first + k0 + k;
+                            const long long cb = cc * a.total / a.G;  // first item of CTA cc
+                            const long long sl = cc * a.maxseg + (t - cb / a.noct);
+                            pv[k] = __ldcg(&a.partial[(size_t)sl * kStTN + col]);
+                        }
+                    }
+                    #pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        if (k0 + k < nseg) v += pv[k];
+                }
+                const int n = (int)t * kStTN + col;
+                if (n < a.N) {
+                    if (YF32) ((float*)a.y)[n] = v * inv;
+                    else ((__half*)a.y)[n] = __float2half_rn(v * inv);
+                }
+            }
+            if (ctid == 0) a.counters[t] = 0u;  // ready for the next call
+        };
+        int nflush = 0;
+
+        for (long long t = t_first; t <= t_last; ++t) {
+            acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
+            const long long tb = max(ibeg, t * a.noct), te = min(iend, (t + 1) * a.noct);
+            long long it = tb + ((grp - (tb - ibeg) % kM1Groups + kM1Groups) % kM1Groups);
+            for (; it < te; it += kM1Groups) {
+                const int i = (int)(it - ibeg);
+                const int s = m1_stage(i);
+                if (!mbar_wait(full_bar(s), m1_parity(i), abort_flag, &g_gemv_status)) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty_bar(s));
+                    continue;
+                }
+                const uint32_t st_u = smem0 + (uint32_t)s * a.stage_bytes;
+                const uint8_t* st = smem + (size_t)s * a.stage_bytes;
+                const uint8_t* sc = st + kM1WBytes;
+                const uint8_t* xs = sc + a.s_bytes;
+                // block sums X[b] of the stage's 8 blocks: lane l sums rows 8l..8l+7
+                float xsum;
+                if constexpr (XF32) {
+                    const float4 v0 = *reinterpret_cast<const float4*>(xs + lane * 32);
+                    const float4 v1 = *reinterpret_cast<const float4*>(xs + lane * 32 + 16);
+                    xsum = ((((((v0.x + v0.y) + v0.z) + v0.w) + v1.x) + v1.y) + v1.z) + v1.w;
+                } else {
+                    const uint4 v = *reinterpret_cast<const uint4*>(xs + lane * 16);
+                    xsum = ((((((h_lo(v.x) + h_hi(v.x)) + h_lo(v.y)) + h_hi(v.y)) + h_lo(v.z)) + h_hi(v.z)) + h_lo(v.w)) +
+                           h_hi(v.w);
+                }
+                xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+                xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
+                #pragma unroll 1
+                for (int pass = 0; pass < NPASS; pass++) {
+                    // ldmatrix row of this lane: block and rotated row (swizzle phase differs per lane)
+                    const int lblk = XF32 ? 4 * pass + lq : lq + 4 * lh;
+                    const int lrot = RMUL * lds + 2 * lq + le + ((XF32 && lh) ? 2 : 0);
+                    const uint32_t lbase = st_u + (uint32_t)(lblk * 32 * 128);
+                    // row offsets for the 4 step phases (steps p = 4m + d advance the row by 8m (f16) / 16m (f32))
+                    uint32_t roff[4], swz[4];
+                    #pragma unroll
+                    for (int d = 0; d < 4; d++) {
+                        const int r = (RMUL * d + lrot) & 31;
+                        roff[d] = (uint32_t)(r * 128);
+                        swz[d] = (uint32_t)((seg ^ (r & 7)) << 4);
+                    }
+                    // B-fragment sources: lanes that feed zeros read a zeroed area instead
+                    uint32_t xb0, xb1, xoff;
+                    if constexpr (XF32) {
+                        const bool mine = (g >> 1) == q;
+                        xb0 = mine ? smem_u32(xs) + (uint32_t)((4 * pass + q) * 128) : smem_u32(s_zero);
+                        xb1 = xb0;
+                        xoff = (uint32_t)(8 * q);
+                    } else {
+                        xb0 = g == q ? smem_u32(xs) + (uint32_t)(q * 64) : smem_u32(s_zero);
+                        xb1 = g == q + 4 ? smem_u32(xs) + (uint32_t)((q + 4) * 64) : smem_u32(s_zero);
+                        xoff = (uint32_t)(4 * q);
+                    }
+                    float C[2][4];
+                    #pragma unroll
+                    for (int k = 0; k < 2; k++) C[k][0] = C[k][1] = C[k][2] = C[k][3] = 0.f;
+                    #pragma unroll
+                    for (int p = 0; p < NSTEP; p += 2) {
+                        const int d = p & 3, mrow = (p >> 2) * (RMUL == 2 ? 1024 : 2048);
+                        const uint32_t addr = lbase + (((roff[d] + (uint32_t)mrow) & 4095u) | swz[d]);
+                        uint32_t ra0, rb0, ra1, rb1;
+                        ldsm_x4_trans(addr, ra0, rb0, ra1, rb1);
+                        #pragma unroll
+                        for (int ss = 0; ss < 2; ss++) {
+                            const uint32_t RA = ss ? ra1 : ra0, RB = ss ? rb1 : rb0;
+                            const int pp = p + ss;
+                            uint32_t b0, b1;
+                            if constexpr (XF32) {
+                                const uint32_t o0 = (xoff + 16u * pp) & 127u, o1 = (xoff + 16u * pp + 8u) & 127u;
+                                float2 xa, xb;
+                                asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(xa.x), "=f"(xa.y) : "r"(xb0 + o0));
+                                asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(xb.x), "=f"(xb.y) : "r"(xb1 + o1));
+                                const bool lo = (g & 1) != 0;
+                                b0 = split_pair(xa.x, xa.y, lo);
+                                b1 = split_pair(xb.x, xb.y, lo);
+                            } else {
+                                const uint32_t o = (xoff + 4u * pp) & 63u;
+                                asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(xb0 + o));
+                                asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(xb1 + o));
+                            }
+                            const uint32_t RA8 = RA >> 8, RB8 = RB >> 8;
+                            mma_16816(C[0], RA & 0x000F000Fu, RA8 & 0x000F000Fu, RB & 0x000F000Fu, RB8 & 0x000F000Fu, b0, b1);
+                            mma_16816(C[1], RA & 0x00F000F0u, RA8 & 0x00F000F0u, RB & 0x00F000F0u, RB8 & 0x00F000F0u, b0, b1);
+                        }
+                    }
+                    // per-block scale, 2^E and -8 X correction, in f32
+                    int blk0, blk1;
+                    if constexpr (XF32) { blk0 = 4 * pass + q; blk1 = blk0; } else { blk0 = 2 * q; blk1 = 2 * q + 1; }
+                    const float X0 = __shfl_sync(0xffffffffu, xsum, 4 * blk0);
+                    const float X1 = __shfl_sync(0xffffffffu, xsum, 4 * blk1);
+                    // scales of columns colA .. colA+3 in blocks blk0 / blk1
+                    float s0[4], s1[4];
+                    if constexpr (SFMT == G4B_SCALE_F16) {
+                        const uint2 u0 = *reinterpret_cast<const uint2*>(sc + (blk0 * kStTN + colA) * 2);
+                        const uint2 u1 = *reinterpret_cast<const uint2*>(sc + (blk1 * kStTN + colA) * 2);
+                        s0[0] = h_lo(u0.x); s0[1] = h_hi(u0.x); s0[2] = h_lo(u0.y); s0[3] = h_hi(u0.y);
+                        s1[0] = h_lo(u1.x); s1[1] = h_hi(u1.x); s1[2] = h_lo(u1.y); s1[3] = h_hi(u1.y);
+                    } else {
+                        const uint32_t u0 = *reinterpret_cast<const uint32_t*>(sc + blk0 * kStTN + colA);
+                        const uint32_t u1 = *reinterpret_cast<const uint32_t*>(sc + blk1 * kStTN + colA);
+                        uint32_t h;
+                        h = e4m3x2_to_f16x2((uint16_t)(u0 & 0xffffu)); s0[0] = h_lo(h); s0[1] = h_hi(h);
+                        h = e4m3x2_to_f16x2((uint16_t)(u0 >> 16));     s0[2] = h_lo(h); s0[3] = h_hi(h);
+                        h = e4m3x2_to_f16x2((uint16_t)(u1 & 0xffffu)); s1[0] = h_lo(h); s1[1] = h_hi(h);
+                        h = e4m3x2_to_f16x2((uint16_t)(u1 >> 16));     s1[2] = h_lo(h); s1[3] = h_hi(h);
+                    }
+                    #pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        const float E = j ? 1048576.0f : 16777216.0f;  // 2^20 (high nibble) / 2^24 (low nibble)
+                        // C[j][0..1]: column colA + j; C[j][2..3]: column colA + 2 + j
+                        if constexpr (XF32) {
+                            acc[j][0] = fmaf(s0[j], fmaf(C[j][0] + C[j][1], E, -8.0f * X0), acc[j][0]);
+                            acc[j][1] = fmaf(s0[2 + j], fmaf(C[j][2] + C[j][3], E, -8.0f * X0), acc[j][1]);
+                        } else {
+                            acc[j][0] = fmaf(s0[j], fmaf(C[j][0], E, -8.0f * X0), acc[j][0]);
+                            acc[j][0] = fmaf(s1[j], fmaf(C[j][1], E, -8.0f * X1), acc[j][0]);
+                            acc[j][1] = fmaf(s0[2 + j], fmaf(C[j][2], E, -8.0f * X0), acc[j][1]);
+                            acc[j][1] = fmaf(s1[2 + j], fmaf(C[j][3], E, -8.0f * X1), acc[j][1]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty_bar(s));
+            }
+            // ---- flush tile t: quad sum (the lanes of a quad hold different blocks), group sum, CTA share
+            #pragma unroll
+            for (int k = 0; k < 2; k++)
+                #pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    float v = acc[k][h];
+                    v += __shfl_xor_sync(0xffffffffu, v, 1);
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    acc[k][h] = v;
+                }
+            const int rb = nflush++ & 1;
+            if (q == 0) {
+                #pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    red[rb][grp][colA + j] = acc[j][0];
+                    red[rb][grp][colA + 2 + j] = acc[j][1];
+                }
+            }
+            named_bar_sync(1, kM1Consumers);
+            const int c = blockIdx.x;
+            const long long c_first = ((t * a.noct + 1) * a.G - 1) / a.total;
+            const long long c_last = (((t + 1) * a.noct) * a.G - 1) / a.total;
+            const bool single = c_first == c_last;
+            const bool ok = !*abort_flag;
+            const long long slot = (long long)c * a.maxseg + (t - ibeg / a.noct);
+            if (ctid < kStTN && ok) {
+                const int col = ctid;
+                float v = red[rb][0][col];
+                #pragma unroll
+                for (int gg = 1; gg < kM1Groups; gg++) v += red[rb][gg][col];
+                const int n = (int)t * kStTN + col;
+                if (single) {
+                    if (n < a.N) {
+                        if (YF32) ((float*)a.y)[n] = v * inv;
+                        else ((__half*)a.y)[n] = __float2half_rn(v * inv);
+                    }
+                } else {
+                    a.partial[(size_t)slot * kStTN + col] = v;
+                }
+            }
+            if (!single) {
+                // publish this CTA's partial: one thread fences for the CTA (after the barrier) and
+                // arrives on the tile's counter; the last of the tile's CTAs to arrive reduces it
+                named_bar_sync(1, kM1Consumers);
+                if (t < t_last) {
+                    // not our final tile: do not stall the other consumers on the atomic; if we
+                    // turn out to be the last arriver, the reduction runs after our last item
+                    if (ctid == 0 && ok) {
+                        __threadfence();
+                        if (atomicAdd(&a.counters[t], 1u) == (unsigned)(c_last - c_first)) s_pending = t;
+                    }
+                } else {
+                    if (ctid == 0) {
+                        unsigned last = 0;
+                        if (ok) {
+                            __threadfence();
+                            last = atomicAdd(&a.counters[t], 1u) == (unsigned)(c_last - c_first) ? 1u : 0u;
+                        }
+                        s_last = last;
+                    }
+                    named_bar_sync(1, kM1Consumers);
+                    if (s_last) {
+                        __threadfence();
+                        reduce_tile(t);
+                    }
+                }
+            }
+        }
+        // the deferred reduction of an earlier tile this CTA was the last to finish
+        named_bar_sync(1, kM1Consumers);
+        if (s_pending >= 0 && !*abort_flag) {
+            __threadfence();
+            reduce_tile(s_pending);
+        }
+    }
+
+    __syncthreads();
+    if (tid == 0 && *abort_flag) {
+        const int issued = s_issued;
+        for (int i = max(0, issued - kM1Stages); i < issued; i++) {
+            const uint64_t t0 = global_ns();
+            while (!mbar_try_wait(full_bar(m1_stage(i)), m1_parity(i)) && global_ns() - t0 < kWaitLimitNs) {
+            }
+        }
+    }
+}
+
+struct M1Plan {
+    int ntiles, noct, G, maxseg, stage_bytes, s_bytes;
+    long long total;
+    size_t smem, ws_bytes;
+};
+
+static M1Plan m1_plan(int N, int K, int sms, bool xf32, int sfmt) {
+    M1Plan p{};
+    p.noct = K / 256;
+    p.ntiles = (N + kStTN - 1) / kStTN;
+    p.total = (long long)p.ntiles * p.noct;
+    p.G = (int)std::max<long long>(1, std::min<long long>(std::max(sms, 1), p.total));
+    const long long lmax = (p.total + p.G - 1) / p.G;
+    p.maxseg = (int)((lmax + p.noct - 1) / p.noct + 1);
+    p.s_bytes = 8 * kStTN * (sfmt == G4B_SCALE_F16 ? 2 : 1);
+    p.stage_bytes = (kM1WBytes + p.s_bytes + kM1Rows * (xf32 ? 4 : 2) + 1023) & ~1023;  // swizzle atoms stay aligned
+    p.smem = (size_t)kM1Stages * p.stage_bytes + 1024;                                     // + base alignment slack
+    // a tile is split across CTAs unless every CTA boundary falls on a tile boundary
+    bool multi = false;
+    for (int c = 1; c < p.G && !multi; c++)
+        if (((long long)c * p.total / p.G) % p.noct) multi = true;
+    if (multi) p.ws_bytes = kGemvCounterBytes + (((size_t)p.G * p.maxseg * kStTN * sizeof(float) + 255) & ~(size_t)255);
+    return p;
+}
+
+static bool m1_ok(int M, int N, int K, int split) { return M == 1 && split == 0 && N % 32 == 0 && K % 256 == 0; }
+
+template <bool XF32, int SFMT, bool YF32>
+static int launch_m1(const M1Args& a, const M1Plan& p, const uint32_t* wp, const void* scales, cudaStream_t s) {
+    CUtensorMap wmap, smap;
+    int st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, wp, (uint64_t)a.N / 8, (uint64_t)a.K,
+                           (uint64_t)a.N / 2, kStTN / 8, kM1Rows, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != G4B_OK) return st;
+    constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
+    st = tensor_map_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT64, scales, (uint64_t)a.N * ssz / 8, (uint64_t)a.K / 32,
+                       (uint64_t)a.N * ssz, kStTN * ssz / 8, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != G4B_OK) return st;
+    auto kern = gemv_i4_m1_kernel<XF32, SFMT, YF32>;
+    static int attr_set_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_set_mask & (1 << (dev & 31)))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        attr_set_mask |= 1 << (dev & 31);
+    }
+    cudaError_t e = launch_k(kern, dim3(p.G), dim3(kM1Threads), p.smem, s, a, wmap, smap);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: launch: %s", cudaGetErrorString(e));
+    return G4B_OK;
+}
+
+static int dispatch_m1(const M1Args& a, const M1Plan& p, const uint32_t* wp, const void* sc, bool xf32, int sfmt,
+                       bool yf32, cudaStream_t s) {
+    if (xf32) {
+        if (sfmt == G4B_SCALE_F16) return yf32 ? launch_m1<true, G4B_SCALE_F16, true>(a, p, wp, sc, s) : launch_m1<true, G4B_SCALE_F16, false>(a, p, wp, sc, s);
+        return yf32 ? launch_m1<true, G4B_SCALE_E4M3, true>(a, p, wp, sc, s) : launch_m1<true, G4B_SCALE_E4M3, false>(a, p, wp, sc, s);
+    }
+    if (sfmt == G4B_SCALE_F16) return yf32 ? launch_m1<false, G4B_SCALE_F16, true>(a, p, wp, sc, s) : launch_m1<false, G4B_SCALE_F16, false>(a, p, wp, sc, s);
+    return yf32 ? launch_m1<false, G4B_SCALE_E4M3, true>(a, p, wp, sc, s) : launch_m1<false, G4B_SCALE_E4M3, false>(a, p, wp, sc, s);
+}
+
+unsigned read_status_gemv() {
+    unsigned v = 0, z = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemv_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (v) cudaMemcpyToSymbol(g_gemv_status, &z, sizeof(z));
+    return v;
+}
+
+struct StreamPlan {
+    int ntiles, nquad, G, L, maxseg, stages, stage_bytes, s_bytes;
+    long long total;
+    size_t smem, part_bytes, ws_bytes;
+};
+
+static StreamPlan stream_plan(int M, int N, int K, int split, int sms, bool xf32, int sfmt) {
+    StreamPlan p{};
+    const int nblk = K / 32, mg = std::min(M, kGemvMaxTok);
+    p.nquad = nblk / 4;
+    p.ntiles = (N + kStTN - 1) / kStTN;
+    p.total = (long long)p.ntiles * p.nquad;
+    if (split > 0) {
+        p.L = p.nquad / split;  // split divides nblk/4 here (checked by the caller)
+        p.G = p.ntiles * split;
+    } else {
+        const int min_items = 2;  // at least 32 KB of weights per CTA
+        long long G = std::min<long long>(2LL * std::max(sms, 1), (p.total + min_items - 1) / min_items);
+        G = std::max<long long>(G, 1);
+        p.L = (int)((p.total + G - 1) / G);
+        p.G = (int)((p.total + p.L - 1) / p.L);
+    }
+    p.maxseg = (p.L + p.nquad - 1) / p.nquad + 1;
+    p.s_bytes = 4 * kStTN * (sfmt == G4B_SCALE_F16 ? 2 : 1);
+    const int nt = mg <= 4 ? 1 : 2;
+    p.stage_bytes = (kStWBytes + p.s_bytes + mg * kStRows * (xf32 ? 4 : 2) + 127) & ~127;
+    const size_t red_bytes = (size_t)4 * nt * 4 * 8 * 33 * sizeof(float);
+    const size_t budget = 110 * 1024;  // two CTAs per SM
+    p.stages = (int)std::max<size_t>(2, std::min<size_t>(kStMaxStages, (budget - red_bytes) / p.stage_bytes));
+    p.smem = (size_t)p.stages * p.stage_bytes + red_bytes;
+    const bool multi = (p.L % p.nquad) != 0;  // some tile is shared by several CTAs
+    if (multi) {
+        p.part_bytes = (size_t)p.G * p.maxseg * mg * kStTN * sizeof(float);
+        p.ws_bytes = kGemvCounterBytes + ((p.part_bytes + 255) & ~(size_t)255);
+    }
+    return p;
+}
+
+template <bool XF32, int SFMT, int NT, bool YF32>
+static int launch_stream(const StreamArgs& a, const StreamPlan& p, const uint32_t* wp, const void* scales,
+                         cudaStream_t s) {
+    CUtensorMap wmap, smap;
+    int st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, wp, (uint64_t)a.N / 8, (uint64_t)a.K,
+                           (uint64_t)a.N / 2, kStTN / 8, kStRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != G4B_OK) return st;
+    constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
+    st = tensor_map_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT64, scales, (uint64_t)a.N * ssz / 8, (uint64_t)a.K / 32,
+                       (uint64_t)a.N * ssz, kStTN * ssz / 8, 4, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != G4B_OK) return st;
+    auto kern = gemv_i4_stream_kernel<XF32, SFMT, NT, YF32>;
+    static int attr_set_mask = 0;  // per device bit
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_set_mask & (1 << (dev & 31)))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
+        if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        attr_set_mask |= 1 << (dev & 31);
+    }
+    cudaError_t e = launch_k(kern, dim3(p.G), dim3(kStThreads), p.smem, s, a, wmap, smap);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: launch: %s", cudaGetErrorString(e));
+    return G4B_OK;
+}
+
+template <bool XF32, int SFMT>
+static int dispatch_stream2(const StreamArgs& a, const StreamPlan& p, const uint32_t* wp, const void* sc, int nt,
+                            bool yf32, cudaStream_t s) {
+    if (nt == 1)
+        return yf32 ? launch_stream<XF32, SFMT, 1, true>(a, p, wp, sc, s) : launch_stream<XF32, SFMT, 1, false>(a, p, wp, sc, s);
+    return yf32 ? launch_stream<XF32, SFMT, 2, true>(a, p, wp, sc, s) : launch_stream<XF32, SFMT, 2, false>(a, p, wp, sc, s);
+}
+
+static int dispatch_stream(const StreamArgs& a, const StreamPlan& p, const uint32_t* wp, const void* sc, bool xf32,
+                           int sfmt, int nt, bool yf32, cudaStream_t s) {
+    if (xf32)
+        return sfmt == G4B_SCALE_F16 ? dispatch_stream2<true, G4B_SCALE_F16>(a, p, wp, sc, nt, yf32, s)
+                                     : dispatch_stream2<true, G4B_SCALE_E4M3>(a, p, wp, sc, nt, yf32, s);
+    return sfmt == G4B_SCALE_F16 ? dispatch_stream2<false, G4B_SCALE_F16>(a, p, wp, sc, nt, yf32, s)
+                                 : dispatch_stream2<false, G4B_SCALE_E4M3>(a, p, wp, sc, nt, yf32, s);
+}
+
+// The streaming kernel needs 16-byte rows (N % 32), whole block quads
+// (K % 128) and, with a caller-given split, K-slices of whole quads.
+static bool stream_ok(int N, int K, int split) {
+    const int nblk = K / 32;
+    return N % 32 == 0 && nblk % 4 == 0 && (split == 0 || (nblk / split) % 4 == 0);
+}
+
 // ---------------------------------------------------------------- planning
 struct GemvPlan {
     int ntiles, slices, bps, mg;   // mg = tokens per launch (<= 8)
@@ -339,10 +1153,11 @@ static GemvPlan gemv_plan(int M, int N, int K, int split, int sms) {
         bps = std::max(bps, std::min(kGemvWarps, nblk));
         p.bps = bps;
         p.slices = (nblk + bps - 1) / bps;
+        if (p.ntiles > kGemvMaxTiles) { p.slices = 1; p.bps = nblk; }
     }
     if (p.slices > 1) {
         p.part_bytes = align256((size_t)p.slices * p.mg * N * sizeof(float));
-        p.ws_bytes = p.part_bytes + align256((size_t)p.ntiles * sizeof(unsigned));
+        p.ws_bytes = kGemvCounterBytes + p.part_bytes;
     }
     return p;
 }
@@ -350,7 +1165,7 @@ static GemvPlan gemv_plan(int M, int N, int K, int split, int sms) {
 template <bool XF32, int SFMT, int NT, bool WIDE, bool YF32>
 static void launch_gemv(const GemvArgs& a, const GemvPlan& p, cudaStream_t s) {
     dim3 grid(p.ntiles, p.slices);
-    gemv_i4_kernel<XF32, SFMT, NT, WIDE, YF32><<<grid, kGemvThreads, 0, s>>>(a);
+    launch_k(gemv_i4_kernel<XF32, SFMT, NT, WIDE, YF32>, grid, dim3(kGemvThreads), 0, s, a);
 }
 
 template <bool XF32, int SFMT, int NT>
@@ -440,17 +1255,44 @@ using namespace g4b;
 extern "C" {
 
 size_t g4b_gemv_workspace_bytes(int M, int N, int K, int split) {
-    if (M <= 0 || N <= 0 || K <= 0 || K % 32) return 0;
+    if (M <= 0 || N <= 0 || K <= 0 || K % 32 || N % 16) return 0;
+    if (split > 0 && (K / 32) % split) return 0;
     int sms = 148;
     if (check_device(&sms) != G4B_OK) sms = 148;
     clear_error();
+    // the activation and scale formats only change the shared-memory layout, not the workspace
+    if (m1_ok(M, N, K, split)) return m1_plan(N, K, sms, true, G4B_SCALE_F16).ws_bytes;
+    if (stream_ok(N, K, split)) return stream_plan(M, N, K, split, sms, true, G4B_SCALE_F16).ws_bytes;
     return gemv_plan(M, N, K, split, sms).ws_bytes;
 }
+
+static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,
+                        float inv, void* y, int y_dtype, int N, int K, int split, void* workspace, size_t ws_bytes,
+                        g4b_stream_t stream);
 
 int g4b_gemv_i4(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,
                 float inv, void* y, int y_dtype, int N, int K, int split, void* workspace, size_t ws_bytes,
                 g4b_stream_t stream) {
     G4B_ENTRY("gemv_i4");
+    t_pdl = false;
+    return gemv_i4_impl(x, x_dtype, M, wp, scales, scale_fmt, inv, y, y_dtype, N, K, split, workspace, ws_bytes, stream);
+}
+
+int g4b_gemv_i4_ex(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,
+                   float inv, void* y, int y_dtype, int N, int K, int split, void* workspace, size_t ws_bytes,
+                   unsigned flags, g4b_stream_t stream) {
+    G4B_ENTRY("gemv_i4");
+    G4B_REQUIRE((flags & ~(unsigned)G4B_GEMV_PDL) == 0, G4B_E_ARG, "gemv_i4_ex: unknown flags 0x%x", flags);
+    t_pdl = (flags & G4B_GEMV_PDL) != 0;
+    const int st = gemv_i4_impl(x, x_dtype, M, wp, scales, scale_fmt, inv, y, y_dtype, N, K, split, workspace, ws_bytes,
+                                stream);
+    t_pdl = false;
+    return st;
+}
+
+static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,
+                        float inv, void* y, int y_dtype, int N, int K, int split, void* workspace, size_t ws_bytes,
+                        g4b_stream_t stream) {
     G4B_REQUIRE(x && wp && scales && y, G4B_E_ARG, "gemv_i4: NULL pointer argument");
     G4B_REQUIRE(x_dtype == G4B_DT_F32 || x_dtype == G4B_DT_F16, G4B_E_ARG, "gemv_i4: bad x_dtype %d", x_dtype);
     G4B_REQUIRE(y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16, G4B_E_ARG, "gemv_i4: bad y_dtype %d", y_dtype);
@@ -468,15 +1310,85 @@ int g4b_gemv_i4(const void* x, int x_dtype, int M, const uint32_t* wp, const voi
     int sms = 0;
     int st = check_device(&sms);
     if (st != G4B_OK) return st;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const size_t xe = x_dtype == G4B_DT_F32 ? 4 : 2, ye = y_dtype == G4B_DT_F32 ? 4 : 2;
+    if (m1_ok(M, N, K, split)) {
+        const M1Plan p = m1_plan(N, K, sms, x_dtype == G4B_DT_F32, scale_fmt);
+        if (p.ws_bytes) {
+            G4B_REQUIRE(workspace != nullptr && ws_bytes >= p.ws_bytes, G4B_E_WORKSPACE,
+                        "gemv_i4: needs %zu bytes of workspace, got %zu", p.ws_bytes, workspace ? ws_bytes : 0);
+            G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "gemv_i4: workspace must be 16-byte aligned");
+            G4B_REQUIRE(p.ntiles <= kGemvMaxTiles, G4B_E_SHAPE, "gemv_i4: N=%d too large for a split-K call", N);
+        }
+        M1Args a{};
+        a.x = x;
+        a.y = y;
+        a.inv = inv;
+        a.N = N;
+        a.K = K;
+        a.noct = p.noct;
+        a.ntiles = p.ntiles;
+        a.G = p.G;
+        a.maxseg = p.maxseg;
+        a.total = p.total;
+        a.stage_bytes = p.stage_bytes;
+        a.s_bytes = p.s_bytes;
+        if (p.ws_bytes) {
+            a.counters = (unsigned*)workspace;
+            a.partial = (float*)((char*)workspace + kGemvCounterBytes);
+        }
+        st = dispatch_m1(a, p, wp, scales, x_dtype == G4B_DT_F32, scale_fmt, y_dtype == G4B_DT_F32, s);
+        if (st != G4B_OK) return st;
+        count_launch();
+        return launch_status("gemv_i4");
+    }
+    if (stream_ok(N, K, split)) {
+        const StreamPlan p = stream_plan(M, N, K, split, sms, x_dtype == G4B_DT_F32, scale_fmt);
+        if (p.ws_bytes) {
+            G4B_REQUIRE(workspace != nullptr && ws_bytes >= p.ws_bytes, G4B_E_WORKSPACE,
+                        "gemv_i4: needs %zu bytes of workspace, got %zu", p.ws_bytes, workspace ? ws_bytes : 0);
+            G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "gemv_i4: workspace must be 16-byte aligned");
+            G4B_REQUIRE(p.ntiles <= kGemvMaxTiles, G4B_E_SHAPE, "gemv_i4: N=%d too large for a split-K call", N);
+        }
+        for (int m0 = 0; m0 < M; m0 += kGemvMaxTok) {
+            StreamArgs a{};
+            a.M = std::min(kGemvMaxTok, M - m0);
+            a.x = (const char*)x + (size_t)m0 * K * xe;
+            a.y = (char*)y + (size_t)m0 * N * ye;
+            a.inv = inv;
+            a.N = N;
+            a.K = K;
+            a.nquad = p.nquad;
+            a.ntiles = p.ntiles;
+            a.L = p.L;
+            a.maxseg = p.maxseg;
+            a.total = p.total;
+            a.stages = p.stages;
+            a.stage_bytes = p.stage_bytes;
+            a.s_bytes = p.s_bytes;
+            if (p.ws_bytes) {
+                a.counters = (unsigned*)workspace;
+                a.partial = (float*)((char*)workspace + kGemvCounterBytes);
+            }
+            st = dispatch_stream(a, p, wp, scales, x_dtype == G4B_DT_F32, scale_fmt, a.M <= 4 ? 1 : 2,
+                                 y_dtype == G4B_DT_F32, s);
+            if (st != G4B_OK) return st;
+            count_launch();
+            st = launch_status("gemv_i4");
+            if (st != G4B_OK) return st;
+        }
+        return G4B_OK;
+    }
+    // other shapes (N % 32 == 16, K % 128 != 0): the register-streaming kernel
     const GemvPlan p = gemv_plan(M, N, K, split, sms);
     if (p.slices > 1) {
         G4B_REQUIRE(workspace != nullptr && ws_bytes >= p.ws_bytes, G4B_E_WORKSPACE,
                     "gemv_i4: needs %zu bytes of workspace, got %zu", p.ws_bytes, workspace ? ws_bytes : 0);
         G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "gemv_i4: workspace must be 16-byte aligned");
+        G4B_REQUIRE(p.ntiles <= kGemvMaxTiles, G4B_E_SHAPE, "gemv_i4: N=%d too large for a split-K call (split=1 only)",
+                    N);
     }
-    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const bool wide = (N % 32) == 0;
-    const size_t xe = x_dtype == G4B_DT_F32 ? 4 : 2, ye = y_dtype == G4B_DT_F32 ? 4 : 2;
     for (int m0 = 0; m0 < M; m0 += kGemvMaxTok) {
         GemvArgs a{};
         a.M = std::min(kGemvMaxTok, M - m0);
@@ -491,8 +1403,8 @@ int g4b_gemv_i4(const void* x, int x_dtype, int M, const uint32_t* wp, const voi
         a.bps = p.bps;
         a.slices = p.slices;
         if (p.slices > 1) {
-            a.partial = (float*)workspace;
-            a.counters = (unsigned*)((char*)workspace + p.part_bytes);
+            a.counters = (unsigned*)workspace;
+            a.partial = (float*)((char*)workspace + kGemvCounterBytes);
         }
         const int nt = a.M <= 4 ? 1 : 2;
         dispatch_gemv(a, p, x_dtype == G4B_DT_F32, scale_fmt, nt, wide, y_dtype == G4B_DT_F32, s);

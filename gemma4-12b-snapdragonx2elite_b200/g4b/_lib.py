@@ -23,6 +23,7 @@ G4B_E_ARG = -6
 G4B_E_WORKSPACE = -7
 G4B_E_TIMEOUT = -8
 
+GEMV_PDL = 1
 DT_F32 = 0
 DT_F16 = 1
 SCALE_F16 = 0
@@ -33,6 +34,7 @@ Q_DEVICE_OK = 1
 Q_SM_COUNT = 2
 Q_LAUNCHES = 3
 Q_FAULT_COUNTER = 4
+Q_KERNEL_STATUS = 5
 
 _STATUS_NAMES = {
     G4B_E_SHAPE: "G4B_E_SHAPE", G4B_E_ALIGN: "G4B_E_ALIGN", G4B_E_ARCH: "G4B_E_ARCH",
@@ -52,6 +54,7 @@ SIGNATURES = {
     "g4b_stream_wait": (_I, [_P, _I]),
     "g4b_gemv_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g4b_gemv_i4": (_I, [_P, _I, _I, _P, _P, _I, _F, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "g4b_gemv_i4_ex": (_I, [_P, _I, _I, _P, _P, _I, _F, _P, _I, _I, _I, _I, _P, _Z, C.c_uint, _P]),
     "g4b_reduce_partials": (_I, [_P, _P, _I, _I, _P]),
     "g4b_dequant_i4": (_I, [_P, _P, _I, _F, _P, _I, _I, _I, _P]),
     "g4b_cast": (_I, [_P, _I, _P, _I, _Z, _P]),

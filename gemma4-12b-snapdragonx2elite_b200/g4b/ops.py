@@ -99,8 +99,12 @@ def gemv_workspace_bytes(M: int, N: int, K: int, split: int = 0) -> int:
 
 def gemv_i4(x: torch.Tensor, w: DeviceWeight, split: int = 0, out: Optional[torch.Tensor] = None,
             out_dtype: torch.dtype = torch.float32, stream: Optional[torch.cuda.Stream] = None,
-            workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y = x @ dequant(W).T for x [K] or [M, K] (M <= 8 per kernel; larger M loops)."""
+            workspace: Optional[torch.Tensor] = None, pdl: bool = False) -> torch.Tensor:
+    """y = x @ dequant(W).T for x [K] or [M, K] (M <= 8 per kernel; larger M loops).
+
+    pdl=True launches with programmatic dependent launch (g4b_gemv_i4_ex,
+    G4B_GEMV_PDL): only valid when the previous kernel on the stream does not
+    write this layer's packed weights or scales."""
     _need(x, "x")
     squeeze = x.dim() == 1
     x2 = x.view(1, -1) if squeeze else x
@@ -116,9 +120,10 @@ def gemv_i4(x: torch.Tensor, w: DeviceWeight, split: int = 0, out: Optional[torc
     ws = workspace
     if need and ws is None:
         ws = WORKSPACES.get(x.device, sh, need)
-    L.check("g4b_gemv_i4", lib.g4b_gemv_i4(
+    L.check("g4b_gemv_i4", lib.g4b_gemv_i4_ex(
         _ptr(x2), _DT[x2.dtype], M, _ptr(w.wp), _ptr(w.scales), w.scale_fmt, w.inv,
-        _ptr(out), _DT[out.dtype], w.N, w.K, split, _ptr(ws), ws.numel() if ws is not None else 0, sh))
+        _ptr(out), _DT[out.dtype], w.N, w.K, split, _ptr(ws), ws.numel() if ws is not None else 0,
+        L.GEMV_PDL if pdl else 0, sh))
     return out.view(-1) if squeeze else out
 
 

@@ -69,6 +69,10 @@ typedef struct CUstream_st* g4b_stream_t;
 #define G4B_Q_SM_COUNT       2  /* streaming multiprocessors on the current device */
 #define G4B_Q_LAUNCHES       3  /* kernels this process has launched through g4b   */
 #define G4B_Q_FAULT_COUNTER  4  /* calls seen by the fault injector                */
+#define G4B_Q_KERNEL_STATUS  5  /* read-and-clear the kernels' device status word:
+                                   0 = clean, 1 = a bounded wait timed out (the
+                                   kernel gave up and its outputs are invalid);
+                                   synchronises the device */
 
 /* --------------------------------------------------------------- utilities */
 /* Message for the last failing call on this host thread ("" if none). */
@@ -111,6 +115,22 @@ G4B_API int g4b_gemv_i4(const void* x, int x_dtype, int M,
                 const uint32_t* wp, const void* scales, int scale_fmt, float inv,
                 void* y, int y_dtype, int N, int K, int split,
                 void* workspace, size_t ws_bytes, g4b_stream_t stream);
+
+/* g4b_gemv_i4 with launch flags:
+ *   G4B_GEMV_PDL  programmatic dependent launch: the kernel may start while the
+ *                 previous kernel in `stream` is still running and begins
+ *                 streaming wp/scales at once; it reads x and writes y and the
+ *                 workspace only after that kernel has completed.  Use it when
+ *                 the preceding kernel does not write wp or scales (a decode
+ *                 step's chain of GEMVs): it hides launch latency and the
+ *                 previous kernel's tail.  Captured into CUDA graphs as a
+ *                 programmatic edge.
+ * flags == 0 behaves exactly as g4b_gemv_i4. */
+#define G4B_GEMV_PDL 1u
+G4B_API int g4b_gemv_i4_ex(const void* x, int x_dtype, int M,
+                   const uint32_t* wp, const void* scales, int scale_fmt, float inv,
+                   void* y, int y_dtype, int N, int K, int split,
+                   void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream);
 
 /* Split-K partial reduction, vk/reduce.comp:8-12:
  *     y[n] = sum_{c=0}^{split-1} partial[c*N + n]   (c ascending, f32)

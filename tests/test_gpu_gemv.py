@@ -159,3 +159,78 @@ def test_query_device():
     W, pw, dw = _packed(256, 64)
     ops.gemv_i4(torch.zeros(64, device=DEV), dw)
     assert L.launches() == before + 1
+
+
+def test_gemv_shared_workspace_across_shapes_matches_oracle():
+    """One workspace tensor reused by shapes with different partial sizes, in an
+    order where a larger call's partials cover a smaller call's former layout."""
+    cases = [(15360, 3840, 12), (2048, 3840, 0), (3840, 15360, 0), (4096, 3840, 40), (15360, 3840, 0)]
+    need = max(ops.gemv_workspace_bytes(1, N, K, s) for N, K, s in cases)
+    ws = torch.zeros(need, dtype=torch.uint8, device=DEV)
+    for rep in range(2):
+        for N, K, s in cases:
+            W, pw, dw = _packed(N, K, seed=N + 3 * K)
+            x = activations(1, K, seed=N)[0]
+            y = ops.gemv_i4(torch.from_numpy(x).to(DEV), dw, split=s, workspace=ws)
+            torch.cuda.synchronize()
+            assert_close(y.cpu().numpy(), _oracle_y(pw, x), f"rep {rep} N={N} K={K} split={s}")
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_gemv_lm_head_shape(fp8):
+    """lm_head [262144, 3840]: the widest GEMV of the decode stream (1024 column tiles)."""
+    from g4b.quant_gpu import quant_device
+    N, K = 262144, 3840
+    gen = torch.Generator(device=DEV)
+    gen.manual_seed(4)
+    W = torch.randn((N, K), generator=gen, device=DEV).mul_(0.02)
+    dw = quant_device(W, pf=False, fp8=fp8, prefill_i8=False)
+    del W
+    x = activations(1, K, seed=9)[0].astype(np.float16)
+    for rep in range(2):
+        y = ops.gemv_i4(torch.from_numpy(x).to(DEV), dw, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+    wp = dw.wp.cpu().numpy().view(np.uint32)
+    sc = dw.scales.cpu().numpy()
+    ref = O.gemv(x.astype(np.float32), wp, sc.view(np.uint16) if not fp8 else sc, dw.scale_fmt, dw.inv, N, K, 1)
+    assert_close(y.cpu().numpy(), ref, f"lm_head fp8={fp8}")
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_gemv_pdl_chain_keeps_dependencies(fp8):
+    """GEMVs launched with programmatic dependent launch, each consuming the
+    previous one's output through one shared workspace, eager and in a graph."""
+    K = 3840
+    layers = [_packed(K, K, seed=40 + i, fp8=fp8) for i in range(4)]
+    x0 = activations(1, K, seed=3)[0]
+    ref = x0
+    for _, pw, _ in layers:
+        ref = _oracle_y(pw, ref.astype(np.float32)).astype(np.float32)
+    ws = torch.zeros(ops.gemv_workspace_bytes(1, K, K, 0) + 256, dtype=torch.uint8, device=DEV)
+    bufs = [torch.empty(K, device=DEV) for _ in range(len(layers) + 1)]
+    stream = torch.cuda.Stream()
+
+    def chain():
+        for i, (_, _, dw) in enumerate(layers):
+            ops.gemv_i4(bufs[i], dw, out=bufs[i + 1], stream=stream, workspace=ws, pdl=True)
+
+    bufs[0].copy_(torch.from_numpy(x0))
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        chain()
+    stream.synchronize()
+    assert_close(bufs[-1].cpu().numpy(), ref, f"pdl chain eager fp8={fp8}")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        chain()
+    for b in bufs[1:]:
+        b.zero_()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+    stream.synchronize()
+    assert_close(bufs[-1].cpu().numpy(), ref, f"pdl chain graph fp8={fp8}")
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+    del g
