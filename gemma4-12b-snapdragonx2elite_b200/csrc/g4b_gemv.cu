@@ -27,6 +27,7 @@
 //     them in slice order (deterministic), scales by inv and writes y -- the
 //     reduce.comp dispatch fused into the GEMV.
 #include <algorithm>
+#include <mutex>
 #include <utility>
 
 #include "g4b_common.cuh"
@@ -1248,6 +1249,35 @@ __global__ void dequant_i4_kernel(const uint32_t* __restrict__ wp, const void* _
     }
 }
 
+// ------------------------------------------------- allocation-free variant
+// Scratch for g4b_gemv_i4_noalloc: a fixed array in the library's own device
+// memory, present on every GPU that loads the library until the process ends.
+// Host code may only use its name through cudaGetSymbolAddress: on the host the
+// symbol is a stand-in, not a device address.
+constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[128];  // device address of the array, per device ordinal
+
+// Resolve (once per device, with that device current) the array's device address.
+static int noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    if (dev < 0 || dev >= 128) return fail(G4B_E_ARCH, "gemv_i4_noalloc: device index %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(G4B_E_CUDA, "gemv_i4_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return G4B_OK;
+}
+
 }  // namespace g4b
 
 using namespace g4b;
@@ -1413,6 +1443,34 @@ static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, c
         if (st != G4B_OK) return st;
     }
     return G4B_OK;
+}
+
+int g4b_gemv_i4_noalloc(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,
+                        float inv, void* y, int y_dtype, int N, int K, int split, g4b_stream_t stream) {
+    G4B_ENTRY("gemv_i4_noalloc");
+    G4B_REQUIRE(M >= 1 && N > 0 && K > 0 && K % 32 == 0 && N % 16 == 0, G4B_E_SHAPE,
+                "gemv_i4_noalloc: M=%d N=%d K=%d (N %% 16, K %% 32 required)", M, N, K);
+    G4B_REQUIRE(split >= 0 && (split == 0 || (K / 32) % split == 0), G4B_E_SHAPE,
+                "gemv_i4_noalloc: split=%d must divide K/32=%d (or be 0)", split, K / 32);
+    int st = check_device(nullptr);
+    if (st != G4B_OK) return st;
+    const size_t need = g4b_gemv_workspace_bytes(M, N, K, split);
+    clear_error();
+    G4B_REQUIRE(need <= kNoAllocScratchBytes, G4B_E_WORKSPACE,
+                "gemv_i4_noalloc: these sizes need %zu bytes of scratch; the built-in scratch holds %zu "
+                "(use g4b_gemv_i4 with a caller-provided workspace)",
+                need, kNoAllocScratchBytes);
+    void* ws = nullptr;
+    if (need) {
+        st = noalloc_scratch(&ws);
+        if (st != G4B_OK) return st;
+        // the arrival counters at the front of the scratch must start at zero; a previous call
+        // leaves them zero, but one that gave up (kernel status) may not: clear them every call
+        cudaError_t e = cudaMemsetAsync(ws, 0, kGemvCounterBytes, reinterpret_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4_noalloc: cudaMemsetAsync: %s", cudaGetErrorString(e));
+    }
+    t_pdl = false;
+    return gemv_i4_impl(x, x_dtype, M, wp, scales, scale_fmt, inv, y, y_dtype, N, K, split, ws, need, stream);
 }
 
 int g4b_reduce_partials(const float* partial, float* y, int N, int split, g4b_stream_t stream) {

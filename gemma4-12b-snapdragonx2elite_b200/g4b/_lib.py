@@ -55,6 +55,7 @@ SIGNATURES = {
     "g4b_gemv_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g4b_gemv_i4": (_I, [_P, _I, _I, _P, _P, _I, _F, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "g4b_gemv_i4_ex": (_I, [_P, _I, _I, _P, _P, _I, _F, _P, _I, _I, _I, _I, _P, _Z, C.c_uint, _P]),
+    "g4b_gemv_i4_noalloc": (_I, [_P, _I, _I, _P, _P, _I, _F, _P, _I, _I, _I, _I, _P]),
     "g4b_reduce_partials": (_I, [_P, _P, _I, _I, _P]),
     "g4b_dequant_i4": (_I, [_P, _P, _I, _F, _P, _I, _I, _I, _P]),
     "g4b_cast": (_I, [_P, _I, _P, _I, _Z, _P]),

@@ -132,6 +132,27 @@ G4B_API int g4b_gemv_i4_ex(const void* x, int x_dtype, int M,
                    void* y, int y_dtype, int N, int K, int split,
                    void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream);
 
+/* g4b_gemv_i4 for callers that cannot allocate device memory: no workspace
+ * argument.  This entry point has no counterpart in the reference (whose
+ * engine owns all its buffers); it exists for hosts that may not call
+ * cudaMalloc on the decode path -- e.g. code running inside a CUDA-graph
+ * capture or under a custom allocator that forbids allocation after
+ * start-up, or a plugin handed only input and output buffers.
+ *   - The split-K scratch lives in a fixed 4 MiB array inside the library,
+ *     held on every GPU that loads it until the process exits.  Sizes that
+ *     need more (g4b_gemv_workspace_bytes() > 4 MiB, e.g. M = 8 tokens of a
+ *     15360-wide GEMV) are rejected with G4B_E_WORKSPACE before anything runs.
+ *   - The first call on each device looks the array's address up
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - Every call enqueues a small memset of the array's counters, then the
+ *     same kernel as g4b_gemv_i4; nothing is allocated or freed.
+ *   - All calls share the one array, which keeps the last call's contents:
+ *     calls that can overlap on the GPU (different streams, or concurrent
+ *     host threads without ordering) race on it.  Serialise them on one stream. */
+G4B_API int g4b_gemv_i4_noalloc(const void* x, int x_dtype, int M,
+                        const uint32_t* wp, const void* scales, int scale_fmt, float inv,
+                        void* y, int y_dtype, int N, int K, int split, g4b_stream_t stream);
+
 /* Split-K partial reduction, vk/reduce.comp:8-12:
  *     y[n] = sum_{c=0}^{split-1} partial[c*N + n]   (c ascending, f32)
  * Exposed on its own for parity with the reference's reduce dispatch
