@@ -103,6 +103,18 @@ __global__ void __launch_bounds__(256) cast_i8_kernel(const void* __restrict__ X
     }
 }
 
+// f32 -> f16 (RNE) on `s` for the library's own use (the GEMMs' cast_dn step).
+int cast_f32_to_f16_async(const float* src, __half* dst, size_t n, cudaStream_t s) {
+    int sms = 148;
+    int st = check_device(&sms);
+    if (st != G4B_OK) return st;
+    const int threads = 256;
+    const int blocks = (int)std::max<size_t>(1, std::min<size_t>((n / 8 + threads - 1) / threads, (size_t)sms * 8));
+    cast_f32_to_f16_kernel<<<blocks, threads, 0, s>>>(src, dst, n);
+    count_launch();
+    return launch_status("cast f32->f16");
+}
+
 }  // namespace g4b
 
 using namespace g4b;

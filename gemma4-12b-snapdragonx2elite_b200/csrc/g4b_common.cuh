@@ -28,6 +28,9 @@ int launch_status(const char* op);
 // Read-and-clear the device status words the kernels raise (bounded waits that
 // gave up); 0 = clean.
 unsigned read_status_gemv();
+unsigned read_status_gemm();
+// f32 -> f16 (RNE) launched on `s` (the GEMMs' cast_dn step).
+int cast_f32_to_f16_async(const float* src, __half* dst, size_t n, cudaStream_t s);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -63,6 +63,8 @@ SIGNATURES = {
     "g4b_quant_i4": (_I, [_P, _I, _I, _P, _P, _P, _P, _P]),
     "g4b_quant_e4m3": (_I, [_P, _I, _I, _I, _P, _P]),
     "g4b_quant_w8a8": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
+    "g4b_gemm_i4_workspace_bytes": (_Z, [_I, _I, _I, _I]),
+    "g4b_gemm_i4": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
 }
 
 

@@ -127,6 +127,30 @@ def gemv_i4(x: torch.Tensor, w: DeviceWeight, split: int = 0, out: Optional[torc
     return out.view(-1) if squeeze else out
 
 
+def gemm_i4(X: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None,
+            out_dtype: torch.dtype = torch.float16, stream: Optional[torch.cuda.Stream] = None,
+            workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """W4A16 prefill GEMM: Y[M, N] = X[M, K] @ dequant(W) with f16 block scales
+    (gmm()'s f16 path: cast_dn -> coopgemm_i4h -> cast_up)."""
+    _need(X, "X")
+    M, K = X.shape
+    if K != w.K:
+        raise ValueError(f"gemm_i4: X has K={K}, weight has K={w.K}")
+    if out is None:
+        out = torch.empty((M, w.N), dtype=out_dtype, device=X.device)
+    _need(out, "out")
+    sh = _stream_handle(stream, X.device)
+    lib = L.load()
+    need = lib.g4b_gemm_i4_workspace_bytes(M, w.N, w.K, _DT[X.dtype])
+    ws = workspace
+    if need and ws is None:
+        ws = WORKSPACES.get(X.device, sh, need)
+    L.check("g4b_gemm_i4", lib.g4b_gemm_i4(
+        _ptr(X), _DT[X.dtype], _ptr(w.wp), _ptr(w.scales16), _ptr(out), _DT[out.dtype], M, w.N, w.K,
+        _ptr(ws), ws.numel() if ws is not None else 0, sh))
+    return out
+
+
 def reduce_partials(partial: torch.Tensor, split: int, out: Optional[torch.Tensor] = None,
                     stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
     _need(partial, "partial")

@@ -208,6 +208,26 @@ G4B_API int g4b_cast(const void* src, int src_dtype, void* dst, int dst_dtype, s
  *     A8[m,k] = clamp(round_half_even(X[m,k] * inv), -127, 127);  sa[m] = s   */
 G4B_API int g4b_cast_i8(const void* X, int x_dtype, int8_t* A8, float* sa, int M, int K, g4b_stream_t stream);
 
+/* ---------------------------------------------------------------- prefill GEMMs */
+
+/* Bytes of workspace g4b_gemm_i4 needs: non-zero only for f32 X, which is
+ * first converted to f16 in the workspace (the cast_dn step). */
+G4B_API size_t g4b_gemm_i4_workspace_bytes(int M, int N, int K, int x_dtype);
+
+/* W4A16 prefill GEMM with in-kernel dequantisation: vk/coopgemm_i4h.comp:13-35
+ * (the engine's path), vk/coopgemm_i4.comp:14-36 and vk/coopgemm_i4f.comp:12-35,
+ * dispatched by gmm() (src/vk_engine.py:391-400) between cast_dn and cast_up:
+ *     Y[m, n] = sum_k f16(X[m, k]) * f16((q[k, n] - 8) * f32(scale[k/32, n]))
+ * wp / scales_f16 are quant()'s packed words and f16 block scales (the
+ * prefill path always uses f16 scales, src/vk_engine.py:150).  The
+ * dequantised weights are bit-identical to the shader's; the accumulator is
+ * f32 (the i4h shader accumulates in f16).  X [M, K] f16 or f32 (f32 is
+ * converted to f16 in `workspace`, RNE, as cast_dn does); Y [M, N] f16 or f32.
+ * M >= 1 (any), N % 128 == 0, K % 64 == 0; pointers 16-byte aligned. */
+G4B_API int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* scales_f16,
+                        void* Y, int y_dtype, int M, int N, int K,
+                        void* workspace, size_t ws_bytes, g4b_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

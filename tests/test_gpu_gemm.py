@@ -1,0 +1,102 @@
+"""GPU parity of the W4A16 prefill GEMM (g4b_gemm_i4) through the C ABI.
+
+Oracle: oracle/g4b_oracle.c orc_gemm_i4 (vk/coopgemm_i4h.comp:13-35: the
+shader's f16 dequant, products summed in f32).  At the configs' full sizes the
+reference is a plain PyTorch fp32 matmul of the same f16 operands, with the
+dequantised weights taken from g4b_dequant_i4 (bit-exact against the oracle in
+test_gpu_gemv.py).  Floating-point bar (tests/util.py): max relative error
+<= 1e-2 with denominator max(|ref|, 1e-3 * rms(ref)), cosine >= 0.9999.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from g4b import _lib as L
+from g4b import ops, pack
+from util import assert_close, rel_err, weights, activations
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _dw(N, K, seed):
+    pw = pack.quant(weights(N, K, seed), fp8=False, prefill_i8=False)
+    return pw, ops.to_device(pw, DEV)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 128, 64), (256, 256, 128), (300, 384, 192), (1, 128, 64),
+                                   (17, 256, 320), (512, 640, 1024)])
+@pytest.mark.parametrize("xdt,ydt", [(torch.float16, torch.float16), (torch.float32, torch.float32),
+                                     (torch.float16, torch.float32)])
+def test_gemm_i4_matches_oracle(M, N, K, xdt, ydt):
+    pw, dw = _dw(N, K, seed=M + N + K)
+    X = activations(M, K, seed=3)
+    X16 = X.astype(np.float16)
+    ref = O.gemm_i4(X16.view(np.uint16), pw.wp, pw.scales16.view(np.uint16), M, N, K)
+    Xt = torch.from_numpy(X16 if xdt == torch.float16 else X16.astype(np.float32)).to(DEV)
+    Y = ops.gemm_i4(Xt, dw, out_dtype=ydt)
+    torch.cuda.synchronize()
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+    assert_close(Y.float().cpu().numpy(), ref, f"M={M} N={N} K={K} x={xdt} y={ydt}")
+
+
+def test_gemm_i4_f32_input_is_cast_rne():
+    """f32 X goes through the cast_dn step (RNE to f16) first: values that are not
+    f16-representable give the same result as pre-rounded f16 X."""
+    M, N, K = 256, 256, 256
+    pw, dw = _dw(N, K, seed=9)
+    X = activations(M, K, seed=4)
+    Y32 = ops.gemm_i4(torch.from_numpy(X).to(DEV), dw, out_dtype=torch.float32)
+    Y16 = ops.gemm_i4(torch.from_numpy(X.astype(np.float16)).to(DEV), dw, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(Y32, Y16)
+
+
+# Long-K guard.  With K = 3840..15360 every tensor-core f16 GEMM (cuBLAS's
+# included: max rel err 3.4e-2 at K = 15360 against the fp64 product) has
+# absolute errors near 1e-4 x rms(Y) from its f32 accumulation, which the
+# 1e-3 x rms guard turns into "relative" errors above 1e-2 on outputs that are
+# nearly zero.  These tests therefore use a guard of 1e-2 x rms(Y), keep the
+# 1e-2 max-rel and 0.9999 cosine bars, and also require the error to be no
+# worse than 1.5x that of torch's own f16 GEMM (cuBLAS) on the same operands.
+LONG_K_GUARD = 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 15360, 3840), (2048, 3840, 15360)])
+def test_gemm_i4_config3_against_torch_fp32(M, N, K):
+    """Config 3 at full size (and its down_proj shape) against torch fp32."""
+    pw, dw = _dw(N, K, seed=0)
+    X16 = torch.from_numpy(activations(M, K, seed=1).astype(np.float16)).to(DEV)
+    Y = ops.gemm_i4(X16, dw, out_dtype=torch.float16)
+    Wd = ops.dequant_i4(dw, out_dtype=torch.float16)          # [K, N], bit-exact dequant
+    ref = (X16.double() @ Wd.double()).cpu().numpy()
+    cub = (X16 @ Wd).float().cpu().numpy()                    # cuBLAS f16 GEMM, for scale
+    torch.cuda.synchronize()
+    out = Y.float().cpu().numpy()
+    assert_close(out, ref, f"config3 M={M} N={N} K={K}", guard=LONG_K_GUARD)
+    assert rel_err(out, ref, LONG_K_GUARD) <= 1.5 * rel_err(cub, ref, LONG_K_GUARD) + 1e-4
+
+
+def test_gemm_i4_deterministic_and_repeatable():
+    M, N, K = 1024, 1024, 512
+    pw, dw = _dw(N, K, seed=2)
+    X16 = torch.from_numpy(activations(M, K, seed=5).astype(np.float16)).to(DEV)
+    a = ops.gemm_i4(X16, dw)
+    b = ops.gemm_i4(X16, dw)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_gemm_i4_rejects_bad_shapes():
+    lib = L.load()
+    X = torch.zeros((4, 64), dtype=torch.float16, device=DEV)
+    Y = torch.zeros((4, 136), dtype=torch.float16, device=DEV)
+    wp = torch.zeros((64, 17), dtype=torch.int32, device=DEV)
+    sc = torch.zeros((2, 136), dtype=torch.float16, device=DEV)
+    st = lib.g4b_gemm_i4(X.data_ptr(), 1, wp.data_ptr(), sc.data_ptr(), Y.data_ptr(), 1, 4, 136, 64, None, 0,
+                         torch.cuda.current_stream().cuda_stream)
+    assert st == L.G4B_E_SHAPE
+    st = lib.g4b_gemm_i4(X.float().data_ptr(), 0, wp.data_ptr(), sc.data_ptr(), Y.data_ptr(), 1, 4, 128, 64, None,
+                         0, torch.cuda.current_stream().cuda_stream)
+    assert st == L.G4B_E_WORKSPACE

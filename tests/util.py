@@ -29,10 +29,12 @@ def cosine(a, b) -> float:
     return float(a @ b / (na * nb + 1e-300))
 
 
-def assert_close(out, ref, what: str = "", max_rel: float = MAX_REL, min_cos: float = MIN_COS):
-    e = rel_err(out, ref)
+def assert_close(out, ref, what: str = "", max_rel: float = MAX_REL, min_cos: float = MIN_COS,
+                 guard: float = GUARD):
+    e = rel_err(out, ref, guard)
     c = cosine(out, ref)
-    assert e <= max_rel and c >= min_cos, f"{what}: max rel err {e:.3e} (<= {max_rel}), cos {c:.6f} (>= {min_cos})"
+    assert e <= max_rel and c >= min_cos, \
+        f"{what}: max rel err {e:.3e} (<= {max_rel}, guard {guard} x rms), cos {c:.6f} (>= {min_cos})"
 
 
 def weights(N: int, K: int, seed: int = 0, std: float = 0.02) -> np.ndarray:
