@@ -185,9 +185,12 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="stream", choices=["stream", "gemv"],
-                    help="stream: configs[1] decode weight stream (default); gemv: configs[0] single GEMV")
+    ap.add_argument("--workload", default="stream", choices=["stream", "gemv"] + list(GEMM_WORKLOADS),
+                    help="stream: configs[1] decode weight stream (default); gemv: configs[0] single GEMV; "
+                         "gemm_i4 / gemm_i4_down: configs[2] W4A16 prefill GEMM; w8a8 / w4a8: configs[3]")
     args = ap.parse_args()
+    if args.workload in GEMM_WORKLOADS:
+        return run_gemm(args)
     fp8 = args.scales == "fp8"
     metric = "int4 GEMV HBM GB/s (decode weight stream, 48 layers + lm_head, batch 1)"
 
@@ -398,6 +401,198 @@ def main():
                "bytes_per_step": step_bytes}
         print(json.dumps(out), flush=True)
     del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------ prefill GEMMs
+# name -> (M, N, K, kind, BASELINE.json config it is quoted on)
+GEMM_WORKLOADS = {
+    "gemm_i4": (2048, FFN, HIDDEN, "w4a16", "configs[2]: W4A16 prefill GEMM X[2048, 3840] x W[15360, 3840]"),
+    "gemm_i4_down": (2048, HIDDEN, FFN, "w4a16", "configs[2]: W4A16 prefill GEMM, down_proj shape K=15360, N=3840"),
+    "w8a8": (4096, HIDDEN, FFN, "w8a8", "configs[3]: W8A8 prefill GEMM X[4096, 15360] f16 -> cast_i8 -> int8 GEMM"),
+    "w4a8": (4096, HIDDEN, FFN, "w4a8", "configs[3] shape, W4A8: int4 weights requantised in the kernel"),
+}
+
+
+def _gemm_cpu_sample(kind, M, N, K, seconds, O):
+    """The oracle GEMM on a bounded sample of the workload: `rows` token rows of
+    the same [N, K] weights, repeated until `seconds` have elapsed."""
+    rng = np.random.default_rng(0)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    r = O.pack_reference(W, prefill_i8=kind != "w4a16")
+    rows = 32
+    X = rng.standard_normal((rows, K)).astype(np.float16)
+    if kind == "w4a8":
+        ratio = O.w4a8_ratio(r["sc_f32"], r["sw_f32"])
+    done, n, t0 = 0, 0, time.perf_counter()
+    while True:
+        if kind == "w4a16":
+            O.gemm_i4(X.view(np.uint16), r["wp"], r["scales16"].view(np.uint16), rows, N, K)
+        else:
+            A8, sa = O.cast_i8(X.astype(np.float32))
+            if kind == "w8a8":
+                O.gemm_w8a8(A8, r["w8"], sa, r["sw8"].view(np.uint16))
+            else:
+                O.gemm_w4a8(A8, r["wp"], ratio, sa, r["sw8"].view(np.uint16), N)
+        done += 2 * rows * N * K
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            return done / dt / 1e12, n, rows, dt
+
+
+def run_gemm(args):
+    """One prefill GEMM per step; value = 2*M*N*K / device time."""
+    M, N, K, kind, wl = GEMM_WORKLOADS[args.workload]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    unit = "TFLOP/s" if kind == "w4a16" else "TOPS"
+    metric = f"{'W4A16' if kind == 'w4a16' else kind.upper()} prefill GEMM {unit} (M={M}, N={N}, K={K})"
+    config = {"workload": wl, "M": M, "N": N, "K": K, "parallelism": f"replicas{world}",
+              "l2": "256 MB buffer written between timed iterations (L2 flush, outside the events)"}
+    flops = 2 * M * N * K
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        import oracle as O
+        val, n, rows, dt = _gemm_cpu_sample(kind, M, N, K, max(2.0, args.cpu_seconds / 2), O)
+        cpu = {"value": round(val, 5), "unit": unit, "cores": O.num_threads(), "kind": "port",
+               "sample": f"oracle {kind} GEMM on {rows} token rows x the full [{N}, {K}] weight, {n} runs in {dt:.1f} s"}
+        print(json.dumps({"metric": metric, "value": cpu["value"], "unit": unit, "n_gpus": world, "steps": n,
+                          "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "f32" if kind == "w4a16" else "int32", "data": "synthetic", "config": config,
+                          "impl": "reference", "cpu_baseline": cpu,
+                          "e2e": {"value": cpu["value"], "unit": unit, "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from g4b import _lib as L
+    from g4b import ops
+    from g4b import quant_gpu as qz
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    L.load()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    W = torch.randn((N, K), generator=gen, device=device).mul_(0.02)
+    w = qz.quant_device(W, pf=True, fp8=False, prefill_i8=kind != "w4a16", w4a8=kind == "w4a8")
+    del W
+    X = torch.randn((M, K), generator=gen, device=device).to(torch.float16)
+    Y = torch.empty((M, N), dtype=torch.float16, device=device)
+    A8 = torch.empty((M, K), dtype=torch.int8, device=device)
+    sa = torch.empty((M,), dtype=torch.float32, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.Stream(device)
+    sh = int(stream.cuda_stream)
+    lib = L.load()
+
+    def gemm():
+        if kind == "w4a16":
+            ops.gemm_i4(X, w, out=Y, stream=stream)
+        elif kind == "w8a8":
+            ops.gemm_w8a8(A8, sa, w, out=Y, stream=stream)
+        else:
+            ops.gemm_w4a8(A8, sa, w, out=Y, stream=stream)
+
+    def step(ev=None, i=0):
+        if kind != "w4a16":
+            L.check("g4b_cast_i8", lib.g4b_cast_i8(X.data_ptr(), L.DT_F16, A8.data_ptr(), sa.data_ptr(), M, K, sh))
+        if ev is not None:
+            ev[i][1].record(stream)
+        gemm()
+
+    n = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            step()
+    stream.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(n):
+            flush.zero_()
+            ev[i][0].record(stream)
+            step(ev, i)
+            ev[i][2].record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    step_ms = sum(e[0].elapsed_time(e[2]) for e in ev)
+    kern_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
+    if world > 1:
+        t = torch.tensor([step_ms, kern_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms, kern_ms = float(t[0]), float(t[1])
+    value = world * flops * n / (step_ms / 1e3) / 1e12
+    achieved = flops * n / (kern_ms / 1e3) / 1e12
+    peak, src = None, "of measured"
+    try:
+        pk = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))
+        peak = float(pk["bf16_tflops"])
+    except Exception:
+        peak, src = 1590.0, "of fallback"
+    if kind != "w4a16":
+        peak, src = 2 * peak, src + " bf16 x 2 (dense int8 rate is twice the f16 rate)"
+    kname = {"w4a16": "gemm_w4a16_kernel", "w8a8": "gemm_s8_kernel<W8A8>", "w4a8": "gemm_s8_kernel<W4A8>"}[kind]
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": unit,
+                "frac": round(achieved / peak, 4), "traffic": None, "peak_source": src, "kernel": kname,
+                "launches_timed": n, "avg_launch_us": round(kern_ms * 1e3 / n, 2)}
+    tp = os.path.join(REPO, "profiles", "gemm_traffic.json")
+    if os.path.exists(tp):
+        try:
+            roofline["traffic"] = json.load(open(tp)).get(args.workload)
+        except Exception:
+            pass
+
+    # e2e: f16 activations from pinned host memory, the f16 output back, every step
+    Xh = X.cpu().pin_memory()
+    Yh = torch.empty((M, N), dtype=torch.float16).pin_memory()
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            X.copy_(Xh, non_blocking=True)
+            step()
+            Yh.copy_(Y, non_blocking=True)
+        stream.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n):
+            X.copy_(Xh, non_blocking=True)
+            step()
+            Yh.copy_(Y, non_blocking=True)
+            stream.synchronize()
+        e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t[0])
+    e2e = world * flops * n / e2e_s / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle as O
+        val, cn, rows, dt = _gemm_cpu_sample(kind, M, N, K, args.cpu_seconds, O)
+        cpu = {"value": round(val, 5), "unit": unit, "cores": O.num_threads(), "kind": "port",
+               "sample": f"oracle {kind} GEMM on {rows} token rows x the full [{N}, {K}] weight, {cn} runs in {dt:.1f} s"}
+    if rank == 0:
+        print(json.dumps({"metric": metric, "value": round(value, 1), "unit": unit, "n_gpus": world, "steps": n,
+                          "warmup": args.warmup, "ms_per_step": round(step_ms / n, 4), "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None,
+                          "dtype": "f16 x f16 -> f32 acc" if kind == "w4a16" else "s8 x s8 -> s32 acc",
+                          "data": "synthetic (seeded N(0,0.02) weights, N(0,1) f16 activations)", "config": config,
+                          "roofline": roofline, "cpu_baseline": cpu,
+                          "e2e": {"value": round(e2e, 1), "unit": unit, "h2d_bytes_per_step": M * K * 2,
+                                  "d2h_bytes_per_step": M * N * 2},
+                          "gpu_launches": n * (1 if kind == "w4a16" else 2), "clocks": clk}), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -81,6 +81,18 @@ __device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
     return d;
 }
 
+__device__ __forceinline__ uint32_t hmin2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("min.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hmax2_u(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 // Two packed e4m3 bytes (low 16 bits of `v`) -> f16x2, exact.
 __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t v) {
     uint32_t d;

@@ -255,6 +255,298 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
     if (warp == 1) tc::tmem_dealloc(tmem, kW4TmemCols);
 }
 
+// ------------------------------------------------------------ W8A8 / W4A8
+// vk/coopgemm_w8a8.comp:18-37 and vk/coopgemm_w4a8.comp:21-50:
+//     C[m, n] = sum_k A8[m, k] * W8[k, n]            (exact int32)
+//     Y[m, n] = f16((float(C) * sa[m]) * f32(sw[n]))
+// with W8 either the prepared int8 weights [K, N] (W8A8) or, for W4A8, the
+// packed int4 words requantised in the kernel against a per-column scale:
+//     W8[k, n] = clamp(round_half_even((q - 8) * f32(ratio[k/32, n])), -127, 127)
+//
+// Same transposed product as W4A16: D[n, m] in tensor memory, weight columns
+// on the 128 lanes, 256 tokens per tile.  tcgen05.mma kind::i8.
+//   W8A8: both operands come from shared memory.  The weight tile is TMA'd
+//         straight from the reference's [K, N] row-major int8 array, which is
+//         an MN-major operand (128-byte swizzle, one 128-column group per
+//         tile), so no repacking of the weights is needed.  Two accumulator
+//         buffers (2 x 256 TMEM columns) let the epilogue of one tile overlap
+//         the MMAs of the next.
+//   W4A8: 16 requant warps write the int8 weights to tensor memory as the
+//         MMA's A operand (four K values per 32-bit column), like the W4A16
+//         dequant.  Exact round-half-even without any conversion
+//         instruction: fma.rn.f16x2((q - 8), r, 1536) rounds the exact
+//         product once at a spacing of 1.0, and the low byte of the f16
+//         result is the int8 two's-complement value.
+constexpr int kS8BN = 128;                              // weight columns per tile
+constexpr int kS8BT = 256;                              // tokens per tile
+constexpr int kS8BK = 128;                              // K per stage (one 128-byte swizzle row)
+constexpr int kS8Stages = 4;
+constexpr int kS8ABytes = kS8BT * kS8BK;                // activations [256 x 128] s8: 32 KB
+constexpr int kS8W8Bytes = kS8BK * kS8BN;               // W8 [128 K x 128 n] s8: 16 KB
+constexpr int kS8WpBytes = kS8BK * (kS8BN / 8) * 4;     // packed words [128 K x 16]: 8 KB
+constexpr int kS8RBytes = (kS8BK / 32) * kS8BN * 2;     // ratio [4 x 128] f16: 1 KB
+constexpr int kS8DqWarps = 16;
+
+template <bool W4>
+struct S8Cfg {
+    static constexpr int kDq = W4 ? kS8DqWarps : 0;
+    static constexpr int kThreads = (2 + kDq + 4) * 32;
+    static constexpr int kWBytes = W4 ? kS8WpBytes + kS8RBytes : kS8W8Bytes;
+    static constexpr int kStageBytes = kS8ABytes + kWBytes;
+    static constexpr int kAccBufs = W4 ? 1 : 2;
+    static constexpr int kACol = 256;                   // W4A8: first tensor-memory A column
+    static constexpr size_t kSmem = 1024 + (size_t)kS8Stages * kStageBytes;
+};
+static_assert(256 + 32 * kS8Stages <= 512, "TMEM budget");
+
+struct S8Args {
+    void* y;
+    int32_t* c;           // nullable raw accumulators
+    const float* sa;      // [M]
+    const uint16_t* sw;   // [N] f16
+    int M, N, K, nkb, ntm, ntiles;
+};
+
+template <bool W4, bool YF32>
+__global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
+    gemm_s8_kernel(const S8Args a, const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
+                   const __grid_constant__ CUtensorMap rmap) {
+    using Cfg = S8Cfg<W4>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ uint64_t bars[3 * kS8Stages + 5];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    volatile int* abort_flag = &s_abort;
+    const uint32_t raw0 = smem_u32(smem_raw);
+    const uint32_t sm0 = (raw0 + 1023u) & ~1023u;            // activation stages (1024-aligned)
+    const uint32_t smw = sm0 + kS8Stages * kS8ABytes;         // weight stages (W8, or words + ratio)
+    const uint8_t* gsm = smem_raw + (sm0 - raw0);
+    const uint8_t* wsm_b = gsm + kS8Stages * kS8ABytes;
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kS8Stages + s); };
+    auto afull_bar = [&](int s) { return bar0 + 8u * (2 * kS8Stages + s); };
+    auto dfull_bar = [&](int b) { return bar0 + 8u * (3 * kS8Stages + b); };
+    auto dempty_bar = [&](int b) { return bar0 + 8u * (3 * kS8Stages + 2 + b); };
+    const uint32_t drain_bar = bar0 + 8u * (3 * kS8Stages + 4);
+
+    if (tid == 0) {
+        for (int s = 0; s < kS8Stages; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), Cfg::kDq + 1);  // requant warps + the MMA commit
+            mbar_init(afull_bar(s), Cfg::kDq > 0 ? Cfg::kDq : 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(dfull_bar(b), 1);
+            mbar_init(dempty_bar(b), 4);
+        }
+        mbar_init(drain_bar, 1);
+        s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(smem_u32(&s_tmem), 512);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = s_tmem;
+    const int nks = a.nkb;
+
+    if (warp == 0) {
+        // ------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            prefetch_tensor_map(&amap);
+            prefetch_tensor_map(&wmap);
+            if (W4) prefetch_tensor_map(&rmap);
+            uint64_t pol_keep;
+            asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_keep));
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x) {
+                const int nt = t / a.ntm, mt = t % a.ntm;
+                for (int kb = 0; kb < nks; kb++, it++) {
+                    const int s = it % kS8Stages;
+                    if (it >= kS8Stages &&
+                        !mbar_wait(empty_bar(s), ((it / kS8Stages) & 1) ^ 1, abort_flag, &g_gemm_status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_bar(s), Cfg::kStageBytes);
+                    tma_load_2d(sm0 + s * kS8ABytes, &amap, kb * kS8BK, mt * kS8BT, full_bar(s), pol_keep);
+                    if (W4) {
+                        const uint32_t dst = smw + s * Cfg::kWBytes;
+                        tma_load_2d(dst, &wmap, nt * (kS8BN / 8), kb * kS8BK, full_bar(s), pol_keep);
+                        tma_load_2d(dst + kS8WpBytes, &rmap, nt * kS8BN, kb * (kS8BK / 32), full_bar(s), pol_keep);
+                    } else {
+                        tma_load_2d(smw + s * Cfg::kWBytes, &wmap, nt * kS8BN, kb * kS8BK, full_bar(s), pol_keep);
+                    }
+                }
+            }
+            for (int i = std::max(0, it - kS8Stages); i < it; i++)
+                mbar_wait_drain(full_bar(i % kS8Stages), (i / kS8Stages) & 1, &g_gemm_status);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            // D s32, A/B s8; A MN-major from shared memory (W8A8) or K-major from TMEM (W4A8)
+            constexpr uint32_t idesc = tc::idesc(2, 1, 1, W4 ? 0 : 1, 0, kS8BT, kS8BN);
+            int it = 0, tc_i = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x, tc_i++) {
+                const int buf = tc_i % Cfg::kAccBufs;
+                const uint32_t use = (uint32_t)(tc_i / Cfg::kAccBufs);
+                if (!mbar_wait(dempty_bar(buf), (use & 1) ^ 1, abort_flag, &g_gemm_status)) break;
+                tc::fence_after();
+                const uint32_t dt = tmem + (uint32_t)(buf * kS8BT);
+                for (int kb = 0; kb < nks; kb++, it++) {
+                    const int s = it % kS8Stages;
+                    const uint32_t ph = (it / kS8Stages) & 1;
+                    if (!mbar_wait(full_bar(s), ph, abort_flag, &g_gemm_status) ||
+                        (W4 && !mbar_wait(afull_bar(s), ph, abort_flag, &g_gemm_status))) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after();
+                    const uint64_t bdesc = tc::sdesc_sw128(sm0 + s * kS8ABytes, 16, 1024);
+#pragma unroll
+                    for (int kk = 0; kk < kS8BK / 32; kk++) {
+                        if (W4) {
+                            tc::mma_i8_ts(dt, tmem + Cfg::kACol + s * (kS8BK / 4) + kk * 8, bdesc + (uint64_t)(kk * 2),
+                                          idesc, (kb | kk) != 0);
+                        } else {
+                            // MN-major A: 32 K rows of 128 bytes per MMA step
+                            const uint64_t adesc =
+                                tc::sdesc_sw128(smw + s * Cfg::kWBytes + kk * 32 * 128, kS8W8Bytes, 1024);
+                            tc::mma_i8_ss(dt, adesc, bdesc + (uint64_t)(kk * 2), idesc, (kb | kk) != 0);
+                        }
+                    }
+                    tc::commit(empty_bar(s));
+                }
+                if (ok) tc::commit(dfull_bar(buf));
+            }
+            tc::commit(drain_bar);
+            mbar_wait_drain(drain_bar, 0, &g_gemm_status);
+        }
+    } else if (W4 && warp < 2 + Cfg::kDq) {
+        // ------------------------------------------------------- W4A8 requant
+        const int q = warp & 3;                 // TMEM lane quarter this warp may access
+        const int kq = (warp - 2) >> 2;         // which 32-row block of the stage
+        const int nl = q * 32 + lane;
+        const int g = nl >> 3, j = nl & 7;
+        const uint32_t sel = (uint32_t)(j >> 1) | ((uint32_t)(4 + (j >> 1)) << 8);
+        const uint32_t sh = (uint32_t)(j & 1) * 4u;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x) {
+            for (int kb = 0; kb < nks; kb++, it++) {
+                const int s = it % kS8Stages;
+                if (!mbar_wait(full_bar(s), (it / kS8Stages) & 1, abort_flag, &g_gemm_status)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t* wr =
+                    reinterpret_cast<const uint32_t*>(wsm_b + s * Cfg::kWBytes) + kq * 32 * (kS8BN / 8) + g;
+                const uint32_t r = reinterpret_cast<const uint16_t*>(wsm_b + s * Cfg::kWBytes + kS8WpBytes)[kq * kS8BN + nl];
+                const uint32_t r2 = r | (r << 16);
+                // |(q - 8) * r| < 127.5 whenever |r| < 15.9375: no clamp needed
+                const bool big = (r & 0x7fffu) >= 0x4bf8u;
+                uint32_t v[8];
+                if (!__any_sync(0xffffffffu, big)) {
+#pragma unroll
+                    for (int p = 0; p < 8; p++) {
+                        uint32_t t2[2];
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int k = 4 * p + 2 * h;
+                            uint32_t u = prmt(wr[k * (kS8BN / 8)], wr[(k + 1) * (kS8BN / 8)], sel) >> sh;
+                            u = and_or(u, 0x000F000Fu, 0x64006400u);      // f16 (1024 + q) pair
+                            u = hsub2_u(u, 0x64086408u);                   // exact q - 8
+                            t2[h] = hfma2_u(u, r2, 0x66006600u);           // 1536 + rne((q - 8) * r)
+                        }
+                        v[p] = prmt(t2[0], t2[1], 0x6420u);                // low bytes: the int8 values
+                    }
+                } else {
+#pragma unroll
+                    for (int p = 0; p < 8; p++) {
+                        uint32_t t2[2];
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int k = 4 * p + 2 * h;
+                            uint32_t u = prmt(wr[k * (kS8BN / 8)], wr[(k + 1) * (kS8BN / 8)], sel) >> sh;
+                            u = and_or(u, 0x000F000Fu, 0x64006400u);
+                            u = hsub2_u(u, 0x64086408u);
+                            u = hfma2_u(u, r2, 0x66006600u);
+                            t2[h] = hmin2_u(hmax2_u(u, 0x65816581u), 0x667F667Fu);  // clamp to 1536 -+ 127
+                        }
+                        v[p] = prmt(t2[0], t2[1], 0x6420u);
+                    }
+                }
+                tc::st_32x32b_x8(tmem + lane_addr + Cfg::kACol + s * (kS8BK / 4) + kq * 8, v);
+                tc::wait_st();
+                tc::fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(afull_bar(s));
+                    mbar_arrive(empty_bar(s));
+                }
+            }
+        }
+    } else if (warp >= 2 + Cfg::kDq) {
+        // ------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const int nl = q * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        int tc_i = 0;
+        for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, tc_i++) {
+            const int buf = tc_i % Cfg::kAccBufs;
+            const uint32_t use = (uint32_t)(tc_i / Cfg::kAccBufs);
+            if (!mbar_wait(dfull_bar(buf), use & 1, abort_flag, &g_gemm_status)) break;
+            tc::fence_after();
+            const int nt = t / a.ntm, mt = t % a.ntm;
+            const int n = nt * kS8BN + nl;
+            const bool nok = n < a.N;
+            const float swf = nok ? __half2float(__ushort_as_half(a.sw[n])) : 0.0f;
+            const int m0 = mt * kS8BT;
+#pragma unroll 1
+            for (int c = 0; c < kS8BT / 32; c++) {
+                const int mb = m0 + c * 32;
+                if (mb >= a.M) break;
+                uint32_t r[32];
+                tc::ld_32x32b_x32(tmem + lane_addr + (uint32_t)(buf * kS8BT + c * 32), r);
+                tc::wait_ld();
+                const float sav = mb + lane < a.M ? a.sa[mb + lane] : 0.0f;
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const float sam = __shfl_sync(0xffffffffu, sav, i);
+                    const int m = mb + i;
+                    if (m < a.M && nok) {
+                        const int32_t cv = (int32_t)r[i];
+                        if (a.c) a.c[(size_t)m * a.N + n] = cv;
+                        const float f = __fmul_rn(__fmul_rn((float)cv, sam), swf);
+                        if (YF32)
+                            reinterpret_cast<float*>(a.y)[(size_t)m * a.N + n] = f;
+                        else
+                            reinterpret_cast<__half*>(a.y)[(size_t)m * a.N + n] = __float2half_rn(f);
+                    }
+                }
+            }
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dempty_bar(buf));
+        }
+    }
+
+    __syncwarp();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (warp == 1) tc::tmem_dealloc(tmem, 512);
+}
+
 static size_t w4a16_ws(int M, int K, int x_dtype) {
     return x_dtype == G4B_DT_F32 ? (((size_t)M * K * 2 + 255) & ~(size_t)255) : 0;
 }
@@ -322,6 +614,89 @@ int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* 
     kern<<<grid, kW4Threads, kW4Smem, s>>>(a, xmap, wmap, smap);
     count_launch();
     return launch_status("gemm_i4");
+}
+
+}  // extern "C"
+
+namespace g4b {
+
+template <bool W4>
+static int launch_s8(const char* op, const int8_t* A8, const void* W, const uint16_t* ratio, const float* sa,
+                     const uint16_t* sw, void* Y, int y_dtype, int32_t* C, int M, int N, int K, cudaStream_t s) {
+    using Cfg = S8Cfg<W4>;
+    int sms = 0;
+    int st = check_device(&sms);
+    if (st != G4B_OK) return st;
+    CUtensorMap amap, wmap, rmap;
+    st = tensor_map_2d(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, A8, (uint64_t)K, (uint64_t)M, (uint64_t)K, kS8BK, kS8BT,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st == G4B_OK) {
+        if (W4)
+            st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, (uint64_t)N / 8, (uint64_t)K, (uint64_t)N / 2,
+                               kS8BN / 8, kS8BK, CU_TENSOR_MAP_SWIZZLE_NONE);
+        else
+            st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, W, (uint64_t)N, (uint64_t)K, (uint64_t)N, kS8BN,
+                               kS8BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (st == G4B_OK && W4)
+        st = tensor_map_2d(&rmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ratio, (uint64_t)N, (uint64_t)K / 32,
+                           (uint64_t)N * 2, kS8BN, kS8BK / 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != G4B_OK) return st;
+    if (!W4) rmap = wmap;  // unused
+    S8Args a;
+    a.y = Y;
+    a.c = C;
+    a.sa = sa;
+    a.sw = sw;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.nkb = (K + kS8BK - 1) / kS8BK;
+    a.ntm = (M + kS8BT - 1) / kS8BT;
+    a.ntiles = ((N + kS8BN - 1) / kS8BN) * a.ntm;
+    auto kern = y_dtype == G4B_DT_F32 ? gemm_s8_kernel<W4, true> : gemm_s8_kernel<W4, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "%s: cudaFuncSetAttribute: %s", op, cudaGetErrorString(e));
+    const int grid = std::min(a.ntiles, sms);
+    kern<<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(a, amap, wmap, rmap);
+    count_launch();
+    return launch_status(op);
+}
+
+}  // namespace g4b
+
+extern "C" {
+
+int g4b_gemm_w8a8(const int8_t* A8, const int8_t* W8, const float* sa, const uint16_t* sw_f16, void* Y, int y_dtype,
+                  int32_t* C_debug, int M, int N, int K, g4b_stream_t stream) {
+    G4B_ENTRY("gemm_w8a8");
+    G4B_REQUIRE(A8 && W8 && sa && sw_f16 && Y, G4B_E_ARG, "gemm_w8a8: NULL pointer");
+    G4B_REQUIRE(y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16, G4B_E_ARG, "gemm_w8a8: bad y_dtype %d", y_dtype);
+    G4B_REQUIRE(M >= 1 && N >= 16 && K >= 32 && N % 16 == 0 && K % 32 == 0, G4B_E_SHAPE,
+                "gemm_w8a8: need M >= 1, N %% 16 == 0, K %% 32 == 0 (got M=%d N=%d K=%d)", M, N, K);
+    G4B_REQUIRE((long long)M * K < (1ll << 40) && (long long)M * N < (1ll << 40) && (long long)K * N < (1ll << 40),
+                G4B_E_SHAPE, "gemm_w8a8: too large");
+    G4B_REQUIRE(aligned16(A8) && aligned16(W8) && aligned16(Y) && (!C_debug || aligned16(C_debug)), G4B_E_ALIGN,
+                "gemm_w8a8: A8, W8, Y and C_debug must be 16-byte aligned");
+    return launch_s8<false>("gemm_w8a8", A8, W8, nullptr, sa, sw_f16, Y, y_dtype, C_debug, M, N, K,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+int g4b_gemm_w4a8(const int8_t* A8, const uint32_t* wp, const uint16_t* ratio_f16, const float* sa,
+                  const uint16_t* sw_f16, void* Y, int y_dtype, int32_t* C_debug, int M, int N, int K,
+                  g4b_stream_t stream) {
+    G4B_ENTRY("gemm_w4a8");
+    G4B_REQUIRE(A8 && wp && ratio_f16 && sa && sw_f16 && Y, G4B_E_ARG, "gemm_w4a8: NULL pointer");
+    G4B_REQUIRE(y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16, G4B_E_ARG, "gemm_w4a8: bad y_dtype %d", y_dtype);
+    G4B_REQUIRE(M >= 1 && N >= 32 && K >= 32 && N % 32 == 0 && K % 32 == 0, G4B_E_SHAPE,
+                "gemm_w4a8: need M >= 1, N %% 32 == 0, K %% 32 == 0 (got M=%d N=%d K=%d)", M, N, K);
+    G4B_REQUIRE((long long)M * K < (1ll << 40) && (long long)M * N < (1ll << 40) && (long long)K * N < (1ll << 40),
+                G4B_E_SHAPE, "gemm_w4a8: too large");
+    G4B_REQUIRE(aligned16(A8) && aligned16(wp) && aligned16(ratio_f16) && aligned16(Y) &&
+                    (!C_debug || aligned16(C_debug)),
+                G4B_E_ALIGN, "gemm_w4a8: A8, wp, ratio, Y and C_debug must be 16-byte aligned");
+    return launch_s8<true>("gemm_w4a8", A8, wp, ratio_f16, sa, sw_f16, Y, y_dtype, C_debug, M, N, K,
+                           reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

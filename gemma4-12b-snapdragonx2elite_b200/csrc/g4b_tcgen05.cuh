@@ -110,6 +110,14 @@ __device__ __forceinline__ void st_32x32b_x16(uint32_t taddr, const uint32_t (&v
         : "memory");
 }
 
+// Warp-collective: lane i of the warp writes 8 consecutive 32-bit columns of
+// tensor-memory lane (taddr.lane + i).
+__device__ __forceinline__ void st_32x32b_x8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
 // Warp-collective: lane i reads 32 consecutive 32-bit columns of lane (taddr.lane + i).
 __device__ __forceinline__ void ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(

@@ -72,15 +72,19 @@ def to_device(pw: PackedWeight, device="cuda", w4a8: bool = False) -> DeviceWeig
 
 # ------------------------------------------------------------------ workspace
 class _Workspaces:
-    """Zero-filled scratch per (device, stream), grown on demand (never on a hot
-    path once warmed up: the same size is reused)."""
+    """Zero-filled scratch per (device, stream, use), grown on demand (never on
+    a hot path once warmed up: the same size is reused).
+
+    Each use has its own buffer: the GEMV workspace begins with arrival
+    counters that every GEMV leaves at zero for the next one, so no other
+    kernel may write it (the W4A16 GEMM's f32 -> f16 staging has its own)."""
 
     def __init__(self):
         self._lock = threading.Lock()
         self._bufs: dict = {}
 
-    def get(self, device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
-        key = (device.index, stream)
+    def get(self, device: torch.device, stream: int, nbytes: int, use: str = "gemv") -> torch.Tensor:
+        key = (device.index, stream, use)
         with self._lock:
             buf = self._bufs.get(key)
             if buf is None or buf.numel() < nbytes:
@@ -144,10 +148,59 @@ def gemm_i4(X: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None
     need = lib.g4b_gemm_i4_workspace_bytes(M, w.N, w.K, _DT[X.dtype])
     ws = workspace
     if need and ws is None:
-        ws = WORKSPACES.get(X.device, sh, need)
+        ws = WORKSPACES.get(X.device, sh, need, use="gemm_i4")
     L.check("g4b_gemm_i4", lib.g4b_gemm_i4(
         _ptr(X), _DT[X.dtype], _ptr(w.wp), _ptr(w.scales16), _ptr(out), _DT[out.dtype], M, w.N, w.K,
         _ptr(ws), ws.numel() if ws is not None else 0, sh))
+    return out
+
+
+def gemm_w8a8(A8: torch.Tensor, sa: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None,
+              out_dtype: torch.dtype = torch.float16, acc: Optional[torch.Tensor] = None,
+              stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """W8A8 prefill GEMM (PREFILL_I8): Y = f16((A8 @ W8) * sa[m] * sw[n]).
+
+    A8 [M, K] int8 and sa [M] f32 come from cast_i8; the weight's int8 W8
+    [K, N] and f16 sw8 [N] come from quant(..., prefill_i8=True).  acc, if
+    given ([M, N] int32), receives the exact int32 accumulators."""
+    _need(A8, "A8")
+    _need(sa, "sa")
+    if w.w8 is None or w.sw8 is None:
+        raise ValueError("gemm_w8a8: weight was packed without prefill_i8 (no int8 weights)")
+    M, K = A8.shape
+    if K != w.K or A8.dtype != torch.int8:
+        raise ValueError(f"gemm_w8a8: A8 must be int8 [M, {w.K}], got {tuple(A8.shape)} {A8.dtype}")
+    if out is None:
+        out = torch.empty((M, w.N), dtype=out_dtype, device=A8.device)
+    _need(out, "out")
+    if acc is not None:
+        _need(acc, "acc")
+    L.check("g4b_gemm_w8a8", L.load().g4b_gemm_w8a8(
+        _ptr(A8), _ptr(w.w8), _ptr(sa), _ptr(w.sw8), _ptr(out), _DT[out.dtype], _ptr(acc), M, w.N, w.K,
+        _stream_handle(stream, A8.device)))
+    return out
+
+
+def gemm_w4a8(A8: torch.Tensor, sa: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None,
+              out_dtype: torch.dtype = torch.float16, acc: Optional[torch.Tensor] = None,
+              stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """W4A8 prefill GEMM: the int4 weights requantised in the kernel to int8
+    against the per-column scale (ratio16 = f16(scale / s_w)), then as gemm_w8a8."""
+    _need(A8, "A8")
+    _need(sa, "sa")
+    if w.ratio16 is None or w.sw8 is None:
+        raise ValueError("gemm_w4a8: weight has no W4A8 ratio (to_device(..., w4a8=True))")
+    M, K = A8.shape
+    if K != w.K or A8.dtype != torch.int8:
+        raise ValueError(f"gemm_w4a8: A8 must be int8 [M, {w.K}], got {tuple(A8.shape)} {A8.dtype}")
+    if out is None:
+        out = torch.empty((M, w.N), dtype=out_dtype, device=A8.device)
+    _need(out, "out")
+    if acc is not None:
+        _need(acc, "acc")
+    L.check("g4b_gemm_w4a8", L.load().g4b_gemm_w4a8(
+        _ptr(A8), _ptr(w.wp), _ptr(w.ratio16), _ptr(sa), _ptr(w.sw8), _ptr(out), _DT[out.dtype], _ptr(acc),
+        M, w.N, w.K, _stream_handle(stream, A8.device)))
     return out
 
 

@@ -228,6 +228,29 @@ G4B_API int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const ui
                         void* Y, int y_dtype, int M, int N, int K,
                         void* workspace, size_t ws_bytes, g4b_stream_t stream);
 
+/* W8A8 prefill GEMM (PREFILL_I8), vk/coopgemm_w8a8.comp:18-37, dispatched by
+ * gmm() after cast_i8 (src/vk_engine.py:391-397):
+ *     C[m, n] = sum_k A8[m, k] * W8[k, n]                 (exact int32)
+ *     Y[m, n] = f16((float(C) * sa[m]) * f32(sw_f16[n]))
+ *   A8       [M, K] int8 and sa [M] f32: g4b_cast_i8's outputs
+ *   W8       [K, N] int8 row-major and sw_f16 [N]: quant()'s prefill weights
+ *            (src/vk_engine.py:152-157) -- used as they are, no repacking
+ *   Y        [M, N] f16 or f32 (y_dtype; f32 skips the final f16 rounding)
+ *   C_debug  nullable [M, N] int32: the raw accumulators, for exact checks
+ * M >= 1, N % 16 == 0, K % 32 == 0. */
+G4B_API int g4b_gemm_w8a8(const int8_t* A8, const int8_t* W8, const float* sa, const uint16_t* sw_f16,
+                          void* Y, int y_dtype, int32_t* C_debug, int M, int N, int K, g4b_stream_t stream);
+
+/* W4A8 prefill GEMM, vk/coopgemm_w4a8.comp:21-50: the int4 weights are
+ * requantised in the kernel against a per-column scale,
+ *     W8[k, n] = clamp(round_half_even((q[k, n] - 8) * f32(ratio_f16[k/32, n])), -127, 127)
+ * and then multiplied as g4b_gemm_w8a8 does.  ratio_f16 [K/32, N] is
+ * f16(scale / s_w) (benchmarks/coopgemm_w4a8.py:84; g4b_quant_w8a8 makes it).
+ * M >= 1, N % 32 == 0, K % 32 == 0. */
+G4B_API int g4b_gemm_w4a8(const int8_t* A8, const uint32_t* wp, const uint16_t* ratio_f16, const float* sa,
+                          const uint16_t* sw_f16, void* Y, int y_dtype, int32_t* C_debug,
+                          int M, int N, int K, g4b_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -100,3 +100,20 @@ def test_gemm_i4_rejects_bad_shapes():
     st = lib.g4b_gemm_i4(X.float().data_ptr(), 0, wp.data_ptr(), sc.data_ptr(), Y.data_ptr(), 1, 4, 128, 64, None,
                          0, torch.cuda.current_stream().cuda_stream)
     assert st == L.G4B_E_WORKSPACE
+
+
+def test_gemm_f32_staging_does_not_disturb_gemv():
+    """An f32-input W4A16 GEMM stages X as f16 in scratch; a GEMV queued after
+    it on the same stream must still find its own workspace counters at zero."""
+    M, N, K = 256, 256, 256
+    _, dw = _dw(N, K, seed=12)
+    X = torch.from_numpy(activations(M, K, seed=13)).to(DEV)          # f32: uses the staging buffer
+    ops.gemm_i4(X, dw, out_dtype=torch.float32)
+    Ng, Kg = 15360, 3840
+    pw, dwg = _dw(Ng, Kg, seed=14)
+    x = activations(1, Kg, seed=15)[0]
+    y = ops.gemv_i4(torch.from_numpy(x).to(DEV), dwg, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+    ref = O.gemv(x, pw.wp, pw.scales.view(np.uint16), 0, 1.0, Ng, Kg, pw.split)
+    assert_close(y.cpu().numpy(), ref, "gemv after an f32 gemm_i4")
