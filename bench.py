@@ -98,8 +98,15 @@ class GraphEvents:
 
 # ----------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed
+    region.  NVML is read from a background thread every ~2 ms, so that even a
+    timed region of a few milliseconds gets samples; without NVML, nvidia-smi
+    polls every 200 ms.  Reading clocks changes no GPU setting."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -108,8 +115,36 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.path = None
+        self.thread = None
+        self.rows = []
+        self.stop_flag = False
 
     def start(self):
+        import threading
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[self.index]) if vis else self.index
+            h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            masks = [(name, getattr(pynvml, attr)) for name, attr in self.REASONS]
+
+            def run():
+                while not self.stop_flag:
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.rows.append((sm, mx, [n for n, m in masks if r & m]))
+                    except Exception:
+                        pass
+                    time.sleep(0.002)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.thread = None
         try:
             self.path = f"/tmp/g4b_clocks_{os.getpid()}.csv"
             self.proc = subprocess.Popen(
@@ -119,6 +154,15 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=5)
+            if not self.rows:
+                return None
+            sm = [r[0] for r in self.rows]
+            reasons = sorted({n for r in self.rows for n in r[2]})
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[1] for r in self.rows),
+                    "reasons": reasons, "samples": len(self.rows), "source": "nvml"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -142,7 +186,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi"}
 
 
 # ------------------------------------------------------------- model setup
@@ -188,9 +232,14 @@ def main():
     ap.add_argument("--workload", default="stream", choices=["stream", "gemv"] + list(GEMM_WORKLOADS),
                     help="stream: configs[1] decode weight stream (default); gemv: configs[0] single GEMV; "
                          "gemm_i4 / gemm_i4_down: configs[2] W4A16 prefill GEMM; w8a8 / w4a8: configs[3]")
+    ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "replicas"],
+                    help="N > 1: tp (default) shards the stream's output columns / input rows over the GPUs "
+                         "with NCCL all-reduces per layer; replicas streams a full copy per GPU")
     args = ap.parse_args()
     if args.workload in GEMM_WORKLOADS:
         return run_gemm(args)
+    if args.workload == "stream" and int(os.environ.get("WORLD_SIZE", "1")) > 1 and args.parallel != "replicas":
+        return run_tp(args)
     fp8 = args.scales == "fp8"
     metric = "int4 GEMV HBM GB/s (decode weight stream, 48 layers + lm_head, batch 1)"
 
@@ -331,7 +380,7 @@ def main():
         peak_src = "of fallback"
     roofline = {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(kern_gbs / peak, 4), "traffic": None, "peak_source": peak_src,
-                "kernel": "gemv_i4_kernel", "launches_timed": args.steps * len(model),
+                "kernel": "gemv_tc_kernel", "launches_timed": args.steps * len(model),
                 "avg_launch_us": round(kern_ms * 1e3 / (args.steps * len(model)), 3),
                 "per_shape_gbs": {k: round(v[2] * v[1] / (v[0] / 1e3) / 1e9, 1) for k, v in per_shape.items()},
                 "graph_vs_kernels": round(ms_step / (kern_ms / args.steps), 4)}
@@ -596,6 +645,176 @@ def run_gemm(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------------ tensor parallel
+def run_tp(args):
+    """the 48-layer stream sharded over the ranks (g4b.tp): q/k/v/
+    gate/up/lm_head by output columns, o/down by input rows, two NCCL
+    all-reduces per layer and an all-gather of the logits.  One step = one
+    token, captured as one CUDA graph per rank (collectives included).
+    value = the full model's weight bytes / the step's device time (max over
+    ranks): aggregate weight-stream GB/s, strong scaling."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from g4b import _lib as L
+    from g4b import ops, tp
+    from g4b import quant_gpu as qz
+
+    fp8 = args.scales == "fp8"
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    L.load()
+    why = tp.validate_world(HIDDEN, NQ, NKV, FFN, VOCAB, world)
+    if why:
+        raise SystemExit(f"bench: tensor parallel over {world} GPUs impossible: {why}")
+    kinds = dict(tp.LAYER_KINDS)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    full_bytes = 0
+    my_bytes = 0
+
+    def shard(N, K, kind):
+        nonlocal full_bytes, my_bytes
+        W = torch.randn((N, K), generator=gen, device=device).mul_(0.02)   # same full W on every rank
+        if kind == "col":
+            n0, n1 = tp.split_range(N, world, rank, tp.COL_ALIGN)
+            Ws = W[n0:n1].contiguous()
+        else:
+            k0, k1 = tp.split_range(K, world, rank, tp.ROW_ALIGN)
+            Ws = W[:, k0:k1].contiguous()
+        del W
+        full_bytes += weight_bytes(N, K, fp8)
+        w = qz.quant_device(Ws, pf=False, fp8=fp8, prefill_i8=False)
+        my_bytes += weight_bytes(w.N, w.K, fp8)
+        return w
+
+    layers = []
+    for _ in range(args.layers):
+        d = {n: shard(N, K, kinds[n]) for (n, N, K) in LAYER_SHAPES}
+        layers.append(tp.TPLayer(**d))
+    lm = shard(VOCAB, HIDDEN, "col")
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device)
+    ws = torch.zeros(max(ops.gemv_workspace_bytes(1, w.N, w.K, 0) for Lr in layers for w in vars(Lr).values())
+                     + ops.gemv_workspace_bytes(1, lm.N, lm.K, 0) + 256, dtype=torch.uint8, device=device)
+    launches = [0]
+
+    def gemv(x, w, out):
+        ops.gemv_i4(x, w, out=out, stream=stream, workspace=ws, pdl=True)
+        launches[0] += 1
+
+    dec = tp.TPDecoder(layers=layers, lm_head=lm, gemv=gemv, all_reduce=lambda t: dist.all_reduce(t),
+                       all_gather=lambda out, t: dist.all_gather_into_tensor(out, t),
+                       new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=device),
+                       hidden=HIDDEN, vocab=VOCAB, world=world)
+    x = torch.randn((HIDDEN,), generator=gen, device=device)
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            dec.step(x)
+    stream.synchronize()
+    launches[0] = 0
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        dec.step(x)
+    per_step = launches[0]
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    t = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item()) / args.steps
+    value = full_bytes / (ms_step / 1e3) / 1e9
+
+    # kernels only: the same GEMV chain without the collectives, for the roofline
+    graph_k = torch.cuda.CUDAGraph()
+    dec_k = tp.TPDecoder(layers=layers, lm_head=lm, gemv=gemv, all_reduce=lambda t: None,
+                         all_gather=lambda out, t: None,
+                         new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=device),
+                         hidden=HIDDEN, vocab=VOCAB, world=world)
+    with torch.cuda.stream(stream):
+        dec_k.step(x)
+    with torch.cuda.graph(graph_k, stream=stream):
+        dec_k.step(x)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph_k.replay()
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph_k.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_kern = float(t.item()) / args.steps
+    mb = torch.tensor([float(my_bytes)], device=device, dtype=torch.float64)
+    dist.all_reduce(mb, op=dist.ReduceOp.MAX)
+    peak, src = 6650.0, "of fallback"
+    try:
+        peak, src = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["hbm_gbs"]), "of measured"
+    except Exception:
+        pass
+    per_gpu_kern = float(mb.item()) / (ms_kern / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(per_gpu_kern, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(per_gpu_kern / peak, 4), "traffic": None, "peak_source": src,
+                "kernel": "gemv_tc_kernel (per GPU, collectives removed)",
+                "kernels_only_aggregate_gbs": round(full_bytes / (ms_kern / 1e3) / 1e9, 1)}
+
+    # e2e: hidden state in from pinned host memory, gathered logits back, every step
+    xh = x.cpu().pin_memory()
+    lh = torch.empty(dec.bufs["logits"].shape, dtype=torch.float32).pin_memory()
+    dist.barrier()
+    with torch.cuda.stream(stream):
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            x.copy_(xh, non_blocking=True)
+            graph.replay()
+            lh.copy_(dec.bufs["logits"], non_blocking=True)
+            stream.synchronize()
+        e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e = full_bytes * args.steps / float(t.item()) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "int4 GEMV HBM GB/s (decode weight stream, 48 layers + lm_head, batch 1)",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 x f32 -> f32 acc", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) hidden state)",
+            "config": {"workload": "configs[4]: the configs[1] stream tensor-parallel over the GPUs",
+                       "scales": args.scales, "layers": args.layers, "parallelism": f"tp{world}",
+                       "sharding": "q/k/v/gate/up/lm_head by output columns, o/down by input rows; 2 NCCL "
+                                   "all-reduces per layer + logits all-gather, inside one CUDA graph",
+                       "l2": "working set per GPU > 126 MB L2, no flush needed"},
+            "roofline": roofline, "cpu_baseline": None,
+            "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": HIDDEN * 4,
+                    "d2h_bytes_per_step": VOCAB * 4},
+            "gpu_launches": per_step * args.steps, "clocks": clk, "bytes_per_step": full_bytes,
+            "bytes_per_gpu_max": int(mb.item()), "ms_per_step_kernels_only": round(ms_kern, 4)}), flush=True)
+    del graph, graph_k
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def run_reference_arm(args, metric, config, rank, world, fp8):

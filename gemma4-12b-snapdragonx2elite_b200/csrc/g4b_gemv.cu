@@ -30,7 +30,7 @@
 #include <mutex>
 #include <utility>
 
-#include "g4b_common.cuh"
+#include "g4b_tcgen05.cuh"
 
 namespace g4b {
 
@@ -138,7 +138,7 @@ __device__ __forceinline__ void load_stage(Stage<XF32, SFMT, NT>& st, const Gemv
                                            int word0, int col0, int nvalid, int g) {
     const int nb8 = a.N >> 3;
     const int row0 = b * 32 + 8 * q;
-    #pragma unroll
+#pragma unroll
     for (int i = 0; i < 8; i++) {
         const uint32_t* p = a.wp + (size_t)(row0 + i) * nb8 + word0;
         if constexpr (WIDE) {
@@ -161,7 +161,7 @@ __device__ __forceinline__ void load_stage(Stage<XF32, SFMT, NT>& st, const Gemv
             st.s.v[i] = (nvalid * 8 > i * 16) ? ld_stream_v4(sp + 16 * i) : make_uint4(0, 0, 0, 0);
     }
     // activations: thread supplies B column g of each token tile t
-    #pragma unroll
+#pragma unroll
     for (int t = 0; t < NT; t++) {
         const int tok = 4 * t + (g >> 1);
         const bool live = tok < a.M && (XF32 || (g & 1) == 0);
@@ -190,7 +190,7 @@ template <bool XF32, int SFMT, int NT>
 __device__ __forceinline__ void compute_stage(const Stage<XF32, SFMT, NT>& st, float (&acc)[NT][16][2], int g) {
     // B fragments: b[t][h][0] = rows (4h, 4h+1), b[t][h][1] = rows (4h+2, 4h+3)
     uint32_t bf[NT][2][2];
-    #pragma unroll
+#pragma unroll
     for (int t = 0; t < NT; t++) {
         if constexpr (XF32) {
             const bool lo = (g & 1) != 0;
@@ -206,7 +206,7 @@ __device__ __forceinline__ void compute_stage(const Stage<XF32, SFMT, NT>& st, f
             bf[t][1][1] = st.x.v[t].w;
         }
     }
-    #pragma unroll
+#pragma unroll
     for (int u = 0; u < 4; u++) {
         // scales of columns 8u..8u+7 as f32
         float sc[8];
@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(kGemvThreads, NT == 1 ? 3 : 2) gemv_i4_kernel(
     const int b_end = min(a.nblk, b_begin + a.bps);
 
     float acc[NT][16][2];
-    #pragma unroll
+#pragma unroll
     for (int t = 0; t < NT; t++)
         #pragma unroll
         for (int i = 0; i < 16; i++) acc[t][i][0] = acc[t][i][1] = 0.f;
@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(kGemvThreads, NT == 1 ? 3 : 2) gemv_i4_kernel(
     // ---- CTA reduction over the 4 warps (padded rows: conflict-free stores)
     __shared__ float red[kGemvWarps][NT * 4][8][33];
     __shared__ unsigned s_last;
-    #pragma unroll
+#pragma unroll
     for (int t = 0; t < NT; t++) {
         #pragma unroll
         for (int u = 0; u < 4; u++)
@@ -1036,6 +1036,483 @@ static int dispatch_m1(const M1Args& a, const M1Plan& p, const uint32_t* wp, con
     return yf32 ? launch_m1<false, G4B_SCALE_E4M3, true>(a, p, wp, sc, s) : launch_m1<false, G4B_SCALE_E4M3, false>(a, p, wp, sc, s);
 }
 
+// ------------------------------------------------------- M = 1 on tcgen05
+// gemv_tc_kernel: the decode GEMV (M = 1) with the dot products on the
+// tcgen05 tensor core, so that no SM pipe but HBM limits it.
+//
+//  * item = 64 rows (two scale blocks) x 256 columns of packed words (8 KB);
+//    a CTA walks a contiguous, balanced range of items, tile-major, and the
+//    split-K partials of a tile shared by several CTAs are reduced by the last
+//    one to arrive, in CTA order (deterministic), as in gemv_i4_m1_kernel.
+//  * dequantisation is one shift and one AND per 32-bit word, no nibble
+//    gather: TMEM lane 4g+p holds, for every row k, the f16 pair
+//    (q[k][8g+p], q[k][8g+p+4]) as exact subnormals (q * 2^-24 or q * 2^-20,
+//    nibble positions p even / odd), i.e. the row's word shifted right by
+//    8*(p/2) and masked with 0x000F000F or 0x00F000F0.  Four warps write a
+//    64-row item as 64 TMEM columns: the A operand of eight M=128, N=16, K=16
+//    MMAs.
+//  * the B operand is x spread over a sparse [16 x 16] tile per 8 rows: the
+//    low element of a pair meets column 2b, the high element column 2b+1,
+//    where b is the row's scale block within the item; f32 x uses a second
+//    pair of columns for its f16 low part.  The accumulator therefore holds,
+//    per lane, one dot product per (block, column), and the block scales are
+//    applied in f32 afterwards: acc += s * (2^E * dot - 8 * sum(x over block)).
+//    The non-zero positions of the sparse tiles never change, so the tiles are
+//    zeroed once and each item only writes its x values.
+//  * footprint <= half an SM (256 threads, <= 106 KB shared memory, 256 TMEM
+//    columns), so with programmatic dependent launch the next GEMV's CTA
+//    lives beside this one and streams its weights while this one finishes.
+// Warps: 0 TMA producer, 1 MMA issuer (and TMEM owner), 2 x -> B tiles,
+// 3 idle, 4-7 dequant + epilogue (TMEM lane quarters 0-3).
+constexpr int kTcRows = 64;
+constexpr int kTcTN = 256;
+constexpr int kTcWBytes = kTcRows * (kTcTN / 2);  // 8 KB of packed words per item
+constexpr int kTcThreads = 256;
+constexpr int kTcDq0 = 4;                          // first dequant warp
+constexpr uint32_t kTcACol = 0;                    // 2 A stages x 64 columns
+constexpr uint32_t kTcDCol = 128;                  // 2 accumulators x 16 columns
+
+template <bool XF32, int SFMT>
+struct TcCfg {
+    static constexpr int kBTile = 16 * 16 * 2;                   // one [N=16 x K=16] f16 tile
+    static constexpr int kBBytes = (kTcRows / 8) * kBTile;       // 4 KB
+    static constexpr int kSBytes = 2 * kTcTN * (SFMT == G4B_SCALE_F16 ? 2 : 1);
+    static constexpr int kStageBytes = kTcWBytes + kBBytes + kSBytes;
+    static constexpr int kStages = 8;
+    static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 128;
+};
+
+struct TcArgs {
+    const void* x;
+    void* y;
+    float* partial;      // [G * maxseg, 256]
+    unsigned* counters;  // [ntiles]
+    float inv;
+    int N, K, noct, ntiles, G, maxseg;
+    long long total;
+};
+
+// byte offset of element (n, kk) in a K-major, unswizzled [16 x 16] f16 tile
+// (core matrices of 8 rows x 8 elements: K groups 128 B apart, row groups 256 B)
+__device__ __forceinline__ uint32_t btile_off(int n, int kk) {
+    return (uint32_t)((n >> 3) * 256 + (kk >> 3) * 128 + (n & 7) * 16 + (kk & 7) * 2);
+}
+
+template <bool XF32, int SFMT, bool YF32>
+__global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap wmap,
+                                                               const __grid_constant__ CUtensorMap smap) {
+    using Cfg = TcCfg<XF32, SFMT>;
+    constexpr int S = Cfg::kStages;
+    constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ uint64_t bars[4 * S + 9];
+    __shared__ float s_xb[S][2];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort;
+    __shared__ int s_issued;
+    __shared__ long long s_pending;
+    __shared__ unsigned s_last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    volatile int* abort_flag = &s_abort;
+    const uint32_t raw0 = smem_u32(smem_raw);
+    const uint32_t sm0 = (raw0 + 127u) & ~127u;
+    uint8_t* smem = smem_raw + (sm0 - raw0);
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };               // TMA landed (1 + tx)
+    auto bfull_bar = [&](int s) { return bar0 + 8u * (S + s); };        // B tiles + block sums written (1)
+    auto wempty_bar = [&](int s) { return bar0 + 8u * (2 * S + s); };   // words + scales consumed (4)
+    auto bempty_bar = [&](int s) { return bar0 + 8u * (3 * S + s); };   // MMAs done with the B tiles (commit)
+    auto afull_bar = [&](int i) { return bar0 + 8u * (4 * S + i); };    // A stage written (4)
+    auto aempty_bar = [&](int i) { return bar0 + 8u * (4 * S + 2 + i); };  // MMAs done with the A stage
+    auto dfull_bar = [&](int i) { return bar0 + 8u * (4 * S + 4 + i); };   // accumulator ready
+    auto dempty_bar = [&](int i) { return bar0 + 8u * (4 * S + 6 + i); };  // accumulator read (4)
+    const uint32_t drain_bar = bar0 + 8u * (4 * S + 8);
+    const long long ibeg = (long long)blockIdx.x * a.total / a.G;
+    const long long iend = (long long)(blockIdx.x + 1) * a.total / a.G;
+    const int n_items = (int)(iend - ibeg);
+
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(bfull_bar(s), 1);
+            mbar_init(wempty_bar(s), 4);
+            mbar_init(bempty_bar(s), 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(afull_bar(i), 4);
+            mbar_init(aempty_bar(i), 1);
+            mbar_init(dfull_bar(i), 1);
+            mbar_init(dempty_bar(i), 4);
+        }
+        mbar_init(drain_bar, 1);
+        s_abort = 0;
+        s_issued = 0;
+        s_pending = -1;
+        fence_mbar_init();
+    }
+    // the sparse B tiles: zero once, only their fixed non-zero positions are rewritten
+    for (int s = 0; s < S; s++) {
+        uint4* b = reinterpret_cast<uint4*>(smem + (size_t)s * Cfg::kStageBytes + kTcWBytes);
+        for (int v = tid; v < Cfg::kBBytes / 16; v += kTcThreads) b[v] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    tc::fence_proxy_async_smem();
+    if (warp == 1) {
+        tc::tmem_alloc(smem_u32(&s_tmem), 256);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = s_tmem;
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        // ------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            prefetch_tensor_map(&wmap);
+            prefetch_tensor_map(&smap);
+            const uint64_t pol = l2_evict_first_policy();
+            int i = 0;
+            for (; i < n_items; i++) {
+                const int s = i % S;
+                if (i >= S && !mbar_wait(wempty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status)) break;
+                const long long it = ibeg + i;
+                const int t = (int)(it / a.noct), o = (int)(it % a.noct);
+                const uint32_t st = sm0 + (uint32_t)(s * Cfg::kStageBytes);
+                mbar_arrive_expect_tx(full_bar(s), kTcWBytes + Cfg::kSBytes);
+                tma_load_2d(st, &wmap, t * (kTcTN / 8), o * kTcRows, full_bar(s), pol);
+                tma_load_2d(st + kTcWBytes + Cfg::kBBytes, &smap, t * (kTcTN * ssz / 8), o * 2, full_bar(s), pol);
+            }
+            s_issued = i;
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc(1, 0, 0, 0, 0, 16, 128);
+            bool ok = true;
+            for (int i = 0; ok && i < n_items; i++) {
+                const int s = i % S, ab = i & 1;
+                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+                if (!mbar_wait(dempty_bar(ab), ph ^ 1u, abort_flag, &g_gemv_status) ||
+                    !mbar_wait(afull_bar(ab), ph, abort_flag, &g_gemv_status) ||
+                    !mbar_wait(bfull_bar(s), (uint32_t)(i / S) & 1u, abort_flag, &g_gemv_status)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after();
+                const uint32_t bst = sm0 + (uint32_t)(s * Cfg::kStageBytes + kTcWBytes);
+#pragma unroll
+                for (int j = 0; j < kTcRows / 8; j++)
+                    tc::mma_f16_ts(tmem + kTcDCol + 16u * ab, tmem + kTcACol + 64u * ab + 8u * j,
+                                   tc::sdesc_noswz(bst + j * Cfg::kBTile, 128, 256), idesc, j != 0);
+                tc::commit(aempty_bar(ab));
+                tc::commit(bempty_bar(s));
+                tc::commit(dfull_bar(ab));
+            }
+            tc::commit(drain_bar);
+            mbar_wait_drain(drain_bar, 0, &g_gemv_status);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------- x -> sparse B tiles
+        pdl_wait();
+        for (int i = 0; i < n_items; i++) {
+            const int s = i % S;
+            const bool good = i < S || mbar_wait(bempty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status);
+            if (!__all_sync(0xffffffffu, good)) break;  // warp-uniform exit
+            const int o = (int)((ibeg + i) % a.noct);
+            uint8_t* bt = smem + (size_t)s * Cfg::kStageBytes + kTcWBytes;
+            float xs[2];
+#pragma unroll
+            for (int blk = 0; blk < 2; blk++) {
+                const int r = 32 * blk + lane;  // row within the item
+                const int k = o * kTcRows + r;
+                uint8_t* tile = bt + (r >> 3) * Cfg::kBTile;
+                const int kk = 2 * (r & 7);
+                float xv;
+                if constexpr (XF32) {
+                    xv = __ldg(reinterpret_cast<const float*>(a.x) + k);
+                    const __half hi = __float2half_rn(xv);
+                    const __half lo = __float2half_rn(xv - __half2float(hi));
+                    *reinterpret_cast<__half*>(tile + btile_off(4 * blk + 0, kk)) = hi;
+                    *reinterpret_cast<__half*>(tile + btile_off(4 * blk + 1, kk + 1)) = hi;
+                    *reinterpret_cast<__half*>(tile + btile_off(4 * blk + 2, kk)) = lo;
+                    *reinterpret_cast<__half*>(tile + btile_off(4 * blk + 3, kk + 1)) = lo;
+                } else {
+                    const __half h = __ldg(reinterpret_cast<const __half*>(a.x) + k);
+                    xv = __half2float(h);
+                    *reinterpret_cast<__half*>(tile + btile_off(2 * blk + 0, kk)) = h;
+                    *reinterpret_cast<__half*>(tile + btile_off(2 * blk + 1, kk + 1)) = h;
+                }
+#pragma unroll
+                for (int m = 16; m >= 1; m >>= 1) xv += __shfl_xor_sync(0xffffffffu, xv, m);
+                xs[blk] = xv;
+            }
+            if (lane == 0) {
+                s_xb[s][0] = xs[0];
+                s_xb[s][1] = xs[1];
+            }
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bfull_bar(s));
+        }
+    } else if (warp >= kTcDq0) {
+        // ------------------------------------------------------- dequant + epilogue
+        pdl_wait();
+        const int qd = warp & 3;
+        const int lam = 32 * qd + lane;                 // TMEM lane
+        const int g = lam >> 2, p = lam & 3;
+        const int c0 = 8 * g + p, c1 = c0 + 4;          // this lane's two columns of the tile
+        const uint32_t sh = (uint32_t)(p >> 1) * 8u;
+        const uint32_t mask = (p & 1) ? 0x00F000F0u : 0x000F000Fu;
+        const float E = (p & 1) ? 1048576.0f : 16777216.0f;  // 2^20 / 2^24
+        const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
+        const float inv = SFMT == G4B_SCALE_E4M3 ? a.inv : 1.0f;
+        const long long t_first = ibeg / a.noct;
+        const long long t_last = n_items > 0 ? (iend - 1) / a.noct : t_first - 1;
+        const int dq = tid - kTcDq0 * 32;               // 0..127 among the dequant threads
+
+        auto write_y = [&](long long t, int col, float v) {
+            const int n = (int)t * kTcTN + col;
+            if (n < a.N) {
+                if (YF32) reinterpret_cast<float*>(a.y)[n] = v * inv;
+                else reinterpret_cast<__half*>(a.y)[n] = __float2half_rn(v * inv);
+            }
+        };
+        auto reduce_tile = [&](long long t) {
+            const long long c_first = ((t * a.noct + 1) * a.G - 1) / a.total;
+            const long long c_last = (((t + 1) * a.noct) * a.G - 1) / a.total;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int col = h ? c1 : c0;
+                float v = 0.f;
+                for (long long cc = c_first; cc <= c_last; cc++) {
+                    const long long cb = cc * a.total / a.G;
+                    const long long sl = cc * a.maxseg + (t - cb / a.noct);
+                    v += __ldcg(&a.partial[(size_t)sl * kTcTN + col]);
+                }
+                write_y(t, col, v);
+            }
+            if (dq == 0) a.counters[t] = 0u;  // ready for the next call
+        };
+        auto flush_tile = [&](long long t, float acc0, float acc1) {
+            const long long c_first = ((t * a.noct + 1) * a.G - 1) / a.total;
+            const long long c_last = (((t + 1) * a.noct) * a.G - 1) / a.total;
+            const bool ok = !*abort_flag;
+            if (c_first == c_last) {
+                if (ok) {
+                    write_y(t, c0, acc0);
+                    write_y(t, c1, acc1);
+                }
+                return;
+            }
+            const long long slot = (long long)blockIdx.x * a.maxseg + (t - t_first);
+            if (ok) {
+                a.partial[(size_t)slot * kTcTN + c0] = acc0;
+                a.partial[(size_t)slot * kTcTN + c1] = acc1;
+            }
+            named_bar_sync(1, 128);
+            if (t < t_last) {
+                if (dq == 0 && ok) {
+                    __threadfence();
+                    if (atomicAdd(&a.counters[t], 1u) == (unsigned)(c_last - c_first)) s_pending = t;
+                }
+            } else {
+                if (dq == 0) {
+                    unsigned last = 0;
+                    if (ok) {
+                        __threadfence();
+                        last = atomicAdd(&a.counters[t], 1u) == (unsigned)(c_last - c_first) ? 1u : 0u;
+                    }
+                    s_last = last;
+                }
+                named_bar_sync(1, 128);
+                if (s_last) {
+                    __threadfence();
+                    reduce_tile(t);
+                }
+            }
+        };
+
+        float acc0 = 0.f, acc1 = 0.f;
+        // scales and block sums of the item whose epilogue is still pending
+        float ps00 = 0.f, ps01 = 0.f, ps10 = 0.f, ps11 = 0.f, px0 = 0.f, px1 = 0.f;
+        auto epilogue = [&](int i) -> bool {
+            const int ab = i & 1;
+            const bool good = mbar_wait(dfull_bar(ab), (uint32_t)(i >> 1) & 1u, abort_flag, &g_gemv_status);
+            if (!__all_sync(0xffffffffu, good)) return false;
+            tc::fence_after();
+            uint32_t d[8];
+            tc::ld_32x32b_x8(tmem + lane_addr + kTcDCol + 16u * ab, d);
+            tc::wait_ld();
+            float d00, d01, d10, d11;  // d<block><column>
+            if constexpr (XF32) {
+                d00 = __uint_as_float(d[0]) + __uint_as_float(d[2]);
+                d01 = __uint_as_float(d[1]) + __uint_as_float(d[3]);
+                d10 = __uint_as_float(d[4]) + __uint_as_float(d[6]);
+                d11 = __uint_as_float(d[5]) + __uint_as_float(d[7]);
+            } else {
+                d00 = __uint_as_float(d[0]);
+                d01 = __uint_as_float(d[1]);
+                d10 = __uint_as_float(d[2]);
+                d11 = __uint_as_float(d[3]);
+            }
+            acc0 = fmaf(ps00, fmaf(d00, E, -8.0f * px0), acc0);
+            acc1 = fmaf(ps01, fmaf(d01, E, -8.0f * px0), acc1);
+            acc0 = fmaf(ps10, fmaf(d10, E, -8.0f * px1), acc0);
+            acc1 = fmaf(ps11, fmaf(d11, E, -8.0f * px1), acc1);
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(dempty_bar(ab));
+            return true;
+        };
+
+        // Every dequant warp runs the same sequence of items, epilogues and tile
+        // flushes (with their named barriers) even after a wait has given up:
+        // `ok` only turns the work off, never the control flow.
+        bool ok = true;
+        for (int i = 0; i < n_items; i++) {
+            const int s = i % S, ab = i & 1;
+            const uint32_t ps = (uint32_t)(i / S) & 1u;
+            bool good = ok && mbar_wait(full_bar(s), ps, abort_flag, &g_gemv_status) &&
+                        mbar_wait(bfull_bar(s), ps, abort_flag, &g_gemv_status) &&
+                        (i < 2 || mbar_wait(aempty_bar(ab), ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_flag, &g_gemv_status));
+            ok = __all_sync(0xffffffffu, good);
+            float s00 = 0.f, s01 = 0.f, s10 = 0.f, s11 = 0.f, x0 = 0.f, x1 = 0.f;
+            if (ok) {
+                tc::fence_after();
+                const uint8_t* st = smem + (size_t)s * Cfg::kStageBytes;
+                const uint8_t* sc = st + kTcWBytes + Cfg::kBBytes;
+                if constexpr (SFMT == G4B_SCALE_F16) {
+                    const __half* sh16 = reinterpret_cast<const __half*>(sc);
+                    s00 = __half2float(sh16[c0]);
+                    s01 = __half2float(sh16[c1]);
+                    s10 = __half2float(sh16[kTcTN + c0]);
+                    s11 = __half2float(sh16[kTcTN + c1]);
+                } else {
+                    s00 = e4m3_decode_ref(sc[c0]);
+                    s01 = e4m3_decode_ref(sc[c1]);
+                    s10 = e4m3_decode_ref(sc[kTcTN + c0]);
+                    s11 = e4m3_decode_ref(sc[kTcTN + c1]);
+                }
+                x0 = s_xb[s][0];
+                x1 = s_xb[s][1];
+                const uint32_t* wr = reinterpret_cast<const uint32_t*>(st) + g;
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    uint32_t v[32];
+#pragma unroll
+                    for (int r = 0; r < 32; r++) v[r] = (wr[(32 * hh + r) * (kTcTN / 8)] >> sh) & mask;
+                    tc::st_32x32b_x32(tmem + lane_addr + kTcACol + 64u * ab + 32u * hh, v);
+                }
+                tc::wait_st();
+                tc::fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(afull_bar(ab));
+                    mbar_arrive(wempty_bar(s));
+                }
+            }
+            // epilogue of the previous item (its MMAs ran while this item was dequantised)
+            if (i > 0) {
+                if (ok) ok = epilogue(i - 1);
+                const long long tp = (ibeg + i - 1) / a.noct;
+                if (tp != (ibeg + i) / a.noct) {
+                    flush_tile(tp, acc0, acc1);
+                    acc0 = acc1 = 0.f;
+                }
+            }
+            ps00 = s00; ps01 = s01; ps10 = s10; ps11 = s11; px0 = x0; px1 = x1;
+        }
+        if (n_items > 0) {
+            if (ok) ok = epilogue(n_items - 1);
+            flush_tile(t_last, acc0, acc1);
+        }
+        // the deferred reduction of an earlier tile this CTA was the last to finish
+        named_bar_sync(1, 128);
+        if (s_pending >= 0 && !*abort_flag) {
+            __threadfence();
+            reduce_tile(s_pending);
+        }
+    }
+
+    __syncwarp();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (tid == 0 && *abort_flag) {
+        const int issued = s_issued;
+        for (int i = max(0, issued - S); i < issued; i++) mbar_wait_drain(full_bar(i % S), (i / S) & 1, &g_gemv_status);
+    }
+    __syncthreads();
+    if (warp == 1) tc::tmem_dealloc(tmem, 256);
+}
+
+struct TcPlan {
+    int ntiles, noct, G, maxseg;
+    long long total;
+    size_t smem, ws_bytes;
+};
+
+static bool tc_ok(int M, int N, int K, int split) { return M == 1 && split == 0 && N % 32 == 0 && K % kTcRows == 0; }
+
+static TcPlan tc_plan(int N, int K, int sms, bool xf32, int sfmt) {
+    TcPlan p{};
+    p.noct = K / kTcRows;
+    p.ntiles = (N + kTcTN - 1) / kTcTN;
+    p.total = (long long)p.ntiles * p.noct;
+    p.G = (int)std::max<long long>(1, std::min<long long>(std::max(sms, 1), p.total));
+    const long long lmax = (p.total + p.G - 1) / p.G;
+    p.maxseg = (int)((lmax + p.noct - 1) / p.noct + 1);
+    p.smem = xf32 ? (sfmt == G4B_SCALE_F16 ? TcCfg<true, G4B_SCALE_F16>::kSmem : TcCfg<true, G4B_SCALE_E4M3>::kSmem)
+                  : (sfmt == G4B_SCALE_F16 ? TcCfg<false, G4B_SCALE_F16>::kSmem : TcCfg<false, G4B_SCALE_E4M3>::kSmem);
+    bool multi = false;
+    for (int c = 1; c < p.G && !multi; c++)
+        if (((long long)c * p.total / p.G) % p.noct) multi = true;
+    if (multi) p.ws_bytes = kGemvCounterBytes + (((size_t)p.G * p.maxseg * kTcTN * sizeof(float) + 255) & ~(size_t)255);
+    return p;
+}
+
+template <bool XF32, int SFMT, bool YF32>
+static int launch_tc(const TcArgs& a, const TcPlan& p, const uint32_t* wp, const void* scales, cudaStream_t s) {
+    CUtensorMap wmap, smap;
+    int st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, wp, (uint64_t)a.N / 8, (uint64_t)a.K,
+                           (uint64_t)a.N / 2, kTcTN / 8, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != G4B_OK) return st;
+    constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
+    st = tensor_map_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT64, scales, (uint64_t)a.N * ssz / 8, (uint64_t)a.K / 32,
+                       (uint64_t)a.N * ssz, kTcTN * ssz / 8, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != G4B_OK) return st;
+    auto kern = gemv_tc_kernel<XF32, SFMT, YF32>;
+    static int attr_set_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_set_mask & (1 << (dev & 31)))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)TcCfg<XF32, SFMT>::kSmem);
+        if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        attr_set_mask |= 1 << (dev & 31);
+    }
+    cudaError_t e = launch_k(kern, dim3(p.G), dim3(kTcThreads), TcCfg<XF32, SFMT>::kSmem, s, a, wmap, smap);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: launch: %s", cudaGetErrorString(e));
+    return G4B_OK;
+}
+
+static int dispatch_tc(const TcArgs& a, const TcPlan& p, const uint32_t* wp, const void* sc, bool xf32, int sfmt,
+                       bool yf32, cudaStream_t s) {
+    if (xf32) {
+        if (sfmt == G4B_SCALE_F16)
+            return yf32 ? launch_tc<true, G4B_SCALE_F16, true>(a, p, wp, sc, s)
+                        : launch_tc<true, G4B_SCALE_F16, false>(a, p, wp, sc, s);
+        return yf32 ? launch_tc<true, G4B_SCALE_E4M3, true>(a, p, wp, sc, s)
+                    : launch_tc<true, G4B_SCALE_E4M3, false>(a, p, wp, sc, s);
+    }
+    if (sfmt == G4B_SCALE_F16)
+        return yf32 ? launch_tc<false, G4B_SCALE_F16, true>(a, p, wp, sc, s)
+                    : launch_tc<false, G4B_SCALE_F16, false>(a, p, wp, sc, s);
+    return yf32 ? launch_tc<false, G4B_SCALE_E4M3, true>(a, p, wp, sc, s)
+                : launch_tc<false, G4B_SCALE_E4M3, false>(a, p, wp, sc, s);
+}
+
 unsigned read_status_gemv() {
     unsigned v = 0, z = 0;
     if (cudaMemcpyFromSymbol(&v, g_gemv_status, sizeof(v)) != cudaSuccess) return 0xffffffffu;
@@ -1291,7 +1768,7 @@ size_t g4b_gemv_workspace_bytes(int M, int N, int K, int split) {
     if (check_device(&sms) != G4B_OK) sms = 148;
     clear_error();
     // the activation and scale formats only change the shared-memory layout, not the workspace
-    if (m1_ok(M, N, K, split)) return m1_plan(N, K, sms, true, G4B_SCALE_F16).ws_bytes;
+    if (tc_ok(M, N, K, split)) return tc_plan(N, K, sms, true, G4B_SCALE_F16).ws_bytes;
     if (stream_ok(N, K, split)) return stream_plan(M, N, K, split, sms, true, G4B_SCALE_F16).ws_bytes;
     return gemv_plan(M, N, K, split, sms).ws_bytes;
 }
@@ -1342,6 +1819,34 @@ static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, c
     if (st != G4B_OK) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const size_t xe = x_dtype == G4B_DT_F32 ? 4 : 2, ye = y_dtype == G4B_DT_F32 ? 4 : 2;
+    if (tc_ok(M, N, K, split)) {
+        const TcPlan p = tc_plan(N, K, sms, x_dtype == G4B_DT_F32, scale_fmt);
+        if (p.ws_bytes) {
+            G4B_REQUIRE(workspace != nullptr && ws_bytes >= p.ws_bytes, G4B_E_WORKSPACE,
+                        "gemv_i4: needs %zu bytes of workspace, got %zu", p.ws_bytes, workspace ? ws_bytes : 0);
+            G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "gemv_i4: workspace must be 16-byte aligned");
+            G4B_REQUIRE(p.ntiles <= kGemvMaxTiles, G4B_E_SHAPE, "gemv_i4: N=%d too large for a split-K call", N);
+        }
+        TcArgs a{};
+        a.x = x;
+        a.y = y;
+        a.inv = inv;
+        a.N = N;
+        a.K = K;
+        a.noct = p.noct;
+        a.ntiles = p.ntiles;
+        a.G = p.G;
+        a.maxseg = p.maxseg;
+        a.total = p.total;
+        if (p.ws_bytes) {
+            a.counters = (unsigned*)workspace;
+            a.partial = (float*)((char*)workspace + kGemvCounterBytes);
+        }
+        st = dispatch_tc(a, p, wp, scales, x_dtype == G4B_DT_F32, scale_fmt, y_dtype == G4B_DT_F32, s);
+        if (st != G4B_OK) return st;
+        count_launch();
+        return launch_status("gemv_i4");
+    }
     if (m1_ok(M, N, K, split)) {
         const M1Plan p = m1_plan(N, K, sms, x_dtype == G4B_DT_F32, scale_fmt);
         if (p.ws_bytes) {

@@ -34,7 +34,8 @@ def _oracle_y(pw, x32, split=None):
 
 
 @pytest.mark.parametrize("N,K", [(15360, 3840), (4096, 3840), (2048, 3840), (3840, 4096), (3840, 15360),
-                                 (256, 32), (272, 64), (48, 96), (1040, 1024)])
+                                 (256, 32), (272, 64), (48, 96), (1040, 1024),
+                                 (800, 576), (2080, 64), (32, 3840)])
 @pytest.mark.parametrize("fp8", [False, True])
 def test_gemv_matches_oracle(N, K, fp8):
     W, pw, dw = _packed(N, K, seed=N + K, fp8=fp8)
@@ -60,8 +61,15 @@ def test_gemv_f16_output_config1():
     torch.cuda.synchronize()
     out = y.float().cpu().numpy()
     assert_close(out, ref, "config1 f16 out")
-    # the f16 output is the f32 result rounded once: compare with the rounded oracle too
-    assert rel_err(out, ref.astype(np.float16).astype(np.float32)) < 2e-3
+    # The f16 output is the f32 result rounded once.  Against the exact product
+    # (f64, from the bit-exact f32 dequantisation) rounded to f16 it may differ by
+    # one f16 ulp plus f32 summation noise: at the 1e-3 x rms guard a 2e-6
+    # absolute f32 error (the oracle's own, summing 3840 products in order) is
+    # already 1.5e-3 of the denominator, so the bound is 3e-3.
+    Wd = ops.dequant_i4(dw, out_dtype=torch.float32).double()          # [K, N], exact (q - 8) * s
+    exact = (torch.from_numpy(x16).to(DEV).double() @ Wd).cpu().numpy()
+    assert rel_err(out, exact.astype(np.float16).astype(np.float32)) < 3e-3
+    assert rel_err(ref, exact) < 3e-3                                   # the oracle meets the same bound
 
 
 @pytest.mark.parametrize("M", [2, 3, 4, 5, 8, 13])
