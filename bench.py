@@ -232,6 +232,9 @@ def main():
     ap.add_argument("--workload", default="stream", choices=["stream", "gemv"] + list(GEMM_WORKLOADS),
                     help="stream: configs[1] decode weight stream (default); gemv: configs[0] single GEMV; "
                          "gemm_i4 / gemm_i4_down: configs[2] W4A16 prefill GEMM; w8a8 / w4a8: configs[3]")
+    ap.add_argument("--unfused", action="store_true",
+                    help="stream: launch all 337 GEMVs separately, each on its own x, instead of fusing "
+                         "q|k|v and gate|up (which read the same x in a decode step)")
     ap.add_argument("--parallel", default="auto", choices=["auto", "tp", "replicas"],
                     help="N > 1: tp (default) shards the stream's output columns / input rows over the GPUs "
                          "with NCCL all-reduces per layer; replicas streams a full copy per GPU")
@@ -284,25 +287,48 @@ def main():
         metric = "int4 GEMV HBM GB/s (W[15360, 3840], batch 1)"
     else:
         model = build_model(torch, ops, qz, device, fp8, args.layers)
-    shapes = [(name, w.N, w.K) for name, w in model]
-    step_bytes = sum(gemv_bytes(N, K, fp8) for _, N, K in shapes)
-    # per-GEMV activations (f16 N(0,1)) and outputs, resident in HBM
+    # launch groups: GEMVs that read the same x run as one fused launch (the
+    # engine's q/k/v on the normed hidden state, gate/up on the post-attention
+    # one); --unfused launches every GEMV on its own x
+    groups = []
+    if args.workload == "stream" and not args.unfused:
+        for li in range(args.layers):
+            b = 7 * li
+            groups += [[b, b + 1, b + 2], [b + 3], [b + 4, b + 5], [b + 6]]
+        groups.append([7 * args.layers])
+    else:
+        groups = [[i] for i in range(len(model))]
+    ws_list = [w for _, w in model]
+    if args.workload == "stream":
+        config["schedule"] = (f"{len(groups)} launches per token: q|k|v fused, o, gate|up fused, down per layer, "
+                              "then lm_head" if not args.unfused else f"{len(groups)} separate GEMVs per token")
+    step_bytes = (sum(weight_bytes(w.N, w.K, fp8) + 2 * w.N for w in ws_list)
+                  + sum(2 * ws_list[g[0]].K for g in groups))
+    # per-group activations (f16 N(0,1)) and per-GEMV outputs, resident in HBM
     gen = torch.Generator(device=device)
     gen.manual_seed(1 + rank)
-    xs = [torch.randn((w.K,), generator=gen, device=device).to(torch.float16) for _, w in model]
-    ys = [torch.empty((w.N,), device=device, dtype=torch.float16) for _, w in model]
+    xs = [torch.randn((ws_list[g[0]].K,), generator=gen, device=device).to(torch.float16) for g in groups]
+    ys = [torch.empty((w.N,), device=device, dtype=torch.float16) for w in ws_list]
     stream = torch.cuda.Stream(device)
     sh = int(stream.cuda_stream)
-    ws = torch.zeros(max(ops.gemv_workspace_bytes(1, w.N, w.K, 0) for _, w in model) + 256,
-                     dtype=torch.uint8, device=device)
+    need = 0
+    for g in groups:
+        ns = [ws_list[i].N for i in g]
+        need = max(need, ops.gemv_fused_workspace_bytes(ns, ws_list[g[0]].K) if len(g) > 1
+                   else ops.gemv_workspace_bytes(1, ns[0], ws_list[g[0]].K, 0))
+    ws = torch.zeros(need + 256, dtype=torch.uint8, device=device)
 
     def step(gev=None):
-        for i, ((_, w), x, y) in enumerate(zip(model, xs, ys)):
+        for gi, (g, x) in enumerate(zip(groups, xs)):
             if gev is not None:
-                gev.record(2 * i, sh)
-            ops.gemv_i4(x, w, out=y, stream=stream, workspace=ws, pdl=True)
+                gev.record(2 * gi, sh)
+            if len(g) == 1:
+                ops.gemv_i4(x, ws_list[g[0]], out=ys[g[0]], stream=stream, workspace=ws, pdl=True)
+            else:
+                ops.gemv_i4_fused(x, [ws_list[i] for i in g], outs=[ys[i] for i in g], stream=stream,
+                                  workspace=ws, pdl=True)
             if gev is not None:
-                gev.record(2 * i + 1, sh)
+                gev.record(2 * gi + 1, sh)
 
     # warm-up and graph capture (the reference records one command buffer per token)
     with torch.cuda.stream(stream):
@@ -312,7 +338,7 @@ def main():
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
-    gev = GraphEvents(len(model))
+    gev = GraphEvents(len(groups))
     graph_ev = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph_ev, stream=stream):
         step(gev)
@@ -348,7 +374,7 @@ def main():
     barrier()
     ms = e0.elapsed_time(e1)
     ms = max_over_ranks(ms)
-    launches_per_step = len(model)
+    launches_per_step = len(groups)
     ms_step = ms / args.steps
     value = world * step_bytes / (ms_step / 1e3) / 1e9
 
@@ -360,12 +386,14 @@ def main():
         for _ in range(args.steps):
             graph_ev.replay()
             stream.synchronize()
-            for i, (name, N, K) in enumerate(shapes):
-                d = gev.elapsed_ms(2 * i, 2 * i + 1)
+            for gi, g in enumerate(groups):
+                d = gev.elapsed_ms(2 * gi, 2 * gi + 1)
+                K = ws_list[g[0]].K
+                gb = sum(weight_bytes(ws_list[i].N, K, fp8) + 2 * ws_list[i].N for i in g) + 2 * K
                 kern_ms += d
-                kern_bytes += gemv_bytes(N, K, fp8)
-                key = f"{N}x{K}"
-                a = per_shape.setdefault(key, [0.0, 0, gemv_bytes(N, K, fp8)])
+                kern_bytes += gb
+                key = "+".join(str(ws_list[i].N) for i in g) + f"x{K}"
+                a = per_shape.setdefault(key, [0.0, 0, gb])
                 a[0] += d
                 a[1] += 1
     clk = clocks.stop()
@@ -380,8 +408,8 @@ def main():
         peak_src = "of fallback"
     roofline = {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(kern_gbs / peak, 4), "traffic": None, "peak_source": peak_src,
-                "kernel": "gemv_tc_kernel", "launches_timed": args.steps * len(model),
-                "avg_launch_us": round(kern_ms * 1e3 / (args.steps * len(model)), 3),
+                "kernel": "gemv_tc_kernel", "launches_timed": args.steps * len(groups),
+                "avg_launch_us": round(kern_ms * 1e3 / (args.steps * len(groups)), 3),
                 "per_shape_gbs": {k: round(v[2] * v[1] / (v[0] / 1e3) / 1e9, 1) for k, v in per_shape.items()},
                 "graph_vs_kernels": round(ms_step / (kern_ms / args.steps), 4)}
     tp = os.path.join(REPO, "profiles", "gemv_traffic.json")

@@ -1082,15 +1082,39 @@ struct TcCfg {
     static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 128;
 };
 
+// Up to three GEMVs that read the same x (the engine's q/k/v, or gate/up) run
+// as one launch: their column tiles are numbered one after another ("segments"),
+// and every per-tile decision (which weights to load, where y goes, which
+// e4m3 inverse scale applies) looks the segment up from the tile index.
+constexpr int kTcMaxSeg = 3;
+
+struct TcSeg {
+    void* y;
+    float inv;    // e4m3 2^-shift (1 for f16 scales)
+    int N;
+    int tile0;    // first tile of this segment in the launch's tile numbering
+};
+
 struct TcArgs {
     const void* x;
-    void* y;
     float* partial;      // [G * maxseg, 256]
     unsigned* counters;  // [ntiles]
-    float inv;
-    int N, K, noct, ntiles, G, maxseg;
+    TcSeg seg0, seg1, seg2;
+    int nseg, K, noct, ntiles, G, maxseg;
     long long total;
 };
+
+struct TcMaps {
+    CUtensorMap w[kTcMaxSeg];
+    CUtensorMap s[kTcMaxSeg];
+};
+
+__device__ __forceinline__ int tc_seg_of(const TcArgs& a, long long t) {
+    return (int)(t >= a.seg1.tile0) + (int)(t >= a.seg2.tile0);
+}
+__device__ __forceinline__ const TcSeg& tc_seg(const TcArgs& a, int sg) {
+    return sg == 0 ? a.seg0 : (sg == 1 ? a.seg1 : a.seg2);
+}
 
 // byte offset of element (n, kk) in a K-major, unswizzled [16 x 16] f16 tile
 // (core matrices of 8 rows x 8 elements: K groups 128 B apart, row groups 256 B)
@@ -1099,12 +1123,11 @@ __device__ __forceinline__ uint32_t btile_off(int n, int kk) {
 }
 
 template <bool XF32, int SFMT, bool YF32>
-__global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, const __grid_constant__ CUtensorMap wmap,
-                                                               const __grid_constant__ CUtensorMap smap) {
+__global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps maps) {
     using Cfg = TcCfg<XF32, SFMT>;
     constexpr int S = Cfg::kStages;
     constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
-    extern __shared__ __align__(128) uint8_t smem_raw[];
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[4 * S + 9];
     __shared__ float s_xb[S][2];
     __shared__ uint32_t s_tmem;
@@ -1169,8 +1192,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
     if (warp == 0) {
         // ------------------------------------------------------- TMA producer
         if (lane == 0) {
-            prefetch_tensor_map(&wmap);
-            prefetch_tensor_map(&smap);
+            for (int sg = 0; sg < a.nseg; sg++) {
+                prefetch_tensor_map(&maps.w[sg]);
+                prefetch_tensor_map(&maps.s[sg]);
+            }
             const uint64_t pol = l2_evict_first_policy();
             int i = 0;
             for (; i < n_items; i++) {
@@ -1178,10 +1203,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
                 if (i >= S && !mbar_wait(wempty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status)) break;
                 const long long it = ibeg + i;
                 const int t = (int)(it / a.noct), o = (int)(it % a.noct);
+                const int sg = tc_seg_of(a, t);
+                const int lt = t - tc_seg(a, sg).tile0;  // tile within its segment
                 const uint32_t st = sm0 + (uint32_t)(s * Cfg::kStageBytes);
                 mbar_arrive_expect_tx(full_bar(s), kTcWBytes + Cfg::kSBytes);
-                tma_load_2d(st, &wmap, t * (kTcTN / 8), o * kTcRows, full_bar(s), pol);
-                tma_load_2d(st + kTcWBytes + Cfg::kBBytes, &smap, t * (kTcTN * ssz / 8), o * 2, full_bar(s), pol);
+                tma_load_2d(st, &maps.w[sg], lt * (kTcTN / 8), o * kTcRows, full_bar(s), pol);
+                tma_load_2d(st + kTcWBytes + Cfg::kBBytes, &maps.s[sg], lt * (kTcTN * ssz / 8), o * 2, full_bar(s), pol);
             }
             s_issued = i;
         }
@@ -1266,16 +1293,17 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
         const uint32_t mask = (p & 1) ? 0x00F000F0u : 0x000F000Fu;
         const float E = (p & 1) ? 1048576.0f : 16777216.0f;  // 2^20 / 2^24
         const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
-        const float inv = SFMT == G4B_SCALE_E4M3 ? a.inv : 1.0f;
         const long long t_first = ibeg / a.noct;
         const long long t_last = n_items > 0 ? (iend - 1) / a.noct : t_first - 1;
         const int dq = tid - kTcDq0 * 32;               // 0..127 among the dequant threads
 
         auto write_y = [&](long long t, int col, float v) {
-            const int n = (int)t * kTcTN + col;
-            if (n < a.N) {
-                if (YF32) reinterpret_cast<float*>(a.y)[n] = v * inv;
-                else reinterpret_cast<__half*>(a.y)[n] = __float2half_rn(v * inv);
+            const TcSeg& sgm = tc_seg(a, tc_seg_of(a, t));
+            const int n = ((int)t - sgm.tile0) * kTcTN + col;
+            const float inv = SFMT == G4B_SCALE_E4M3 ? sgm.inv : 1.0f;
+            if (n < sgm.N) {
+                if (YF32) reinterpret_cast<float*>(sgm.y)[n] = v * inv;
+                else reinterpret_cast<__half*>(sgm.y)[n] = __float2half_rn(v * inv);
             }
         };
         auto reduce_tile = [&](long long t) {
@@ -1455,10 +1483,11 @@ struct TcPlan {
 
 static bool tc_ok(int M, int N, int K, int split) { return M == 1 && split == 0 && N % 32 == 0 && K % kTcRows == 0; }
 
-static TcPlan tc_plan(int N, int K, int sms, bool xf32, int sfmt) {
+static TcPlan tc_plan(int nseg, const int* Ns, int K, int sms, bool xf32, int sfmt) {
     TcPlan p{};
     p.noct = K / kTcRows;
-    p.ntiles = (N + kTcTN - 1) / kTcTN;
+    p.ntiles = 0;
+    for (int i = 0; i < nseg; i++) p.ntiles += (Ns[i] + kTcTN - 1) / kTcTN;
     p.total = (long long)p.ntiles * p.noct;
     p.G = (int)std::max<long long>(1, std::min<long long>(std::max(sms, 1), p.total));
     const long long lmax = (p.total + p.G - 1) / p.G;
@@ -1473,15 +1502,20 @@ static TcPlan tc_plan(int N, int K, int sms, bool xf32, int sfmt) {
 }
 
 template <bool XF32, int SFMT, bool YF32>
-static int launch_tc(const TcArgs& a, const TcPlan& p, const uint32_t* wp, const void* scales, cudaStream_t s) {
-    CUtensorMap wmap, smap;
-    int st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, wp, (uint64_t)a.N / 8, (uint64_t)a.K,
-                           (uint64_t)a.N / 2, kTcTN / 8, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (st != G4B_OK) return st;
+static int launch_tc(const TcArgs& a, const TcPlan& p, const uint32_t* const* wps, const void* const* scales,
+                     cudaStream_t s) {
+    TcMaps maps;
     constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
-    st = tensor_map_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT64, scales, (uint64_t)a.N * ssz / 8, (uint64_t)a.K / 32,
-                       (uint64_t)a.N * ssz, kTcTN * ssz / 8, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (st != G4B_OK) return st;
+    for (int i = 0; i < kTcMaxSeg; i++) {
+        const int k = i < a.nseg ? i : 0;  // unused slots repeat segment 0's maps
+        const int N = k == 0 ? a.seg0.N : (k == 1 ? a.seg1.N : a.seg2.N);
+        int st = tensor_map_2d(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, wps[k], (uint64_t)N / 8, (uint64_t)a.K,
+                               (uint64_t)N / 2, kTcTN / 8, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st != G4B_OK) return st;
+        st = tensor_map_2d(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, scales[k], (uint64_t)N * ssz / 8,
+                           (uint64_t)a.K / 32, (uint64_t)N * ssz, kTcTN * ssz / 8, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st != G4B_OK) return st;
+    }
     auto kern = gemv_tc_kernel<XF32, SFMT, YF32>;
     static int attr_set_mask = 0;
     int dev = 0;
@@ -1492,13 +1526,13 @@ static int launch_tc(const TcArgs& a, const TcPlan& p, const uint32_t* wp, const
         if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         attr_set_mask |= 1 << (dev & 31);
     }
-    cudaError_t e = launch_k(kern, dim3(p.G), dim3(kTcThreads), TcCfg<XF32, SFMT>::kSmem, s, a, wmap, smap);
+    cudaError_t e = launch_k(kern, dim3(p.G), dim3(kTcThreads), TcCfg<XF32, SFMT>::kSmem, s, a, maps);
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: launch: %s", cudaGetErrorString(e));
     return G4B_OK;
 }
 
-static int dispatch_tc(const TcArgs& a, const TcPlan& p, const uint32_t* wp, const void* sc, bool xf32, int sfmt,
-                       bool yf32, cudaStream_t s) {
+static int dispatch_tc(const TcArgs& a, const TcPlan& p, const uint32_t* const* wp, const void* const* sc, bool xf32,
+                       int sfmt, bool yf32, cudaStream_t s) {
     if (xf32) {
         if (sfmt == G4B_SCALE_F16)
             return yf32 ? launch_tc<true, G4B_SCALE_F16, true>(a, p, wp, sc, s)
@@ -1511,6 +1545,59 @@ static int dispatch_tc(const TcArgs& a, const TcPlan& p, const uint32_t* wp, con
                     : launch_tc<false, G4B_SCALE_F16, false>(a, p, wp, sc, s);
     return yf32 ? launch_tc<false, G4B_SCALE_E4M3, true>(a, p, wp, sc, s)
                 : launch_tc<false, G4B_SCALE_E4M3, false>(a, p, wp, sc, s);
+}
+
+// Plan, check the workspace, and launch the tensor-core GEMV over `nseg`
+// segments that share x (shapes already validated by the caller).
+static int run_tc(const void* x, int x_dtype, int nseg, const g4b_gemv_segment* segs, int scale_fmt, int y_dtype,
+                  int K, void* workspace, size_t ws_bytes, int sms, cudaStream_t s, const char* op) {
+    int Ns[kTcMaxSeg];
+    for (int i = 0; i < nseg; i++) Ns[i] = segs[i].N;
+    const TcPlan p = tc_plan(nseg, Ns, K, sms, x_dtype == G4B_DT_F32, scale_fmt);
+    G4B_REQUIRE(p.ntiles <= kGemvMaxTiles || p.ws_bytes == 0, G4B_E_SHAPE, "%s: too many columns for a split-K call",
+                op);
+    if (p.ws_bytes) {
+        G4B_REQUIRE(workspace != nullptr && ws_bytes >= p.ws_bytes, G4B_E_WORKSPACE,
+                    "%s: needs %zu bytes of workspace, got %zu", op, p.ws_bytes, workspace ? ws_bytes : 0);
+        G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "%s: workspace must be 16-byte aligned", op);
+    }
+    TcArgs a{};
+    a.x = x;
+    TcSeg* dst[kTcMaxSeg] = {&a.seg0, &a.seg1, &a.seg2};
+    const uint32_t* wps[kTcMaxSeg];
+    const void* scs[kTcMaxSeg];
+    int tile0 = 0;
+    for (int i = 0; i < kTcMaxSeg; i++) {
+        if (i < nseg) {
+            dst[i]->y = segs[i].y;
+            dst[i]->inv = segs[i].inv;
+            dst[i]->N = segs[i].N;
+            dst[i]->tile0 = tile0;
+            tile0 += (segs[i].N + kTcTN - 1) / kTcTN;
+            wps[i] = segs[i].wp;
+            scs[i] = segs[i].scales;
+        } else {
+            *dst[i] = *dst[0];
+            dst[i]->tile0 = 1 << 30;  // never reached
+            wps[i] = segs[0].wp;
+            scs[i] = segs[0].scales;
+        }
+    }
+    a.nseg = nseg;
+    a.K = K;
+    a.noct = p.noct;
+    a.ntiles = p.ntiles;
+    a.G = p.G;
+    a.maxseg = p.maxseg;
+    a.total = p.total;
+    if (p.ws_bytes) {
+        a.counters = (unsigned*)workspace;
+        a.partial = (float*)((char*)workspace + kGemvCounterBytes);
+    }
+    const int st = dispatch_tc(a, p, wps, scs, x_dtype == G4B_DT_F32, scale_fmt, y_dtype == G4B_DT_F32, s);
+    if (st != G4B_OK) return st;
+    count_launch();
+    return launch_status(op);
 }
 
 unsigned read_status_gemv() {
@@ -1768,7 +1855,7 @@ size_t g4b_gemv_workspace_bytes(int M, int N, int K, int split) {
     if (check_device(&sms) != G4B_OK) sms = 148;
     clear_error();
     // the activation and scale formats only change the shared-memory layout, not the workspace
-    if (tc_ok(M, N, K, split)) return tc_plan(N, K, sms, true, G4B_SCALE_F16).ws_bytes;
+    if (tc_ok(M, N, K, split)) return tc_plan(1, &N, K, sms, true, G4B_SCALE_F16).ws_bytes;
     if (stream_ok(N, K, split)) return stream_plan(M, N, K, split, sms, true, G4B_SCALE_F16).ws_bytes;
     return gemv_plan(M, N, K, split, sms).ws_bytes;
 }
@@ -1820,32 +1907,8 @@ static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, c
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const size_t xe = x_dtype == G4B_DT_F32 ? 4 : 2, ye = y_dtype == G4B_DT_F32 ? 4 : 2;
     if (tc_ok(M, N, K, split)) {
-        const TcPlan p = tc_plan(N, K, sms, x_dtype == G4B_DT_F32, scale_fmt);
-        if (p.ws_bytes) {
-            G4B_REQUIRE(workspace != nullptr && ws_bytes >= p.ws_bytes, G4B_E_WORKSPACE,
-                        "gemv_i4: needs %zu bytes of workspace, got %zu", p.ws_bytes, workspace ? ws_bytes : 0);
-            G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "gemv_i4: workspace must be 16-byte aligned");
-            G4B_REQUIRE(p.ntiles <= kGemvMaxTiles, G4B_E_SHAPE, "gemv_i4: N=%d too large for a split-K call", N);
-        }
-        TcArgs a{};
-        a.x = x;
-        a.y = y;
-        a.inv = inv;
-        a.N = N;
-        a.K = K;
-        a.noct = p.noct;
-        a.ntiles = p.ntiles;
-        a.G = p.G;
-        a.maxseg = p.maxseg;
-        a.total = p.total;
-        if (p.ws_bytes) {
-            a.counters = (unsigned*)workspace;
-            a.partial = (float*)((char*)workspace + kGemvCounterBytes);
-        }
-        st = dispatch_tc(a, p, wp, scales, x_dtype == G4B_DT_F32, scale_fmt, y_dtype == G4B_DT_F32, s);
-        if (st != G4B_OK) return st;
-        count_launch();
-        return launch_status("gemv_i4");
+        g4b_gemv_segment sg{wp, scales, inv, y, N};
+        return run_tc(x, x_dtype, 1, &sg, scale_fmt, y_dtype, K, workspace, ws_bytes, sms, s, "gemv_i4");
     }
     if (m1_ok(M, N, K, split)) {
         const M1Plan p = m1_plan(N, K, sms, x_dtype == G4B_DT_F32, scale_fmt);
@@ -1948,6 +2011,48 @@ static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, c
         if (st != G4B_OK) return st;
     }
     return G4B_OK;
+}
+
+size_t g4b_gemv_fused_workspace_bytes(int nseg, const int* Ns, int K) {
+    if (nseg < 1 || nseg > kTcMaxSeg || !Ns || K <= 0 || K % kTcRows) return 0;
+    for (int i = 0; i < nseg; i++)
+        if (Ns[i] <= 0 || Ns[i] % 32) return 0;
+    int sms = 148;
+    if (check_device(&sms) != G4B_OK) sms = 148;
+    clear_error();
+    return tc_plan(nseg, Ns, K, sms, true, G4B_SCALE_F16).ws_bytes;
+}
+
+int g4b_gemv_i4_fused(const void* x, int x_dtype, int nseg, const g4b_gemv_segment* segs, int scale_fmt, int y_dtype,
+                      int K, void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream) {
+    G4B_ENTRY("gemv_i4_fused");
+    G4B_REQUIRE((flags & ~(unsigned)G4B_GEMV_PDL) == 0, G4B_E_ARG, "gemv_i4_fused: unknown flags 0x%x", flags);
+    G4B_REQUIRE(x && segs, G4B_E_ARG, "gemv_i4_fused: NULL pointer argument");
+    G4B_REQUIRE(nseg >= 1 && nseg <= kTcMaxSeg, G4B_E_ARG, "gemv_i4_fused: nseg=%d must be 1..%d", nseg, kTcMaxSeg);
+    G4B_REQUIRE(x_dtype == G4B_DT_F32 || x_dtype == G4B_DT_F16, G4B_E_ARG, "gemv_i4_fused: bad x_dtype %d", x_dtype);
+    G4B_REQUIRE(y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16, G4B_E_ARG, "gemv_i4_fused: bad y_dtype %d", y_dtype);
+    G4B_REQUIRE(scale_fmt == G4B_SCALE_F16 || scale_fmt == G4B_SCALE_E4M3, G4B_E_ARG,
+                "gemv_i4_fused: bad scale_fmt %d", scale_fmt);
+    G4B_REQUIRE(K > 0 && K % kTcRows == 0, G4B_E_SHAPE, "gemv_i4_fused: K=%d must be a multiple of %d", K, kTcRows);
+    G4B_REQUIRE(aligned16(x), G4B_E_ALIGN, "gemv_i4_fused: x must be 16-byte aligned");
+    for (int i = 0; i < nseg; i++) {
+        const g4b_gemv_segment& g = segs[i];
+        G4B_REQUIRE(g.wp && g.scales && g.y, G4B_E_ARG, "gemv_i4_fused: segment %d has a NULL pointer", i);
+        G4B_REQUIRE(g.N > 0 && g.N % 32 == 0, G4B_E_SHAPE, "gemv_i4_fused: segment %d N=%d must be a multiple of 32",
+                    i, g.N);
+        G4B_REQUIRE(aligned16(g.wp) && aligned16(g.scales), G4B_E_ALIGN,
+                    "gemv_i4_fused: segment %d wp and scales must be 16-byte aligned", i);
+        G4B_REQUIRE(((uintptr_t)g.y & (y_dtype == G4B_DT_F32 ? 3u : 1u)) == 0, G4B_E_ALIGN,
+                    "gemv_i4_fused: segment %d y misaligned", i);
+    }
+    int sms = 0;
+    int st = check_device(&sms);
+    if (st != G4B_OK) return st;
+    t_pdl = (flags & G4B_GEMV_PDL) != 0;
+    st = run_tc(x, x_dtype, nseg, segs, scale_fmt, y_dtype, K, workspace, ws_bytes, sms,
+                reinterpret_cast<cudaStream_t>(stream), "gemv_i4_fused");
+    t_pdl = false;
+    return st;
 }
 
 int g4b_gemv_i4_noalloc(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,

@@ -56,6 +56,8 @@ SIGNATURES = {
     "g4b_gemv_i4": (_I, [_P, _I, _I, _P, _P, _I, _F, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "g4b_gemv_i4_ex": (_I, [_P, _I, _I, _P, _P, _I, _F, _P, _I, _I, _I, _I, _P, _Z, C.c_uint, _P]),
     "g4b_gemv_i4_noalloc": (_I, [_P, _I, _I, _P, _P, _I, _F, _P, _I, _I, _I, _I, _P]),
+    "g4b_gemv_fused_workspace_bytes": (_Z, [_I, _P, _I]),
+    "g4b_gemv_i4_fused": (_I, [_P, _I, _I, _P, _I, _I, _I, _P, _Z, C.c_uint, _P]),
     "g4b_reduce_partials": (_I, [_P, _P, _I, _I, _P]),
     "g4b_dequant_i4": (_I, [_P, _P, _I, _F, _P, _I, _I, _I, _P]),
     "g4b_cast": (_I, [_P, _I, _P, _I, _Z, _P]),
@@ -68,6 +70,11 @@ SIGNATURES = {
     "g4b_gemm_w8a8": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _P]),
     "g4b_gemm_w4a8": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _P]),
 }
+
+
+class GemvSegment(C.Structure):
+    """struct g4b_gemv_segment (include/g4b.h)."""
+    _fields_ = [("wp", C.c_void_p), ("scales", C.c_void_p), ("inv", C.c_float), ("y", C.c_void_p), ("N", C.c_int)]
 
 
 class G4BError(RuntimeError):

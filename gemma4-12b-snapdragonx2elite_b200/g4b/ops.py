@@ -7,6 +7,7 @@ PyTorch fallback.
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 from dataclasses import dataclass
 from typing import Optional
@@ -129,6 +130,43 @@ def gemv_i4(x: torch.Tensor, w: DeviceWeight, split: int = 0, out: Optional[torc
         _ptr(out), _DT[out.dtype], w.N, w.K, split, _ptr(ws), ws.numel() if ws is not None else 0,
         L.GEMV_PDL if pdl else 0, sh))
     return out.view(-1) if squeeze else out
+
+
+def gemv_fused_workspace_bytes(Ns, K: int) -> int:
+    arr = (ctypes.c_int * len(Ns))(*Ns)
+    return int(L.load().g4b_gemv_fused_workspace_bytes(len(Ns), arr, K))
+
+
+def gemv_i4_fused(x: torch.Tensor, ws_: list, outs: Optional[list] = None, out_dtype: torch.dtype = torch.float32,
+                  stream: Optional[torch.cuda.Stream] = None, workspace: Optional[torch.Tensor] = None,
+                  pdl: bool = False) -> list:
+    """Up to three GEMVs on one x [K] in one launch (q/k/v, gate/up):
+    returns [W_i x for each weight].  All weights share K and the scale format."""
+    _need(x, "x")
+    if not 1 <= len(ws_) <= 3:
+        raise ValueError("gemv_i4_fused: 1 to 3 weights")
+    K = x.numel()
+    fmt = ws_[0].scale_fmt
+    if any(w.K != K or w.scale_fmt != fmt for w in ws_):
+        raise ValueError("gemv_i4_fused: weights must share K and the scale format")
+    if outs is None:
+        outs = [torch.empty((w.N,), dtype=out_dtype, device=x.device) for w in ws_]
+    for o in outs:
+        _need(o, "out")
+    if any(o.dtype != outs[0].dtype for o in outs):
+        raise ValueError("gemv_i4_fused: all outputs must share one dtype")
+    sh = _stream_handle(stream, x.device)
+    lib = L.load()
+    need = gemv_fused_workspace_bytes([w.N for w in ws_], K)
+    ws = workspace
+    if need and ws is None:
+        ws = WORKSPACES.get(x.device, sh, need)
+    segs = (L.GemvSegment * len(ws_))(*[L.GemvSegment(_ptr(w.wp), _ptr(w.scales), w.inv, _ptr(o), w.N)
+                                         for w, o in zip(ws_, outs)])
+    L.check("g4b_gemv_i4_fused", lib.g4b_gemv_i4_fused(
+        _ptr(x), _DT[x.dtype], len(ws_), ctypes.cast(segs, ctypes.c_void_p), fmt, _DT[outs[0].dtype], K,
+        _ptr(ws), ws.numel() if ws is not None else 0, L.GEMV_PDL if pdl else 0, sh))
+    return outs
 
 
 def gemm_i4(X: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None,

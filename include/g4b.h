@@ -153,6 +153,33 @@ G4B_API int g4b_gemv_i4_noalloc(const void* x, int x_dtype, int M,
                         const uint32_t* wp, const void* scales, int scale_fmt, float inv,
                         void* y, int y_dtype, int N, int K, int split, g4b_stream_t stream);
 
+/* One GEMV of a fused launch (g4b_gemv_i4_fused): packed words [K, N/8],
+ * scales [K/32, N] (f16 or e4m3 per the call's scale_fmt), the e4m3 inverse
+ * scale 2^-shift (ignored for f16 scales) and the output y [N]. */
+typedef struct g4b_gemv_segment {
+    const uint32_t* wp;
+    const void* scales;
+    float inv;
+    void* y;
+    int N;
+} g4b_gemv_segment;
+
+/* Workspace bytes for g4b_gemv_i4_fused over segments of these widths. */
+G4B_API size_t g4b_gemv_fused_workspace_bytes(int nseg, const int* Ns, int K);
+
+/* Up to three M = 1 GEMVs that read the same x in one launch: the engine's
+ * consecutive gemv() dispatches on one input buffer -- q, k, v on the normed
+ * hidden state, then gate and up (src/vk_engine.py:280-284; each a
+ * vk/gemv.comp or vk/gemv_fp8.comp dispatch with its reduce).  Every
+ * segment's result is what g4b_gemv_i4 would give it alone, up to f32
+ * summation order; the work of all segments is spread over the SMs as one
+ * grid, so the small k/v GEMVs do not each pay a launch and a ramp.
+ *   x [K] f32 or f16; each segment N % 32 == 0; K % 64 == 0; 1 <= nseg <= 3.
+ *   flags: 0 or G4B_GEMV_PDL (as g4b_gemv_i4_ex). */
+G4B_API int g4b_gemv_i4_fused(const void* x, int x_dtype, int nseg, const g4b_gemv_segment* segs, int scale_fmt,
+                              int y_dtype, int K, void* workspace, size_t ws_bytes, unsigned flags,
+                              g4b_stream_t stream);
+
 /* Split-K partial reduction, vk/reduce.comp:8-12:
  *     y[n] = sum_{c=0}^{split-1} partial[c*N + n]   (c ascending, f32)
  * Exposed on its own for parity with the reference's reduce dispatch

@@ -242,3 +242,51 @@ def test_gemv_pdl_chain_keeps_dependencies(fp8):
     assert_close(bufs[-1].cpu().numpy(), ref, f"pdl chain graph fp8={fp8}")
     assert L.query(L.Q_KERNEL_STATUS) == 0
     del g
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+@pytest.mark.parametrize("xdt", [torch.float16, torch.float32])
+def test_gemv_fused_segments_match_oracle(fp8, xdt):
+    """g4b_gemv_i4_fused: q/k/v (three widths) and gate/up on one x, each
+    segment against the oracle; the e4m3 segments carry different inverse
+    scales (one weight is 16x larger, so its shift differs)."""
+    K = 3840
+    x = activations(1, K, seed=21)[0]
+    xt = torch.from_numpy(x).to(DEV).to(xdt)
+    x_used = xt.float().cpu().numpy()
+    for Ns in ([4096, 2048, 2048], [15360, 15360], [800]):
+        packed = []
+        for i, N in enumerate(Ns):
+            std = 0.32 if i == 1 else 0.02
+            packed.append(_packed(N, K, seed=50 + 7 * i + N, fp8=fp8, std=std))
+        if fp8 and len(Ns) > 1:
+            assert packed[0][1].inv != packed[1][1].inv
+        outs = ops.gemv_i4_fused(xt, [p[2] for p in packed], out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        for (W, pw, dw), y in zip(packed, outs):
+            assert_close(y.cpu().numpy(), _oracle_y(pw, x_used), f"fused N={pw.N} of {Ns} fp8={fp8} x={xdt}")
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+
+
+def test_gemv_fused_rejects_bad_arguments():
+    lib = L.load()
+    K = 256
+    _, _, a = _packed(256, K, seed=1)
+    _, _, b = _packed(272, K, seed=2)                                   # N % 32 != 0
+    x = torch.zeros(K, dtype=torch.float16, device=DEV)
+    y = torch.zeros(512, dtype=torch.float32, device=DEV)
+    sh = torch.cuda.current_stream().cuda_stream
+    mk = lambda ws: (L.GemvSegment * len(ws))(*[L.GemvSegment(w.wp.data_ptr(), w.scales.data_ptr(), 1.0,  # noqa
+                                                                y.data_ptr(), w.N) for w in ws])
+    import ctypes
+    before = L.launches()
+    segs = mk([a, b])
+    assert lib.g4b_gemv_i4_fused(x.data_ptr(), 1, 2, ctypes.cast(segs, ctypes.c_void_p), 0, 0, K, None, 0, 0,
+                                 sh) == L.G4B_E_SHAPE
+    segs = mk([a, a, a, a])
+    assert lib.g4b_gemv_i4_fused(x.data_ptr(), 1, 4, ctypes.cast(segs, ctypes.c_void_p), 0, 0, K, None, 0, 0,
+                                 sh) == L.G4B_E_ARG
+    segs = mk([a])
+    assert lib.g4b_gemv_i4_fused(x.data_ptr(), 1, 1, ctypes.cast(segs, ctypes.c_void_p), 0, 0, 96, None, 0, 0,
+                                 sh) == L.G4B_E_SHAPE                    # K % 64
+    assert L.launches() == before
