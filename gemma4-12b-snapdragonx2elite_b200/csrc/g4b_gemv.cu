@@ -360,6 +360,19 @@ __global__ void __launch_bounds__(kGemvThreads, NT == 1 ? 3 : 2) gemv_i4_kernel(
 // summed by the last CTA to arrive (per-tile counter), in CTA order, so the
 // result is deterministic.  With a caller-given split the ranges are exactly
 // the reference's K-slices.
+// (tile, k-chunk) of consecutive items: one division when a walk starts, none
+// per item (64-bit division is a long emulated sequence on the GPU)
+struct ItemCursor {
+    int t, o, noct;
+    __device__ ItemCursor(long long item, int noct_) : t((int)(item / noct_)), o((int)(item % noct_)), noct(noct_) {}
+    __device__ __forceinline__ void next() {
+        if (++o == noct) {
+            o = 0;
+            ++t;
+        }
+    }
+};
+
 constexpr int kStTN = 256;
 constexpr int kStRows = 128;                         // rows per stage = 4 scale blocks
 constexpr int kStWBytes = kStRows * (kStTN / 2);     // 16 KB of packed weights
@@ -420,10 +433,11 @@ __global__ void __launch_bounds__(kStThreads, 2) gemv_i4_stream_kernel(const Str
             prefetch_tensor_map(&smap);
             const uint64_t pol = l2_evict_first_policy();
             int i = 0;
-            for (long long it = ibeg; it < iend; ++it, ++i) {
+            ItemCursor cw(ibeg, a.nquad);
+            for (long long it = ibeg; it < iend; ++it, ++i, cw.next()) {
                 const int s = i % S;
                 if (i >= S && !mbar_wait(empty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status)) break;
-                const int t = (int)(it / a.nquad), qd = (int)(it % a.nquad);
+                const int t = cw.t, qd = cw.o;
                 // full boxes always land (out-of-range columns are zero-filled)
                 mbar_arrive_expect_tx(full_bar(s), kStWBytes + a.s_bytes + (uint32_t)(a.M * kStRows * esz));
                 const uint32_t st = smem0 + (uint32_t)s * a.stage_bytes;
@@ -436,10 +450,11 @@ __global__ void __launch_bounds__(kStThreads, 2) gemv_i4_stream_kernel(const Str
         // ---------------- activation producer (waits for the previous grid)
         pdl_wait();
         int i = 0;
-        for (long long it = ibeg; it < iend; ++it, ++i) {
+        ItemCursor cx(ibeg, a.nquad);
+        for (long long it = ibeg; it < iend; ++it, ++i, cx.next()) {
             const int s = i % S;
             if (i >= S && !mbar_wait(empty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status)) break;
-            const int qd = (int)(it % a.nquad);
+            const int qd = cx.o;
             if (lane < a.M)
                 bulk_g2s_nohint(smem0 + (uint32_t)s * a.stage_bytes + kStWBytes + a.s_bytes + lane * kStRows * esz,
                                 reinterpret_cast<const uint8_t*>(a.x) + ((size_t)lane * a.K + qd * kStRows) * esz,
@@ -524,8 +539,9 @@ __global__ void __launch_bounds__(kStThreads, 2) gemv_i4_stream_kernel(const Str
         };
 
         int i = 0;
-        for (long long it = ibeg; it < iend; ++it, ++i) {
-            const long long t = it / a.nquad;
+        ItemCursor cc(ibeg, a.nquad);
+        for (long long it = ibeg; it < iend; ++it, ++i, cc.next()) {
+            const long long t = cc.t;
             if (t != cur_t) {
                 if (cur_t >= 0) flush(cur_t);
                 #pragma unroll
@@ -1062,8 +1078,10 @@ static int dispatch_m1(const M1Args& a, const M1Plan& p, const uint32_t* wp, con
 //  * footprint <= half an SM (256 threads, <= 106 KB shared memory, 256 TMEM
 //    columns), so with programmatic dependent launch the next GEMV's CTA
 //    lives beside this one and streams its weights while this one finishes.
-// Warps: 0 TMA producer, 1 MMA issuer (and TMEM owner), 2 x -> B tiles,
-// 3 idle, 4-7 dequant + epilogue (TMEM lane quarters 0-3).
+// Warps: 0 TMA producer (packed words and scales at once, each item's slice of
+// x once the previous grid has completed), 1 MMA issuer (and TMEM owner),
+// 2-3 x -> B tiles (alternate items), 4-7 dequant + epilogue (TMEM lane
+// quarters 0-3).
 constexpr int kTcRows = 64;
 constexpr int kTcTN = 256;
 constexpr int kTcWBytes = kTcRows * (kTcTN / 2);  // 8 KB of packed words per item
@@ -1077,7 +1095,8 @@ struct TcCfg {
     static constexpr int kBTile = 16 * 16 * 2;                   // one [N=16 x K=16] f16 tile
     static constexpr int kBBytes = (kTcRows / 8) * kBTile;       // 4 KB
     static constexpr int kSBytes = 2 * kTcTN * (SFMT == G4B_SCALE_F16 ? 2 : 1);
-    static constexpr int kStageBytes = kTcWBytes + kBBytes + kSBytes;
+    static constexpr int kXBytes = kTcRows * (XF32 ? 4 : 2);    // the item's slice of x
+    static constexpr int kStageBytes = kTcWBytes + kBBytes + kSBytes + kXBytes;
     static constexpr int kStages = 8;
     static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 128;
 };
@@ -1128,11 +1147,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
     constexpr int S = Cfg::kStages;
     constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    __shared__ uint64_t bars[4 * S + 9];
+    __shared__ uint64_t bars[5 * S + 9];
     __shared__ float s_xb[S][2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     __shared__ int s_issued;
+    __shared__ int s_xissued;
     __shared__ long long s_pending;
     __shared__ unsigned s_last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1150,6 +1170,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
     auto dfull_bar = [&](int i) { return bar0 + 8u * (4 * S + 4 + i); };   // accumulator ready
     auto dempty_bar = [&](int i) { return bar0 + 8u * (4 * S + 6 + i); };  // accumulator read (4)
     const uint32_t drain_bar = bar0 + 8u * (4 * S + 8);
+    auto xfull_bar = [&](int s) { return bar0 + 8u * (4 * S + 9 + s); };  // x slice landed (1 + tx)
     const long long ibeg = (long long)blockIdx.x * a.total / a.G;
     const long long iend = (long long)(blockIdx.x + 1) * a.total / a.G;
     const int n_items = (int)(iend - ibeg);
@@ -1158,8 +1179,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
         for (int s = 0; s < S; s++) {
             mbar_init(full_bar(s), 1);
             mbar_init(bfull_bar(s), 1);
-            mbar_init(wempty_bar(s), 4);
+            mbar_init(wempty_bar(s), 4 + 1);  // 4 dequant warps (words, scales) + the builder (x)
             mbar_init(bempty_bar(s), 1);
+            mbar_init(xfull_bar(s), 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(afull_bar(i), 4);
@@ -1170,6 +1192,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
         mbar_init(drain_bar, 1);
         s_abort = 0;
         s_issued = 0;
+        s_xissued = 0;
         s_pending = -1;
         fence_mbar_init();
     }
@@ -1197,20 +1220,39 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
                 prefetch_tensor_map(&maps.s[sg]);
             }
             const uint64_t pol = l2_evict_first_policy();
-            int i = 0;
-            for (; i < n_items; i++) {
+            auto issue_w = [&](int i, int t, int o) {  // packed words + scales of item i = (tile t, chunk o)
                 const int s = i % S;
-                if (i >= S && !mbar_wait(wempty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status)) break;
-                const long long it = ibeg + i;
-                const int t = (int)(it / a.noct), o = (int)(it % a.noct);
                 const int sg = tc_seg_of(a, t);
                 const int lt = t - tc_seg(a, sg).tile0;  // tile within its segment
                 const uint32_t st = sm0 + (uint32_t)(s * Cfg::kStageBytes);
                 mbar_arrive_expect_tx(full_bar(s), kTcWBytes + Cfg::kSBytes);
                 tma_load_2d(st, &maps.w[sg], lt * (kTcTN / 8), o * kTcRows, full_bar(s), pol);
                 tma_load_2d(st + kTcWBytes + Cfg::kBBytes, &maps.s[sg], lt * (kTcTN * ssz / 8), o * 2, full_bar(s), pol);
+            };
+            auto issue_x = [&](int i, int o) {  // the item's slice of x (only after the previous grid is done)
+                const int s = i % S;
+                const uint32_t st = sm0 + (uint32_t)(s * Cfg::kStageBytes);
+                mbar_arrive_expect_tx(xfull_bar(s), Cfg::kXBytes);
+                bulk_g2s_nohint(st + kTcWBytes + Cfg::kBBytes + Cfg::kSBytes,
+                                reinterpret_cast<const uint8_t*>(a.x) + (size_t)o * Cfg::kXBytes, Cfg::kXBytes,
+                                xfull_bar(s));
+            };
+            // weights do not depend on the previous kernel: fill every stage before waiting for it
+            const int npre = n_items < S ? n_items : S;
+            ItemCursor cw(ibeg, a.noct), cx(ibeg, a.noct);
+            for (int i = 0; i < npre; i++, cw.next()) issue_w(i, cw.t, cw.o);
+            pdl_wait();
+            for (int i = 0; i < npre; i++, cx.next()) issue_x(i, cx.o);
+            int i = npre, xi = npre;
+            for (; i < n_items; i++, cw.next()) {
+                const int s = i % S;
+                if (!mbar_wait(wempty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status)) break;
+                issue_w(i, cw.t, cw.o);
+                issue_x(i, cw.o);
+                xi = i + 1;
             }
             s_issued = i;
+            s_xissued = xi;
         }
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
@@ -1227,11 +1269,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
                     break;
                 }
                 tc::fence_after();
-                const uint32_t bst = sm0 + (uint32_t)(s * Cfg::kStageBytes + kTcWBytes);
+                // the B tiles of a stage are kBTile apart: step the descriptor's start-address field
+                const uint64_t bdesc = tc::sdesc_noswz(sm0 + (uint32_t)(s * Cfg::kStageBytes + kTcWBytes), 128, 256);
+                const uint32_t dcol = tmem + kTcDCol + 16u * ab, acol = tmem + kTcACol + 64u * ab;
 #pragma unroll
                 for (int j = 0; j < kTcRows / 8; j++)
-                    tc::mma_f16_ts(tmem + kTcDCol + 16u * ab, tmem + kTcACol + 64u * ab + 8u * j,
-                                   tc::sdesc_noswz(bst + j * Cfg::kBTile, 128, 256), idesc, j != 0);
+                    tc::mma_f16_ts(dcol, acol + 8u * j, bdesc + (uint64_t)(j * (Cfg::kBTile >> 4)), idesc, j != 0);
                 tc::commit(aempty_bar(ab));
                 tc::commit(bempty_bar(s));
                 tc::commit(dfull_bar(ab));
@@ -1239,25 +1282,26 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
             tc::commit(drain_bar);
             mbar_wait_drain(drain_bar, 0, &g_gemv_status);
         }
-    } else if (warp == 2) {
+    } else if (warp == 2 || warp == 3) {
         // ------------------------------------------------------- x -> sparse B tiles
-        pdl_wait();
-        for (int i = 0; i < n_items; i++) {
+        // two warps, alternating items; x is already in the stage (bulk-copied by warp 0)
+        for (int i = warp - 2; i < n_items; i += 2) {
             const int s = i % S;
-            const bool good = i < S || mbar_wait(bempty_bar(s), ((i / S) & 1) ^ 1, abort_flag, &g_gemv_status);
+            const uint32_t ps = (uint32_t)(i / S) & 1u;
+            const bool good = mbar_wait(xfull_bar(s), ps, abort_flag, &g_gemv_status) &&
+                              (i < S || mbar_wait(bempty_bar(s), ps ^ 1u, abort_flag, &g_gemv_status));
             if (!__all_sync(0xffffffffu, good)) break;  // warp-uniform exit
-            const int o = (int)((ibeg + i) % a.noct);
             uint8_t* bt = smem + (size_t)s * Cfg::kStageBytes + kTcWBytes;
+            const uint8_t* xsm = bt + Cfg::kBBytes + Cfg::kSBytes;
             float xs[2];
 #pragma unroll
             for (int blk = 0; blk < 2; blk++) {
                 const int r = 32 * blk + lane;  // row within the item
-                const int k = o * kTcRows + r;
                 uint8_t* tile = bt + (r >> 3) * Cfg::kBTile;
                 const int kk = 2 * (r & 7);
                 float xv;
                 if constexpr (XF32) {
-                    xv = __ldg(reinterpret_cast<const float*>(a.x) + k);
+                    xv = reinterpret_cast<const float*>(xsm)[r];
                     const __half hi = __float2half_rn(xv);
                     const __half lo = __float2half_rn(xv - __half2float(hi));
                     *reinterpret_cast<__half*>(tile + btile_off(4 * blk + 0, kk)) = hi;
@@ -1265,14 +1309,17 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
                     *reinterpret_cast<__half*>(tile + btile_off(4 * blk + 2, kk)) = lo;
                     *reinterpret_cast<__half*>(tile + btile_off(4 * blk + 3, kk + 1)) = lo;
                 } else {
-                    const __half h = __ldg(reinterpret_cast<const __half*>(a.x) + k);
+                    const __half h = reinterpret_cast<const __half*>(xsm)[r];
                     xv = __half2float(h);
                     *reinterpret_cast<__half*>(tile + btile_off(2 * blk + 0, kk)) = h;
                     *reinterpret_cast<__half*>(tile + btile_off(2 * blk + 1, kk + 1)) = h;
                 }
-#pragma unroll
-                for (int m = 16; m >= 1; m >>= 1) xv += __shfl_xor_sync(0xffffffffu, xv, m);
                 xs[blk] = xv;
+            }
+#pragma unroll
+            for (int m = 16; m >= 1; m >>= 1) {
+                xs[0] += __shfl_xor_sync(0xffffffffu, xs[0], m);
+                xs[1] += __shfl_xor_sync(0xffffffffu, xs[1], m);
             }
             if (lane == 0) {
                 s_xb[s][0] = xs[0];
@@ -1280,7 +1327,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
             }
             tc::fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(bfull_bar(s));
+            if (lane == 0) {
+                mbar_arrive(bfull_bar(s));
+                mbar_arrive(wempty_bar(s));  // x slice consumed
+            }
         }
     } else if (warp >= kTcDq0) {
         // ------------------------------------------------------- dequant + epilogue
@@ -1398,7 +1448,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
         // flushes (with their named barriers) even after a wait has given up:
         // `ok` only turns the work off, never the control flow.
         bool ok = true;
-        for (int i = 0; i < n_items; i++) {
+        ItemCursor cur(ibeg, a.noct);
+        int t_prev = cur.t;
+        for (int i = 0; i < n_items; i++, t_prev = cur.t, cur.next()) {
             const int s = i % S, ab = i & 1;
             const uint32_t ps = (uint32_t)(i / S) & 1u;
             bool good = ok && mbar_wait(full_bar(s), ps, abort_flag, &g_gemv_status) &&
@@ -1443,9 +1495,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
             // epilogue of the previous item (its MMAs ran while this item was dequantised)
             if (i > 0) {
                 if (ok) ok = epilogue(i - 1);
-                const long long tp = (ibeg + i - 1) / a.noct;
-                if (tp != (ibeg + i) / a.noct) {
-                    flush_tile(tp, acc0, acc1);
+                if (t_prev != cur.t) {  // item i - 1 was the last of its tile in this CTA
+                    flush_tile(t_prev, acc0, acc1);
                     acc0 = acc1 = 0.f;
                 }
             }
@@ -1468,8 +1519,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
     __syncthreads();
     tc::fence_after();
     if (tid == 0 && *abort_flag) {
-        const int issued = s_issued;
+        const int issued = s_issued, xissued = s_xissued;
         for (int i = max(0, issued - S); i < issued; i++) mbar_wait_drain(full_bar(i % S), (i / S) & 1, &g_gemv_status);
+        for (int i = max(0, xissued - S); i < xissued; i++)
+            mbar_wait_drain(xfull_bar(i % S), (i / S) & 1, &g_gemv_status);
     }
     __syncthreads();
     if (warp == 1) tc::tmem_dealloc(tmem, 256);

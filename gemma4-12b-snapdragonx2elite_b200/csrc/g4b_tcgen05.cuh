@@ -182,7 +182,7 @@ __device__ __forceinline__ void ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32])
 // CTA releases its shared and tensor memory).
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, unsigned* status) {
     const uint64_t t0 = global_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_suspend(bar, parity, kSuspendHintNs)) {
         if (global_ns() - t0 > kWaitLimitNs) {
             atomicOr(status, kStatusTimeout);
             return false;

@@ -1,0 +1,96 @@
+"""Worker for tests/test_gpu_tp.py: one rank of a tensor-parallel decode over
+NCCL (launched by torch.distributed.run).  Rank 0 also runs the same chain
+with the unsharded weights on its own GPU and compares (tests/util.py bar).
+Exit code 0 = match."""
+import os
+import sys
+from datetime import timedelta
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+sys.path.insert(0, os.path.join(ROOT, "gemma4-12b-snapdragonx2elite_b200"))
+sys.path.insert(0, HERE)
+
+from g4b import _lib as L  # noqa: E402
+from g4b import ops, tp  # noqa: E402
+from g4b import quant_gpu as qz  # noqa: E402
+from util import assert_close  # noqa: E402
+
+H, NQ, NKV, FFN, VOCAB, LAYERS = 1024, 1024, 512, 2048, 8192, 2
+
+
+def main():
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+    L.load()
+    fp8 = os.environ.get("TP_FP8") == "1"
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    shapes = {"q": (NQ, H), "k": (NKV, H), "v": (NKV, H), "o": (H, NQ), "gate": (FFN, H), "up": (FFN, H),
+              "down": (H, FFN)}
+    kinds = dict(tp.LAYER_KINDS)
+    full, mine = [], []
+    for _ in range(LAYERS):
+        f, m = {}, {}
+        for name, (N, K) in shapes.items():
+            W = torch.randn((N, K), generator=gen, device=dev).mul_(0.02)
+            if rank == 0:
+                f[name] = qz.quant_device(W, pf=False, fp8=fp8, prefill_i8=False)
+            if kinds[name] == "col":
+                n0, n1 = tp.split_range(N, world, rank, tp.COL_ALIGN)
+                m[name] = qz.quant_device(W[n0:n1].contiguous(), pf=False, fp8=fp8, prefill_i8=False)
+            else:
+                k0, k1 = tp.split_range(K, world, rank, tp.ROW_ALIGN)
+                m[name] = qz.quant_device(W[:, k0:k1].contiguous(), pf=False, fp8=fp8, prefill_i8=False)
+        full.append(tp.TPLayer(**f) if rank == 0 else None)
+        mine.append(tp.TPLayer(**m))
+    Wl = torch.randn((VOCAB, H), generator=gen, device=dev).mul_(0.02)
+    n0, n1 = tp.split_range(VOCAB, world, rank, tp.COL_ALIGN)
+    lm = qz.quant_device(Wl[n0:n1].contiguous(), pf=False, fp8=fp8, prefill_i8=False)
+    lm_full = qz.quant_device(Wl, pf=False, fp8=fp8, prefill_i8=False) if rank == 0 else None
+    stream = torch.cuda.Stream(dev)
+
+    def gemv(x, w, out):
+        ops.gemv_i4(x, w, out=out, stream=stream, pdl=True)
+
+    dec = tp.TPDecoder(layers=mine, lm_head=lm, gemv=gemv, all_reduce=lambda t: dist.all_reduce(t),
+                       all_gather=lambda out, t: dist.all_gather_into_tensor(out, t),
+                       new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=dev),
+                       hidden=H, vocab=VOCAB, world=world)
+    x = torch.randn((H,), generator=gen, device=dev)
+    with torch.cuda.stream(stream):
+        logits = dec.step(x).clone()
+        # the same step captured in a CUDA graph (collectives included) and replayed
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            dec.step(x)
+        g.replay()
+    stream.synchronize()
+    replay = dec.bufs["logits"].clone()
+    ok = torch.tensor([1], device=dev)
+    if rank == 0:
+        ref = tp.decode_reference(full, lm_full, x, lambda h, w: ops.gemv_i4(h, w, out_dtype=torch.float32))
+        torch.cuda.synchronize()
+        try:
+            assert_close(logits.cpu().numpy(), ref.cpu().numpy(), f"TP world {world} vs unsharded")
+            assert torch.equal(logits, replay), "graph replay differs from the eager step"
+            assert L.query(L.Q_KERNEL_STATUS) == 0
+        except AssertionError as e:
+            print(e, flush=True)
+            ok.zero_()
+    dist.broadcast(ok, 0)
+    del g
+    dist.destroy_process_group()
+    sys.exit(0 if ok.item() == 1 else 1)
+
+
+if __name__ == "__main__":
+    main()
