@@ -633,6 +633,34 @@ constexpr int kM1WarpsPerGroup = 8;
 constexpr int kM1Consumers = 32 * kM1WarpsPerGroup * kM1Groups;  // 512
 constexpr int kM1Threads = kM1Consumers + 64;      // + TMA producer warp + activation producer warp
 
+// Up to three GEMVs that read the same x (the engine's q/k/v, or gate/up) run
+// as one launch: their column tiles are numbered one after another ("segments"),
+// and every per-tile decision (which weights to load, where y goes, which
+// e4m3 inverse scale applies) looks the segment up from the tile index.
+constexpr int kTcMaxSeg = 3;
+constexpr int kMaxCtas = 256;  // split-K plans never use more CTAs than this (one per SM)
+
+struct TcSeg {
+    void* y;
+    float inv;    // e4m3 2^-shift (1 for f16 scales)
+    int N;
+    int tile0;    // first tile of this segment in the launch's tile numbering
+};
+
+struct TcMaps {
+    CUtensorMap w[kTcMaxSeg];
+    CUtensorMap s[kTcMaxSeg];
+};
+
+template <class A>
+__host__ __device__ __forceinline__ int tc_seg_of(const A& a, long long t) {
+    return (int)(t >= a.seg1.tile0) + (int)(t >= a.seg2.tile0);
+}
+template <class A>
+__host__ __device__ __forceinline__ const TcSeg& tc_seg(const A& a, int sg) {
+    return sg == 0 ? a.seg0 : (sg == 1 ? a.seg1 : a.seg2);
+}
+
 // item i of a CTA -> its group, shared-memory stage and barrier phase parity
 __device__ __forceinline__ int m1_group(int i) { return i % kM1Groups; }
 __device__ __forceinline__ int m1_stage(int i) { return i % kM1Groups + kM1Groups * ((i / kM1Groups) % kM1PerGroup); }
@@ -640,11 +668,10 @@ __device__ __forceinline__ uint32_t m1_parity(int i) { return (uint32_t)((i / kM
 
 struct M1Args {
     const void* x;
-    void* y;
     float* partial;      // [G * maxseg, kStTN]
     unsigned* counters;  // [ntiles]
-    float inv;
-    int N, K, noct, ntiles, G, maxseg, stage_bytes, s_bytes;
+    TcSeg seg0, seg1, seg2;
+    int nseg, K, noct, ntiles, G, maxseg, stage_bytes, s_bytes;
     long long total;
 };
 
@@ -660,8 +687,7 @@ __device__ __forceinline__ int swz128(int row, int word) {
 
 template <bool XF32, int SFMT, bool YF32>
 __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args a,
-                                                                  const __grid_constant__ CUtensorMap wmap,
-                                                                  const __grid_constant__ CUtensorMap smap) {
+                                                                  const __grid_constant__ TcMaps maps) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[2 * kM1Stages];
     __shared__ float red[2][kM1Groups][kStTN];  // double-buffered: consecutive flushes never share it
@@ -670,6 +696,7 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
     __shared__ int s_issued;
     __shared__ int s_abort;
     __shared__ __align__(16) uint32_t s_zero[32];  // B-fragment source for lanes that feed zeros
+    __shared__ int s_ftile[kMaxCtas];              // first tile of each CTA's item range
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     volatile int* abort_flag = &s_abort;
     constexpr int esz = XF32 ? 4 : 2;
@@ -697,23 +724,30 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
         fence_mbar_init();
     }
     if (tid < 32) s_zero[tid] = 0u;
+    // the split-K reduction needs every CTA's first tile: one division per CTA, here, in parallel
+    for (int c = tid; c < a.G; c += blockDim.x)
+        s_ftile[c] = (int)(((long long)c * a.total / a.G) / a.noct);
     __syncthreads();
     pdl_launch_dependents();
 
     if (warp == pw) {
         if (lane == 0) {
-            prefetch_tensor_map(&wmap);
-            prefetch_tensor_map(&smap);
+            for (int sg = 0; sg < a.nseg; sg++) {
+                prefetch_tensor_map(&maps.w[sg]);
+                prefetch_tensor_map(&maps.s[sg]);
+            }
             const uint64_t pol = l2_evict_first_policy();
             int i = 0;
-            for (long long it = ibeg; it < iend; ++it, ++i) {
+            ItemCursor cw(ibeg, a.noct);
+            for (long long it = ibeg; it < iend; ++it, ++i, cw.next()) {
                 const int s = m1_stage(i);
                 if (i >= kM1Stages && !mbar_wait(empty_bar(s), m1_parity(i) ^ 1u, abort_flag, &g_gemv_status)) break;
-                const int t = (int)(it / a.noct), o = (int)(it % a.noct);
+                const int sg = tc_seg_of(a, cw.t);
+                const int lt = cw.t - tc_seg(a, sg).tile0, o = cw.o;
                 mbar_arrive_expect_tx(full_bar(s), kM1WBytes + a.s_bytes + kM1Rows * esz);
                 const uint32_t st = smem0 + (uint32_t)s * a.stage_bytes;
-                tma_load_2d(st, &wmap, t * (kStTN / 8), o * kM1Rows, full_bar(s), pol);
-                tma_load_2d(st + kM1WBytes, &smap, t * (kStTN * ssz / 8), o * 8, full_bar(s), pol);
+                tma_load_2d(st, &maps.w[sg], lt * (kStTN / 8), o * kM1Rows, full_bar(s), pol);
+                tma_load_2d(st + kM1WBytes, &maps.s[sg], lt * (kStTN * ssz / 8), o * 8, full_bar(s), pol);
             }
             s_issued = i;
         }
@@ -721,10 +755,11 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
         pdl_wait();
         if (lane == 0) {
             int i = 0;
-            for (long long it = ibeg; it < iend; ++it, ++i) {
+            ItemCursor cx(ibeg, a.noct);
+            for (long long it = ibeg; it < iend; ++it, ++i, cx.next()) {
                 const int s = m1_stage(i);
                 if (i >= kM1Stages && !mbar_wait(empty_bar(s), m1_parity(i) ^ 1u, abort_flag, &g_gemv_status)) break;
-                const int o = (int)(it % a.noct);
+                const int o = cx.o;
                 bulk_g2s_nohint(smem0 + (uint32_t)s * a.stage_bytes + kM1WBytes + a.s_bytes,
                                 reinterpret_cast<const uint8_t*>(a.x) + (size_t)o * kM1Rows * esz, kM1Rows * esz,
                                 full_bar(s));
@@ -738,7 +773,16 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
         // ldmatrix.x4: lane L addresses row L%8 of matrix L/8; matrix m = (step p + m/2, k-pair m%2)
         const int lm = lane >> 3, lrr = lane & 7, lq = lrr >> 1, le = lrr & 1;
         const int lds = lm >> 1, lh = lm & 1;
-        const float inv = SFMT == G4B_SCALE_E4M3 ? a.inv : 1.0f;
+        // y[n] of the tile's segment, scaled by its e4m3 inverse scale
+        auto write_y = [&](long long t, int col, float v) {
+            const TcSeg& sgm = tc_seg(a, tc_seg_of(a, t));
+            const int n = ((int)t - sgm.tile0) * kStTN + col;
+            const float inv = SFMT == G4B_SCALE_E4M3 ? sgm.inv : 1.0f;
+            if (n < sgm.N) {
+                if (YF32) ((float*)sgm.y)[n] = v * inv;
+                else ((__half*)sgm.y)[n] = __float2half_rn(v * inv);
+            }
+        };
         constexpr int NPASS = XF32 ? 2 : 1;   // f32 x: two passes of 4 blocks
         constexpr int NSTEP = XF32 ? 8 : 16;  // mma steps per pass
         constexpr int RMUL = XF32 ? 4 : 2;    // rows advanced per step
@@ -759,8 +803,7 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
                         pv[k] = 0.f;
                         if (k0 + k < nseg) {
                             const long long cc = c_first + k0 + k;
-                            const long long cb = cc * a.total / a.G;  // first item of CTA cc
-                            const long long sl = cc * a.maxseg + (t - cb / a.noct);
+                            const long long sl = cc * a.maxseg + (t - s_ftile[cc]);
                             pv[k] = __ldcg(&a.partial[(size_t)sl * kStTN + col]);
                         }
                     }
@@ -768,11 +811,7 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
                     for (int k = 0; k < 8; k++)
                         if (k0 + k < nseg) v += pv[k];
                 }
-                const int n = (int)t * kStTN + col;
-                if (n < a.N) {
-                    if (YF32) ((float*)a.y)[n] = v * inv;
-                    else ((__half*)a.y)[n] = __float2half_rn(v * inv);
-                }
+                write_y(t, col, v);
             }
             if (ctid == 0) a.counters[t] = 0u;  // ready for the next call
         };
@@ -934,12 +973,8 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
                 float v = red[rb][0][col];
                 #pragma unroll
                 for (int gg = 1; gg < kM1Groups; gg++) v += red[rb][gg][col];
-                const int n = (int)t * kStTN + col;
                 if (single) {
-                    if (n < a.N) {
-                        if (YF32) ((float*)a.y)[n] = v * inv;
-                        else ((__half*)a.y)[n] = __float2half_rn(v * inv);
-                    }
+                    write_y(t, col, v);
                 } else {
                     a.partial[(size_t)slot * kStTN + col] = v;
                 }
@@ -997,12 +1032,13 @@ struct M1Plan {
     size_t smem, ws_bytes;
 };
 
-static M1Plan m1_plan(int N, int K, int sms, bool xf32, int sfmt) {
+static M1Plan m1_plan(int nseg, const int* Ns, int K, int sms, bool xf32, int sfmt) {
     M1Plan p{};
     p.noct = K / 256;
-    p.ntiles = (N + kStTN - 1) / kStTN;
+    p.ntiles = 0;
+    for (int i = 0; i < nseg; i++) p.ntiles += (Ns[i] + kStTN - 1) / kStTN;
     p.total = (long long)p.ntiles * p.noct;
-    p.G = (int)std::max<long long>(1, std::min<long long>(std::max(sms, 1), p.total));
+    p.G = (int)std::max<long long>(1, std::min<long long>(std::min(std::max(sms, 1), kMaxCtas), p.total));
     const long long lmax = (p.total + p.G - 1) / p.G;
     p.maxseg = (int)((lmax + p.noct - 1) / p.noct + 1);
     p.s_bytes = 8 * kStTN * (sfmt == G4B_SCALE_F16 ? 2 : 1);
@@ -1019,15 +1055,20 @@ static M1Plan m1_plan(int N, int K, int sms, bool xf32, int sfmt) {
 static bool m1_ok(int M, int N, int K, int split) { return M == 1 && split == 0 && N % 32 == 0 && K % 256 == 0; }
 
 template <bool XF32, int SFMT, bool YF32>
-static int launch_m1(const M1Args& a, const M1Plan& p, const uint32_t* wp, const void* scales, cudaStream_t s) {
-    CUtensorMap wmap, smap;
-    int st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, wp, (uint64_t)a.N / 8, (uint64_t)a.K,
-                           (uint64_t)a.N / 2, kStTN / 8, kM1Rows, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st != G4B_OK) return st;
+static int launch_m1(const M1Args& a, const M1Plan& p, const uint32_t* const* wps, const void* const* scales,
+                     cudaStream_t s) {
+    TcMaps maps;
     constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
-    st = tensor_map_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT64, scales, (uint64_t)a.N * ssz / 8, (uint64_t)a.K / 32,
-                       (uint64_t)a.N * ssz, kStTN * ssz / 8, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (st != G4B_OK) return st;
+    for (int i = 0; i < kTcMaxSeg; i++) {
+        const int k = i < a.nseg ? i : 0;  // unused slots repeat segment 0's maps
+        const int N = tc_seg(a, k).N;
+        int st = tensor_map_2d(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, wps[k], (uint64_t)N / 8, (uint64_t)a.K,
+                               (uint64_t)N / 2, kStTN / 8, kM1Rows, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st != G4B_OK) return st;
+        st = tensor_map_2d(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, scales[k], (uint64_t)N * ssz / 8,
+                           (uint64_t)a.K / 32, (uint64_t)N * ssz, kStTN * ssz / 8, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st != G4B_OK) return st;
+    }
     auto kern = gemv_i4_m1_kernel<XF32, SFMT, YF32>;
     static int attr_set_mask = 0;
     int dev = 0;
@@ -1037,13 +1078,13 @@ static int launch_m1(const M1Args& a, const M1Plan& p, const uint32_t* wp, const
         if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         attr_set_mask |= 1 << (dev & 31);
     }
-    cudaError_t e = launch_k(kern, dim3(p.G), dim3(kM1Threads), p.smem, s, a, wmap, smap);
+    cudaError_t e = launch_k(kern, dim3(p.G), dim3(kM1Threads), p.smem, s, a, maps);
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4: launch: %s", cudaGetErrorString(e));
     return G4B_OK;
 }
 
-static int dispatch_m1(const M1Args& a, const M1Plan& p, const uint32_t* wp, const void* sc, bool xf32, int sfmt,
-                       bool yf32, cudaStream_t s) {
+static int dispatch_m1(const M1Args& a, const M1Plan& p, const uint32_t* const* wp, const void* const* sc, bool xf32,
+                       int sfmt, bool yf32, cudaStream_t s) {
     if (xf32) {
         if (sfmt == G4B_SCALE_F16) return yf32 ? launch_m1<true, G4B_SCALE_F16, true>(a, p, wp, sc, s) : launch_m1<true, G4B_SCALE_F16, false>(a, p, wp, sc, s);
         return yf32 ? launch_m1<true, G4B_SCALE_E4M3, true>(a, p, wp, sc, s) : launch_m1<true, G4B_SCALE_E4M3, false>(a, p, wp, sc, s);
@@ -1101,18 +1142,6 @@ struct TcCfg {
     static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 128;
 };
 
-// Up to three GEMVs that read the same x (the engine's q/k/v, or gate/up) run
-// as one launch: their column tiles are numbered one after another ("segments"),
-// and every per-tile decision (which weights to load, where y goes, which
-// e4m3 inverse scale applies) looks the segment up from the tile index.
-constexpr int kTcMaxSeg = 3;
-
-struct TcSeg {
-    void* y;
-    float inv;    // e4m3 2^-shift (1 for f16 scales)
-    int N;
-    int tile0;    // first tile of this segment in the launch's tile numbering
-};
 
 struct TcArgs {
     const void* x;
@@ -1123,17 +1152,7 @@ struct TcArgs {
     long long total;
 };
 
-struct TcMaps {
-    CUtensorMap w[kTcMaxSeg];
-    CUtensorMap s[kTcMaxSeg];
-};
 
-__device__ __forceinline__ int tc_seg_of(const TcArgs& a, long long t) {
-    return (int)(t >= a.seg1.tile0) + (int)(t >= a.seg2.tile0);
-}
-__device__ __forceinline__ const TcSeg& tc_seg(const TcArgs& a, int sg) {
-    return sg == 0 ? a.seg0 : (sg == 1 ? a.seg1 : a.seg2);
-}
 
 // byte offset of element (n, kk) in a K-major, unswizzled [16 x 16] f16 tile
 // (core matrices of 8 rows x 8 elements: K groups 128 B apart, row groups 256 B)
@@ -1148,6 +1167,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
     constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[5 * S + 9];
+    __shared__ int s_ftile[kMaxCtas];  // first tile of each CTA's item range
     __shared__ float s_xb[S][2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
@@ -1196,6 +1216,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
         s_pending = -1;
         fence_mbar_init();
     }
+    for (int c = tid; c < a.G; c += kTcThreads) s_ftile[c] = (int)(((long long)c * a.total / a.G) / a.noct);
     // the sparse B tiles: zero once, only their fixed non-zero positions are rewritten
     for (int s = 0; s < S; s++) {
         uint4* b = reinterpret_cast<uint4*>(smem + (size_t)s * Cfg::kStageBytes + kTcWBytes);
@@ -1364,8 +1385,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) gemv_tc_kernel(const TcArgs a, 
                 const int col = h ? c1 : c0;
                 float v = 0.f;
                 for (long long cc = c_first; cc <= c_last; cc++) {
-                    const long long cb = cc * a.total / a.G;
-                    const long long sl = cc * a.maxseg + (t - cb / a.noct);
+                    const long long sl = cc * a.maxseg + (t - s_ftile[cc]);
                     v += __ldcg(&a.partial[(size_t)sl * kTcTN + col]);
                 }
                 write_y(t, col, v);
@@ -1542,7 +1562,7 @@ static TcPlan tc_plan(int nseg, const int* Ns, int K, int sms, bool xf32, int sf
     p.ntiles = 0;
     for (int i = 0; i < nseg; i++) p.ntiles += (Ns[i] + kTcTN - 1) / kTcTN;
     p.total = (long long)p.ntiles * p.noct;
-    p.G = (int)std::max<long long>(1, std::min<long long>(std::max(sms, 1), p.total));
+    p.G = (int)std::max<long long>(1, std::min<long long>(std::min(std::max(sms, 1), kMaxCtas), p.total));
     const long long lmax = (p.total + p.G - 1) / p.G;
     p.maxseg = (int)((lmax + p.noct - 1) / p.noct + 1);
     p.smem = xf32 ? (sfmt == G4B_SCALE_F16 ? TcCfg<true, G4B_SCALE_F16>::kSmem : TcCfg<true, G4B_SCALE_E4M3>::kSmem)
@@ -1648,6 +1668,61 @@ static int run_tc(const void* x, int x_dtype, int nseg, const g4b_gemv_segment* 
         a.partial = (float*)((char*)workspace + kGemvCounterBytes);
     }
     const int st = dispatch_tc(a, p, wps, scs, x_dtype == G4B_DT_F32, scale_fmt, y_dtype == G4B_DT_F32, s);
+    if (st != G4B_OK) return st;
+    count_launch();
+    return launch_status(op);
+}
+
+// Plan, check the workspace, and launch the M = 1 kernel over `nseg` segments
+// that share x (shapes already validated by the caller; K % 256 == 0).
+static int run_m1(const void* x, int x_dtype, int nseg, const g4b_gemv_segment* segs, int scale_fmt, int y_dtype,
+                  int K, void* workspace, size_t ws_bytes, int sms, cudaStream_t s, const char* op) {
+    int Ns[kTcMaxSeg];
+    for (int i = 0; i < nseg; i++) Ns[i] = segs[i].N;
+    const M1Plan p = m1_plan(nseg, Ns, K, sms, x_dtype == G4B_DT_F32, scale_fmt);
+    G4B_REQUIRE(p.ntiles <= kGemvMaxTiles || p.ws_bytes == 0, G4B_E_SHAPE, "%s: too many columns for a split-K call",
+                op);
+    if (p.ws_bytes) {
+        G4B_REQUIRE(workspace != nullptr && ws_bytes >= p.ws_bytes, G4B_E_WORKSPACE,
+                    "%s: needs %zu bytes of workspace, got %zu", op, p.ws_bytes, workspace ? ws_bytes : 0);
+        G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "%s: workspace must be 16-byte aligned", op);
+    }
+    M1Args a{};
+    a.x = x;
+    TcSeg* dst[kTcMaxSeg] = {&a.seg0, &a.seg1, &a.seg2};
+    const uint32_t* wps[kTcMaxSeg];
+    const void* scs[kTcMaxSeg];
+    int tile0 = 0;
+    for (int i = 0; i < kTcMaxSeg; i++) {
+        if (i < nseg) {
+            dst[i]->y = segs[i].y;
+            dst[i]->inv = segs[i].inv;
+            dst[i]->N = segs[i].N;
+            dst[i]->tile0 = tile0;
+            tile0 += (segs[i].N + kStTN - 1) / kStTN;
+            wps[i] = segs[i].wp;
+            scs[i] = segs[i].scales;
+        } else {
+            *dst[i] = *dst[0];
+            dst[i]->tile0 = 1 << 30;  // never reached
+            wps[i] = segs[0].wp;
+            scs[i] = segs[0].scales;
+        }
+    }
+    a.nseg = nseg;
+    a.K = K;
+    a.noct = p.noct;
+    a.ntiles = p.ntiles;
+    a.G = p.G;
+    a.maxseg = p.maxseg;
+    a.total = p.total;
+    a.stage_bytes = p.stage_bytes;
+    a.s_bytes = p.s_bytes;
+    if (p.ws_bytes) {
+        a.counters = (unsigned*)workspace;
+        a.partial = (float*)((char*)workspace + kGemvCounterBytes);
+    }
+    const int st = dispatch_m1(a, p, wps, scs, x_dtype == G4B_DT_F32, scale_fmt, y_dtype == G4B_DT_F32, s);
     if (st != G4B_OK) return st;
     count_launch();
     return launch_status(op);
@@ -1908,6 +1983,7 @@ size_t g4b_gemv_workspace_bytes(int M, int N, int K, int split) {
     if (check_device(&sms) != G4B_OK) sms = 148;
     clear_error();
     // the activation and scale formats only change the shared-memory layout, not the workspace
+    if (m1_ok(M, N, K, split)) return m1_plan(1, &N, K, sms, true, G4B_SCALE_F16).ws_bytes;
     if (tc_ok(M, N, K, split)) return tc_plan(1, &N, K, sms, true, G4B_SCALE_F16).ws_bytes;
     if (stream_ok(N, K, split)) return stream_plan(M, N, K, split, sms, true, G4B_SCALE_F16).ws_bytes;
     return gemv_plan(M, N, K, split, sms).ws_bytes;
@@ -1959,39 +2035,13 @@ static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, c
     if (st != G4B_OK) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const size_t xe = x_dtype == G4B_DT_F32 ? 4 : 2, ye = y_dtype == G4B_DT_F32 ? 4 : 2;
+    if (m1_ok(M, N, K, split)) {
+        g4b_gemv_segment sg{wp, scales, inv, y, N};
+        return run_m1(x, x_dtype, 1, &sg, scale_fmt, y_dtype, K, workspace, ws_bytes, sms, s, "gemv_i4");
+    }
     if (tc_ok(M, N, K, split)) {
         g4b_gemv_segment sg{wp, scales, inv, y, N};
         return run_tc(x, x_dtype, 1, &sg, scale_fmt, y_dtype, K, workspace, ws_bytes, sms, s, "gemv_i4");
-    }
-    if (m1_ok(M, N, K, split)) {
-        const M1Plan p = m1_plan(N, K, sms, x_dtype == G4B_DT_F32, scale_fmt);
-        if (p.ws_bytes) {
-            G4B_REQUIRE(workspace != nullptr && ws_bytes >= p.ws_bytes, G4B_E_WORKSPACE,
-                        "gemv_i4: needs %zu bytes of workspace, got %zu", p.ws_bytes, workspace ? ws_bytes : 0);
-            G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "gemv_i4: workspace must be 16-byte aligned");
-            G4B_REQUIRE(p.ntiles <= kGemvMaxTiles, G4B_E_SHAPE, "gemv_i4: N=%d too large for a split-K call", N);
-        }
-        M1Args a{};
-        a.x = x;
-        a.y = y;
-        a.inv = inv;
-        a.N = N;
-        a.K = K;
-        a.noct = p.noct;
-        a.ntiles = p.ntiles;
-        a.G = p.G;
-        a.maxseg = p.maxseg;
-        a.total = p.total;
-        a.stage_bytes = p.stage_bytes;
-        a.s_bytes = p.s_bytes;
-        if (p.ws_bytes) {
-            a.counters = (unsigned*)workspace;
-            a.partial = (float*)((char*)workspace + kGemvCounterBytes);
-        }
-        st = dispatch_m1(a, p, wp, scales, x_dtype == G4B_DT_F32, scale_fmt, y_dtype == G4B_DT_F32, s);
-        if (st != G4B_OK) return st;
-        count_launch();
-        return launch_status("gemv_i4");
     }
     if (stream_ok(N, K, split)) {
         const StreamPlan p = stream_plan(M, N, K, split, sms, x_dtype == G4B_DT_F32, scale_fmt);
@@ -2073,6 +2123,7 @@ size_t g4b_gemv_fused_workspace_bytes(int nseg, const int* Ns, int K) {
     int sms = 148;
     if (check_device(&sms) != G4B_OK) sms = 148;
     clear_error();
+    if (K % 256 == 0) return m1_plan(nseg, Ns, K, sms, true, G4B_SCALE_F16).ws_bytes;
     return tc_plan(nseg, Ns, K, sms, true, G4B_SCALE_F16).ws_bytes;
 }
 
@@ -2102,8 +2153,10 @@ int g4b_gemv_i4_fused(const void* x, int x_dtype, int nseg, const g4b_gemv_segme
     int st = check_device(&sms);
     if (st != G4B_OK) return st;
     t_pdl = (flags & G4B_GEMV_PDL) != 0;
-    st = run_tc(x, x_dtype, nseg, segs, scale_fmt, y_dtype, K, workspace, ws_bytes, sms,
-                reinterpret_cast<cudaStream_t>(stream), "gemv_i4_fused");
+    st = K % 256 == 0 ? run_m1(x, x_dtype, nseg, segs, scale_fmt, y_dtype, K, workspace, ws_bytes, sms,
+                               reinterpret_cast<cudaStream_t>(stream), "gemv_i4_fused")
+                      : run_tc(x, x_dtype, nseg, segs, scale_fmt, y_dtype, K, workspace, ws_bytes, sms,
+                               reinterpret_cast<cudaStream_t>(stream), "gemv_i4_fused");
     t_pdl = false;
     return st;
 }
