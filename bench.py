@@ -731,16 +731,25 @@ def run_tp(args):
     stream = torch.cuda.Stream(device)
     ws = torch.zeros(max(ops.gemv_workspace_bytes(1, w.N, w.K, 0) for Lr in layers for w in vars(Lr).values())
                      + ops.gemv_workspace_bytes(1, lm.N, lm.K, 0) + 256, dtype=torch.uint8, device=device)
+    L0 = layers[0]
+    ws_fused = max(ops.gemv_fused_workspace_bytes([L0.q.N, L0.k.N, L0.v.N], L0.q.K),
+                   ops.gemv_fused_workspace_bytes([L0.gate.N, L0.up.N], L0.gate.K))
+    if ws.numel() < ws_fused + 256:
+        ws = torch.zeros(ws_fused + 256, dtype=torch.uint8, device=device)
     launches = [0]
 
     def gemv(x, w, out):
         ops.gemv_i4(x, w, out=out, stream=stream, workspace=ws, pdl=True)
         launches[0] += 1
 
+    def gemv_fused(x, ws_, outs):
+        ops.gemv_i4_fused(x, ws_, outs=outs, stream=stream, workspace=ws, pdl=True)
+        launches[0] += 1
+
     dec = tp.TPDecoder(layers=layers, lm_head=lm, gemv=gemv, all_reduce=lambda t: dist.all_reduce(t),
                        all_gather=lambda out, t: dist.all_gather_into_tensor(out, t),
                        new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=device),
-                       hidden=HIDDEN, vocab=VOCAB, world=world)
+                       hidden=HIDDEN, vocab=VOCAB, world=world, gemv_fused=gemv_fused)
     x = torch.randn((HIDDEN,), generator=gen, device=device)
     with torch.cuda.stream(stream):
         for _ in range(max(1, args.warmup)):
@@ -780,7 +789,7 @@ def run_tp(args):
     dec_k = tp.TPDecoder(layers=layers, lm_head=lm, gemv=gemv, all_reduce=lambda t: None,
                          all_gather=lambda out, t: None,
                          new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=device),
-                         hidden=HIDDEN, vocab=VOCAB, world=world)
+                         hidden=HIDDEN, vocab=VOCAB, world=world, gemv_fused=gemv_fused)
     with torch.cuda.stream(stream):
         dec_k.step(x)
     with torch.cuda.graph(graph_k, stream=stream):
@@ -832,8 +841,9 @@ def run_tp(args):
             "dtype": "int4 x f32 -> f32 acc", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) hidden state)",
             "config": {"workload": "configs[4]: the configs[1] stream tensor-parallel over the GPUs",
                        "scales": args.scales, "layers": args.layers, "parallelism": f"tp{world}",
-                       "sharding": "q/k/v/gate/up/lm_head by output columns, o/down by input rows; 2 NCCL "
-                                   "all-reduces per layer + logits all-gather, inside one CUDA graph",
+                       "sharding": "q/k/v/gate/up/lm_head by output columns, o/down by input rows (256-aligned "
+                                   "shards); q|k|v and gate|up fused launches; 2 NCCL all-reduces per layer + "
+                                   "logits all-gather, inside one CUDA graph",
                        "l2": "working set per GPU > 126 MB L2, no flush needed"},
             "roofline": roofline, "cpu_baseline": None,
             "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": HIDDEN * 4,

@@ -40,12 +40,13 @@ import numpy as np
 
 from .pack import BLK, PackedWeight
 
-# Shard granularity: 64 keeps column shards on whole words and row shards on
-# whole 32-row scale blocks, satisfies the tensor-core GEMV's fast path
-# (N % 32, K % 64), and makes q's (gate's) column split the same ranges as
-# o's (down's) row split, so each rank feeds its own slice forward.
-COL_ALIGN = 64
-ROW_ALIGN = 64
+# Shard granularity: 256 keeps column shards on whole words and row shards on
+# whole 32-row scale blocks, keeps every shard on the GEMV's fastest path
+# (N % 32, K % 256), and makes q's (gate's) column split the same ranges as
+# o's (down's) row split, so each rank feeds its own slice forward.  Shards
+# are balanced in units of 256 (e.g. down's K = 15360 over 8 ranks: 1792 or 2048).
+COL_ALIGN = 256
+ROW_ALIGN = 256
 
 
 def split_range(n: int, world: int, rank: int, align: int) -> tuple[int, int]:
@@ -106,8 +107,10 @@ class TPDecoder:
     """The tensor-parallel decode weight stream of one rank.
 
     gemv(x, w, out) computes out = W x for this rank's shard `w`;
-    all_reduce(t) / all_gather(out, t) are the collectives (in place / into
-    `out`).  Buffers are preallocated once; `step` allocates nothing."""
+    gemv_fused(x, [w...], [out...]), if given, runs the GEMVs that read the
+    same x (q|k|v, gate|up) as one launch; all_reduce(t) / all_gather(out, t)
+    are the collectives (in place / into `out`).  Buffers are preallocated
+    once; `step` allocates nothing."""
     layers: List[TPLayer]
     lm_head: object
     gemv: Callable
@@ -117,6 +120,7 @@ class TPDecoder:
     hidden: int
     vocab: int
     world: int
+    gemv_fused: Optional[Callable] = None
     bufs: dict = field(default_factory=dict)
 
     def __post_init__(self):
@@ -136,15 +140,21 @@ class TPDecoder:
         b = self.bufs
         h = x
         for L in self.layers:
-            self.gemv(h, L.q, b["q"])
-            self.gemv(h, L.k, b["k"])
-            self.gemv(h, L.v, b["v"])
+            if self.gemv_fused is not None:
+                self.gemv_fused(h, [L.q, L.k, L.v], [b["q"], b["k"], b["v"]])
+            else:
+                self.gemv(h, L.q, b["q"])
+                self.gemv(h, L.k, b["k"])
+                self.gemv(h, L.v, b["v"])
             # attention would combine q, k, v here; o consumes this rank's heads
             self.gemv(b["q"], L.o, b["h"])
             self.all_reduce(b["h"])
             h = b["h"]
-            self.gemv(h, L.gate, b["gate"])
-            self.gemv(h, L.up, b["up"])
+            if self.gemv_fused is not None:
+                self.gemv_fused(h, [L.gate, L.up], [b["gate"], b["up"]])
+            else:
+                self.gemv(h, L.gate, b["gate"])
+                self.gemv(h, L.up, b["up"])
             # the gated GELU would combine gate and up here; down consumes this rank's slice
             self.gemv(b["gate"], L.down, b["h"])
             self.all_reduce(b["h"])

@@ -27,7 +27,7 @@ sys.path.insert(0, HERE)
 from g4b import pack, tp  # noqa: E402
 from util import assert_close, weights  # noqa: E402
 
-H, NQ, NKV, FFN, VOCAB, LAYERS = 256, 256, 128, 512, 1024, 2
+H, NQ, NKV, FFN, VOCAB, LAYERS = 512, 1024, 512, 2048, 2048, 2
 
 
 def _shapes():
@@ -67,10 +67,14 @@ def _worker(rank, world, port, q):
         def gemv(x, w, out):
             out.copy_(torch.from_numpy(_oracle_gemv(x.numpy(), w)))
 
+        def gemv_fused(x, ws, outs):
+            for w, o in zip(ws, outs):
+                gemv(x, w, o)
+
         dec = tp.TPDecoder(layers=mine, lm_head=lm_mine, gemv=gemv, all_reduce=lambda t: dist.all_reduce(t),
                            all_gather=lambda out, t: dist.all_gather_into_tensor(out, t),
                            new_buffer=lambda n: torch.zeros(n, dtype=torch.float32), hidden=H, vocab=VOCAB,
-                           world=world)
+                           world=world, gemv_fused=gemv_fused)
         x = torch.from_numpy(np.random.default_rng(5).standard_normal(H).astype(np.float32))
         logits = dec.step(x).numpy().copy()
         if rank == 0:
@@ -111,7 +115,7 @@ def test_tp_decode_world2_matches_unsharded():
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_shard_of_packed_equals_packed_shard(world):
-    N, K = 512, 512
+    N, K = 2048, 2048
     W = weights(N, K, 3)
     full = pack.quant(W, fp8=False, prefill_i8=True)
     for r in range(world):
@@ -127,9 +131,12 @@ def test_shard_of_packed_equals_packed_shard(world):
 
 def test_split_covers_and_rejects():
     for n, world in ((4096, 8), (2048, 8), (15360, 8), (262144, 8), (3840, 2)):
-        spans = [tp.split_range(n, world, r, 64) for r in range(world)]
+        spans = [tp.split_range(n, world, r, 256) for r in range(world)]
         assert spans[0][0] == 0 and spans[-1][1] == n
         assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        assert all((b - a) % 256 == 0 for a, b in spans)
     with pytest.raises(ValueError):
         tp.split_range(96, 2, 0, 64)
+    with pytest.raises(ValueError):
+        tp.split_range(256, 2, 0, 256)   # one unit cannot go to two ranks
     assert tp.validate_world(3840, 4096, 2048, 15360, 262144, 8) is None

@@ -61,10 +61,13 @@ def main():
     def gemv(x, w, out):
         ops.gemv_i4(x, w, out=out, stream=stream, pdl=True)
 
+    def gemv_fused(x, ws, outs):
+        ops.gemv_i4_fused(x, ws, outs=outs, stream=stream, pdl=True)
+
     dec = tp.TPDecoder(layers=mine, lm_head=lm, gemv=gemv, all_reduce=lambda t: dist.all_reduce(t),
                        all_gather=lambda out, t: dist.all_gather_into_tensor(out, t),
                        new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=dev),
-                       hidden=H, vocab=VOCAB, world=world)
+                       hidden=H, vocab=VOCAB, world=world, gemv_fused=gemv_fused)
     x = torch.randn((H,), generator=gen, device=dev)
     with torch.cuda.stream(stream):
         logits = dec.step(x).clone()
