@@ -229,7 +229,7 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="stream", choices=["stream", "gemv"] + list(GEMM_WORKLOADS),
+    ap.add_argument("--workload", default="stream", choices=["stream", "gemv", "prefill"] + list(GEMM_WORKLOADS),
                     help="stream: configs[1] decode weight stream (default); gemv: configs[0] single GEMV; "
                          "gemm_i4 / gemm_i4_down: configs[2] W4A16 prefill GEMM; w8a8 / w4a8: configs[3]")
     ap.add_argument("--unfused", action="store_true",
@@ -241,6 +241,8 @@ def main():
     args = ap.parse_args()
     if args.workload in GEMM_WORKLOADS:
         return run_gemm(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
     if args.workload == "stream" and int(os.environ.get("WORLD_SIZE", "1")) > 1 and args.parallel != "replicas":
         return run_tp(args)
     fp8 = args.scales == "fp8"
@@ -670,6 +672,124 @@ def run_gemm(args):
                           "e2e": {"value": round(e2e, 1), "unit": unit, "h2d_bytes_per_step": M * K * 2,
                                   "d2h_bytes_per_step": M * N * 2},
                           "gpu_launches": n * (1 if kind == "w4a16" else 2), "clocks": clk}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------ prefill over M
+PREFILL_M = 8192
+
+
+def run_prefill(args):
+    """configs[4] prefill: M = 8192 f16 N(0, 1) tokens through the 48 layers'
+    seven W4A16 GEMMs (the stack of configs[1], f16 scales), the M rows split
+    over the ranks with the weights replicated (no collective).  value =
+    total 2*M*N*K of the stack / device time of the step (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from g4b import _lib as L
+    from g4b import ops, tp
+    from g4b import quant_gpu as qz
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    L.load()
+    m0, m1 = tp.prefill_rows(PREFILL_M, world, rank)
+    Mr = m1 - m0
+    gen = torch.Generator(device=device)
+    gen.manual_seed(0)
+    layers = []
+    for _ in range(args.layers):
+        d = []
+        for name, N, K in LAYER_SHAPES:
+            W = torch.randn((N, K), generator=gen, device=device).mul_(0.02)
+            d.append((name, qz.quant_device(W, pf=False, fp8=False, prefill_i8=False)))
+            del W
+        layers.append(d)
+    # the rank's rows of the activations of each input width, and one output per output width
+    X = {K: torch.randn((PREFILL_M, K), generator=gen, device=device).to(torch.float16)[m0:m1].contiguous()
+         for K in (HIDDEN, NQ, FFN)}
+    Y = {N: torch.empty((Mr, N), dtype=torch.float16, device=device) for N in (NQ, NKV, HIDDEN, FFN)}
+    flops = 2 * PREFILL_M * sum(N * K for _, N, K in LAYER_SHAPES) * args.layers
+    stream = torch.cuda.Stream(device)
+
+    def step():
+        for d in layers:
+            for name, w in d:
+                ops.gemm_i4(X[w.K], w, out=Y[w.N], stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = flops / (ms / 1e3) / 1e12
+    peak, src = 1590.0, "of fallback"
+    try:
+        peak, src = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["bf16_tflops"]), "of measured"
+    except Exception:
+        pass
+    # e2e: this rank's f16 activations in from pinned host memory, the last output back, every step
+    Xh = {K: x.cpu().pin_memory() for K, x in X.items()}
+    Yh = torch.empty(Y[HIDDEN].shape, dtype=torch.float16).pin_memory()
+    if world > 1:
+        dist.barrier()
+    with torch.cuda.stream(stream):
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            for K, x in X.items():
+                x.copy_(Xh[K], non_blocking=True)
+            step()
+            Yh.copy_(Y[HIDDEN], non_blocking=True)
+            stream.synchronize()
+        e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"W4A16 prefill GEMM TFLOP/s (48-layer stack, M={PREFILL_M} split over GPUs)",
+            "value": round(value, 1), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 x f16 -> f32 acc",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) f16 activations)",
+            "config": {"workload": "configs[4] prefill: M=8192 rows split over the GPUs, weights replicated",
+                       "layers": args.layers, "rows_per_gpu": Mr, "parallelism": f"m-split{world}",
+                       "l2": "working set per GPU > 126 MB L2"},
+            "roofline": {"bound": "tensor", "achieved": round(value / world, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(value / world / peak, 4), "traffic": None, "peak_source": src,
+                         "kernel": "gemm_w4a16_kernel (per GPU)"},
+            "cpu_baseline": None,
+            "e2e": {"value": round(flops * args.steps / e2e_s / 1e12, 1), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": world * sum(x.numel() * 2 for x in X.values()),
+                    "d2h_bytes_per_step": world * Yh.numel() * 2},
+            "gpu_launches": 7 * args.layers * args.steps, "clocks": clk}), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

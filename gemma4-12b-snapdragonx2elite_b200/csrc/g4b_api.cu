@@ -183,7 +183,7 @@ long long g4b_query(int what) {
         case G4B_Q_FAULT_COUNTER: return g4b::g_fault_calls.load();
         case G4B_Q_KERNEL_STATUS: {
             if (g4b::check_device(nullptr) != G4B_OK) return -1;
-            return (long long)(g4b::read_status_gemv() | g4b::read_status_gemm());
+            return (long long)(g4b::read_status_gemv() | g4b::read_status_gemm() | g4b::read_status_comm());
         }
         default: return -1;
     }

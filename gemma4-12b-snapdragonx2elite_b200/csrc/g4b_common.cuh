@@ -29,6 +29,7 @@ int launch_status(const char* op);
 // gave up); 0 = clean.
 unsigned read_status_gemv();
 unsigned read_status_gemm();
+unsigned read_status_comm();
 // f32 -> f16 (RNE) launched on `s` (the GEMMs' cast_dn step).
 int cast_f32_to_f16_async(const float* src, __half* dst, size_t n, cudaStream_t s);
 

@@ -67,6 +67,13 @@ SIGNATURES = {
     "g4b_quant_w8a8": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
     "g4b_gemm_i4_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g4b_gemm_i4": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "g4b_allreduce_buffer_bytes": (_Z, [_I, _I]),
+    "g4b_allreduce_f32": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
+    "g4b_comm_alloc": (_I, [_Z, C.POINTER(_P)]),
+    "g4b_comm_free": (_I, [_P]),
+    "g4b_ipc_handle": (_I, [_P, _P]),
+    "g4b_ipc_open": (_I, [_P, C.POINTER(_P)]),
+    "g4b_ipc_close": (_I, [_P]),
     "g4b_gemm_w8a8": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _P]),
     "g4b_gemm_w4a8": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _P]),
 }

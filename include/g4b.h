@@ -278,6 +278,37 @@ G4B_API int g4b_gemm_w4a8(const int8_t* A8, const uint32_t* wp, const uint16_t* 
                           const uint16_t* sw_f16, void* Y, int y_dtype, int32_t* C_debug,
                           int M, int N, int K, g4b_stream_t stream);
 
+/* ------------------------------------------------------------ tensor parallel */
+/* The all-reduce after the row-parallel o and down GEMVs of a tensor-parallel
+ * decode -- the cross-GPU counterpart of vk/reduce.comp:8-12 (the reference
+ * runs on one GPU and has no collective).  One kernel, over NVLink peer
+ * memory: each rank stores x into slot [rank] of every rank's exchange buffer,
+ * raises a flag there (release, system scope), waits for all flags in its own
+ * buffer (acquire; bounded, 2 s, then the kernel status word is raised) and
+ * writes y = the slots summed in rank order, identical bits on every rank.
+ * In-place (x == y) is allowed.  For the 15 KB per-layer reductions of a
+ * batch-1 decode this is latency-bound, where NCCL's general algorithms are not
+ * tuned for it.
+ *   bufs_dev  device array of `world` pointers: bufs_dev[r] = rank r's exchange
+ *             buffer of g4b_allreduce_buffer_bytes(world, n) bytes, from
+ *             g4b_comm_alloc (zero-filled), mapped into this process with
+ *             g4b_ipc_open (own buffer: its own pointer)
+ *   counter   this rank's device u32 call counter (zero-filled once); every rank
+ *             makes the same calls in the same order (stream order, graphs too)
+ * 1 <= world <= 8; n % 4 == 0 gives vectorised stores. */
+G4B_API size_t g4b_allreduce_buffer_bytes(int world, int n);
+G4B_API int g4b_allreduce_f32(const float* x, float* y, int n, int rank, int world, void* const* bufs_dev,
+                              unsigned* counter, g4b_stream_t stream);
+
+/* Setup-time helpers for the exchange buffers (never on the hot path):
+ * cudaMalloc + zero fill, cudaFree, and CUDA IPC export / import / close
+ * (a handle is 64 bytes). */
+G4B_API int g4b_comm_alloc(size_t bytes, void** dptr);
+G4B_API int g4b_comm_free(void* dptr);
+G4B_API int g4b_ipc_handle(const void* dptr, void* handle64);
+G4B_API int g4b_ipc_open(const void* handle64, void** dptr);
+G4B_API int g4b_ipc_close(void* dptr);
+
 #ifdef __cplusplus
 }
 #endif
