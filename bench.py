@@ -232,6 +232,9 @@ def main():
     ap.add_argument("--workload", default="stream", choices=["stream", "gemv", "prefill"] + list(GEMM_WORKLOADS),
                     help="stream: configs[1] decode weight stream (default); gemv: configs[0] single GEMV; "
                          "gemm_i4 / gemm_i4_down: configs[2] W4A16 prefill GEMM; w8a8 / w4a8: configs[3]")
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+                    help="tensor-parallel stream: the per-layer all-reduce as one kernel over NVLink peer memory "
+                         "(g4b_allreduce_f32, default) or NCCL's")
     ap.add_argument("--unfused", action="store_true",
                     help="stream: launch all 337 GEMVs separately, each on its own x, instead of fusing "
                          "q|k|v and gate|up (which read the same x in a decode step)")
@@ -807,7 +810,7 @@ def run_tp(args):
     import torch.distributed as dist
     from datetime import timedelta
     from g4b import _lib as L
-    from g4b import ops, tp
+    from g4b import comm, ops, tp
     from g4b import quant_gpu as qz
 
     fp8 = args.scales == "fp8"
@@ -866,7 +869,15 @@ def run_tp(args):
         ops.gemv_i4_fused(x, ws_, outs=outs, stream=stream, workspace=ws, pdl=True)
         launches[0] += 1
 
-    dec = tp.TPDecoder(layers=layers, lm_head=lm, gemv=gemv, all_reduce=lambda t: dist.all_reduce(t),
+    peer = comm.PeerAllReduce(HIDDEN, device) if args.allreduce == "peer" else None
+    def all_reduce(t):
+        if peer is not None:
+            peer(t, stream=stream)
+            launches[0] += 1          # g4b's own all-reduce kernel
+        else:
+            dist.all_reduce(t)
+
+    dec = tp.TPDecoder(layers=layers, lm_head=lm, gemv=gemv, all_reduce=all_reduce,
                        all_gather=lambda out, t: dist.all_gather_into_tensor(out, t),
                        new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=device),
                        hidden=HIDDEN, vocab=VOCAB, world=world, gemv_fused=gemv_fused)
@@ -962,8 +973,9 @@ def run_tp(args):
             "config": {"workload": "configs[4]: the configs[1] stream tensor-parallel over the GPUs",
                        "scales": args.scales, "layers": args.layers, "parallelism": f"tp{world}",
                        "sharding": "q/k/v/gate/up/lm_head by output columns, o/down by input rows (256-aligned "
-                                   "shards); q|k|v and gate|up fused launches; 2 NCCL all-reduces per layer + "
-                                   "logits all-gather, inside one CUDA graph",
+                                   "shards); q|k|v and gate|up fused launches; 2 all-reduces per layer + "
+                                   "logits all-gather (NCCL), inside one CUDA graph",
+                       "allreduce": "g4b_allreduce_f32 over NVLink peer memory" if peer is not None else "NCCL",
                        "l2": "working set per GPU > 126 MB L2, no flush needed"},
             "roofline": roofline, "cpu_baseline": None,
             "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": HIDDEN * 4,
@@ -972,6 +984,8 @@ def run_tp(args):
             "bytes_per_gpu_max": int(mb.item()), "ms_per_step_kernels_only": round(ms_kern, 4)}), flush=True)
     del graph, graph_k
     dist.barrier()
+    if peer is not None:
+        peer.close()
     dist.destroy_process_group()
 
 

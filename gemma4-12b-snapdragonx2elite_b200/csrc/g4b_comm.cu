@@ -49,7 +49,7 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-__global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(const float* __restrict__ x, float* y, int n,
+__global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(const float* x, float* y, int n,
                                                                   int rank, int world, void* const* bufs,
                                                                   unsigned* counter) {
     __shared__ unsigned s_epoch;

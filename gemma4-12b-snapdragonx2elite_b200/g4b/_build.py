@@ -50,11 +50,27 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> str:
-    """Compile the library if any source is newer than it; return its path."""
+    """Compile the library if any source is newer than it; return its path.
+
+    Processes that load the library at the same time (one per GPU rank) build
+    it at most once: the build holds an exclusive lock on a file in the build
+    directory and re-checks freshness once it has the lock."""
     if not force and up_to_date():
         return LIB_PATH
-    nvcc = nvcc_path()
+    import fcntl
     os.makedirs(BUILD_DIR, exist_ok=True)
+    with open(os.path.join(BUILD_DIR, ".lock"), "w") as lockf:
+        fcntl.flock(lockf, fcntl.LOCK_EX)
+        try:
+            if not force and up_to_date():
+                return LIB_PATH
+            return _build_locked(verbose, ptxas_verbose)
+        finally:
+            fcntl.flock(lockf, fcntl.LOCK_UN)
+
+
+def _build_locked(verbose: bool, ptxas_verbose: bool) -> str:
+    nvcc = nvcc_path()
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
 
     def compile_one(src: str) -> tuple[str, str]:

@@ -27,11 +27,13 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("fp8", [False, True])
-def test_tp_decode_two_gpus(fp8):
+@pytest.mark.parametrize("fp8,allreduce", [(False, "nccl"), (True, "nccl"), (False, "peer")])
+def test_tp_decode_two_gpus(fp8, allreduce):
+    """allreduce="peer" also checks g4b_allreduce_f32 on its own: identical bits
+    on both ranks, equal to NCCL's sum, across repeated calls."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    env = dict(os.environ, TP_FP8="1" if fp8 else "0")
+    env = dict(os.environ, TP_FP8="1" if fp8 else "0", TP_ALLREDUCE=allreduce)
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
            os.path.join(HERE, "tp_worker.py")]

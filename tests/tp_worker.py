@@ -16,7 +16,7 @@ sys.path.insert(0, os.path.join(ROOT, "gemma4-12b-snapdragonx2elite_b200"))
 sys.path.insert(0, HERE)
 
 from g4b import _lib as L  # noqa: E402
-from g4b import ops, tp  # noqa: E402
+from g4b import comm, ops, tp  # noqa: E402
 from g4b import quant_gpu as qz  # noqa: E402
 from util import assert_close  # noqa: E402
 
@@ -32,6 +32,25 @@ def main():
     dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
     L.load()
     fp8 = os.environ.get("TP_FP8") == "1"
+    use_peer = os.environ.get("TP_ALLREDUCE", "nccl") == "peer"
+    peer = comm.PeerAllReduce(H, dev) if use_peer else None
+    if peer is not None:
+        # the peer all-reduce alone: identical bits on every rank, equal to NCCL's two-rank sum
+        a = torch.randn((H,), generator=torch.Generator(device=dev).manual_seed(100 + rank), device=dev)
+        ref = a.clone()
+        dist.all_reduce(ref)
+        got = peer(a.clone())
+        for _ in range(3):                       # repeated calls alternate the buffer halves
+            got2 = peer(a.clone())
+        torch.cuda.synchronize()
+        allg = [torch.empty_like(got) for _ in range(world)]
+        dist.all_gather(allg, got)
+        ok_ar = all(torch.equal(allg[0], g_) for g_ in allg) and torch.equal(got, got2)
+        if world == 2:
+            ok_ar = ok_ar and torch.equal(got, ref)
+        if not ok_ar:
+            print("peer all-reduce mismatch", flush=True)
+            sys.exit(1)
     gen = torch.Generator(device=dev)
     gen.manual_seed(0)
     shapes = {"q": (NQ, H), "k": (NKV, H), "v": (NKV, H), "o": (H, NQ), "gate": (FFN, H), "up": (FFN, H),
@@ -64,7 +83,8 @@ def main():
     def gemv_fused(x, ws, outs):
         ops.gemv_i4_fused(x, ws, outs=outs, stream=stream, pdl=True)
 
-    dec = tp.TPDecoder(layers=mine, lm_head=lm, gemv=gemv, all_reduce=lambda t: dist.all_reduce(t),
+    all_reduce = (lambda t: peer(t, stream=stream)) if peer is not None else (lambda t: dist.all_reduce(t))
+    dec = tp.TPDecoder(layers=mine, lm_head=lm, gemv=gemv, all_reduce=all_reduce,
                        all_gather=lambda out, t: dist.all_gather_into_tensor(out, t),
                        new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=dev),
                        hidden=H, vocab=VOCAB, world=world, gemv_fused=gemv_fused)
@@ -91,6 +111,8 @@ def main():
             ok.zero_()
     dist.broadcast(ok, 0)
     del g
+    if peer is not None:
+        peer.close()
     dist.destroy_process_group()
     sys.exit(0 if ok.item() == 1 else 1)
 
