@@ -235,6 +235,10 @@ def main():
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="tensor-parallel stream: the per-layer all-reduce as one kernel over NVLink peer memory "
                          "(g4b_allreduce_f32, default) or NCCL's")
+    ap.add_argument("--schedule", default="launches", choices=["chain", "launches"],
+                    help="stream: launches (default) runs one launch per (fused) GEMV, chained by programmatic "
+                         "dependent launch; chain runs the token's GEMVs as one persistent launch "
+                         "(g4b_gemv_chain: each step waits for every tile of the step before it)")
     ap.add_argument("--unfused", action="store_true",
                     help="stream: launch all 337 GEMVs separately, each on its own x, instead of fusing "
                          "q|k|v and gate|up (which read the same x in a decode step)")
@@ -323,7 +327,26 @@ def main():
                    else ops.gemv_workspace_bytes(1, ns[0], ws_list[g[0]].K, 0))
     ws = torch.zeros(need + 256, dtype=torch.uint8, device=device)
 
+    use_chain = args.workload == "stream" and args.schedule == "chain"
+    chain = None
+    if use_chain:
+        # the token's GEMVs as one persistent launch; step j waits for every
+        # tile of step j-1 (the command buffer's barrier) before it reads x
+        chain = ops.GemvChain([(x, [ws_list[i] for i in g], [ys[i] for i in g]) for g, x in zip(groups, xs)])
+        config["schedule"] = (f"one persistent launch per token (g4b_gemv_chain) of {len(groups)} GEMV steps "
+                              f"({'fused q|k|v and gate|up' if not args.unfused else 'unfused'}); each step "
+                              "starts reading x once every tile of the step before it is written")
+    # event groups: one pair of events per launch
+    ev_groups = [list(range(len(ws_list)))] if use_chain else groups
+
     def step(gev=None):
+        if use_chain:
+            if gev is not None:
+                gev.record(0, sh)
+            chain.run(stream)
+            if gev is not None:
+                gev.record(1, sh)
+            return
         for gi, (g, x) in enumerate(zip(groups, xs)):
             if gev is not None:
                 gev.record(2 * gi, sh)
@@ -343,7 +366,7 @@ def main():
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
-    gev = GraphEvents(len(groups))
+    gev = GraphEvents(len(ev_groups))
     graph_ev = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph_ev, stream=stream):
         step(gev)
@@ -379,7 +402,7 @@ def main():
     barrier()
     ms = e0.elapsed_time(e1)
     ms = max_over_ranks(ms)
-    launches_per_step = len(groups)
+    launches_per_step = len(ev_groups)
     ms_step = ms / args.steps
     value = world * step_bytes / (ms_step / 1e3) / 1e9
 
@@ -391,13 +414,17 @@ def main():
         for _ in range(args.steps):
             graph_ev.replay()
             stream.synchronize()
-            for gi, g in enumerate(groups):
+            for gi, g in enumerate(ev_groups):
                 d = gev.elapsed_ms(2 * gi, 2 * gi + 1)
-                K = ws_list[g[0]].K
-                gb = sum(weight_bytes(ws_list[i].N, K, fp8) + 2 * ws_list[i].N for i in g) + 2 * K
                 kern_ms += d
+                if use_chain:
+                    gb = step_bytes
+                    key = f"chain of {len(groups)} steps"
+                else:
+                    K = ws_list[g[0]].K
+                    gb = sum(weight_bytes(ws_list[i].N, K, fp8) + 2 * ws_list[i].N for i in g) + 2 * K
+                    key = "+".join(str(ws_list[i].N) for i in g) + f"x{K}"
                 kern_bytes += gb
-                key = "+".join(str(ws_list[i].N) for i in g) + f"x{K}"
                 a = per_shape.setdefault(key, [0.0, 0, gb])
                 a[0] += d
                 a[1] += 1
@@ -413,15 +440,19 @@ def main():
         peak_src = "of fallback"
     roofline = {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(kern_gbs / peak, 4), "traffic": None, "peak_source": peak_src,
-                "kernel": "gemv_tc_kernel", "launches_timed": args.steps * len(groups),
-                "avg_launch_us": round(kern_ms * 1e3 / (args.steps * len(groups)), 3),
+                "kernel": "gemv_i4_m1_kernel<CHAIN>" if use_chain else "gemv_i4_m1_kernel",
+                "launches_timed": args.steps * len(ev_groups),
+                "avg_launch_us": round(kern_ms * 1e3 / (args.steps * len(ev_groups)), 3),
                 "per_shape_gbs": {k: round(v[2] * v[1] / (v[0] / 1e3) / 1e9, 1) for k, v in per_shape.items()},
                 "graph_vs_kernels": round(ms_step / (kern_ms / args.steps), 4)}
     tp = os.path.join(REPO, "profiles", "gemv_traffic.json")
     if os.path.exists(tp):
         try:
             t = json.load(open(tp))
-            roofline["traffic"] = t.get("bytes_per_launch_scaled", {}).get(args.workload)
+            if use_chain:
+                roofline["traffic"] = int(round(t["traffic_ratio"] * step_bytes))
+            else:
+                roofline["traffic"] = t.get("bytes_per_launch_scaled", {}).get(args.workload)
             roofline["traffic_note"] = t.get("note")
         except Exception:
             pass
@@ -482,7 +513,10 @@ def main():
                "gpu_launches": launches_per_step * args.steps, "clocks": clk,
                "bytes_per_step": step_bytes}
         print(json.dumps(out), flush=True)
-    del graph
+    del graph, graph_ev
+    if chain is not None:
+        torch.cuda.synchronize()
+        chain.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -872,7 +906,7 @@ def run_tp(args):
     peer = comm.PeerAllReduce(HIDDEN, device) if args.allreduce == "peer" else None
     def all_reduce(t):
         if peer is not None:
-            peer(t, stream=stream)
+            peer(t, stream=stream, pdl=True)
             launches[0] += 1          # g4b's own all-reduce kernel
         else:
             dist.all_reduce(t)
@@ -946,7 +980,7 @@ def run_tp(args):
     per_gpu_kern = float(mb.item()) / (ms_kern / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(per_gpu_kern, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(per_gpu_kern / peak, 4), "traffic": None, "peak_source": src,
-                "kernel": "gemv_tc_kernel (per GPU, collectives removed)",
+                "kernel": "gemv_i4_m1_kernel (per GPU, collectives removed)",
                 "kernels_only_aggregate_gbs": round(full_bytes / (ms_kern / 1e3) / 1e9, 1)}
 
     # e2e: hidden state in from pinned host memory, gathered logits back, every step

@@ -114,16 +114,16 @@ int check_device(int* sm_count) {
 struct TmapKey {
     uintptr_t base;
     uint64_t dim0, dim1, stride1;
-    uint32_t box0, box1, dtype, swizzle;
+    uint32_t box0, box1, dtype, swizzle, promo;
     bool operator==(const TmapKey& o) const {
         return base == o.base && dim0 == o.dim0 && dim1 == o.dim1 && stride1 == o.stride1 && box0 == o.box0 &&
-               box1 == o.box1 && dtype == o.dtype && swizzle == o.swizzle;
+               box1 == o.box1 && dtype == o.dtype && swizzle == o.swizzle && promo == o.promo;
     }
 };
 struct TmapKeyHash {
     size_t operator()(const TmapKey& k) const {
         size_t h = std::hash<uint64_t>()(k.base);
-        for (uint64_t v : {k.dim0, k.dim1, k.stride1, (uint64_t)k.box0 << 32 | k.box1, (uint64_t)k.dtype << 8 | k.swizzle})
+        for (uint64_t v : {k.dim0, k.dim1, k.stride1, (uint64_t)k.box0 << 32 | k.box1, (uint64_t)k.dtype << 16 | k.swizzle << 8 | k.promo})
             h = h * 1000003u ^ std::hash<uint64_t>()(v);
         return h;
     }
@@ -133,8 +133,10 @@ static std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> g_tmaps;
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
-                  uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle) {
-    TmapKey key{(uintptr_t)base, dim0, dim1, stride1_bytes, box0, box1, (uint32_t)dtype, (uint32_t)swizzle};
+                  uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle,
+                  CUtensorMapL2promotion promo) {
+    TmapKey key{(uintptr_t)base, dim0, dim1, stride1_bytes, box0, box1, (uint32_t)dtype, (uint32_t)swizzle,
+                (uint32_t)promo};
     std::lock_guard<std::mutex> lk(g_tmap_mu);
     auto it = g_tmaps.find(key);
     if (it != g_tmaps.end()) {
@@ -155,7 +157,7 @@ int tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base,
     const cuuint32_t estr[2] = {1, 1};
     CUtensorMap m;
     CUresult r = g_encode(&m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                          swizzle, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(G4B_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     if (g_tmaps.size() > 8192) g_tmaps.clear();
     g_tmaps.emplace(key, m);

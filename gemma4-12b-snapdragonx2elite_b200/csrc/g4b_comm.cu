@@ -4,17 +4,22 @@
 // After the row-parallel o and down GEMVs every rank holds a partial hidden
 // state (3840 f32 = 15 KB) that the ranks must sum: the cross-GPU counterpart
 // of vk/reduce.comp:8-12.  At this size a collective is pure latency, so one
-// kernel does it in one shot:
-//   1. every rank stores its partial into slot [rank] of every rank's exchange
-//      buffer (plain P2P stores over NVLink; the buffers are CUDA-IPC mapped);
-//   2. a system-scope fence, then a release store of the call's epoch into
-//      flag [rank] of every rank's buffer;
-//   3. each rank waits (bounded) until all `world` flags of its own buffer
-//      carry the epoch, and
-//   4. adds the `world` slots in rank order -- every rank gets the same bits.
-// Two buffer halves alternate by epoch parity: a rank can be at most one call
-// ahead of any other (it cannot pass call e+1 before every rank has finished
-// call e), so it never overwrites a half that a peer is still reading.
+// small kernel does it in one shot, with no fence and no separate flag:
+//   1. every rank stores each element of its partial, paired with the call's
+//      epoch in one 64-bit word {f32 bits, epoch}, into slot [rank] of every
+//      rank's exchange buffer (plain P2P stores over NVLink into CUDA-IPC
+//      mapped buffers).  A 64-bit aligned store is single-copy atomic, so a
+//      reader that sees the epoch also sees the value that came with it;
+//   2. each thread polls its own elements of all `world` slots in its own
+//      buffer until every word carries the epoch (bounded), and
+//   3. adds the slots in rank order -- every rank gets the same bits.
+// Two buffer halves alternate by epoch parity.  A rank can be at most one call
+// ahead of any other: it cannot finish call e before every rank has started
+// call e, and a rank starts call e only after its call e-1 kernel finished
+// (the kernel waits for its predecessor in the stream before it stores
+// anything), so no rank overwrites a half that a peer is still reading.
+// With programmatic dependent launch the next kernel in the stream may start
+// (and e.g. prefetch weights) while this one waits for the peers.
 // No multicast object, no TMA: only ordinary loads and stores to peer memory.
 #include <cstring>
 
@@ -31,86 +36,66 @@ unsigned read_status_comm() {
     return v;
 }
 
-constexpr int kArThreads = 512;
+constexpr int kArThreads = 256;  // small enough to share an SM with a GEMV CTA
 constexpr int kArMaxWorld = 8;
 
-// Exchange buffer of one rank: [2 halves][world][n] f32 slots, then [2][world]
-// u32 flags (16-byte aligned).
-__host__ __device__ inline size_t ar_slots_bytes(int world, int n) {
-    return (((size_t)2 * world * n * sizeof(float)) + 15) & ~(size_t)15;
+// Exchange buffer of one rank: [2 halves][world][n] 64-bit words {f32, epoch}.
+__host__ __device__ inline size_t ar_buffer_bytes(int world, int n) {
+    return (size_t)2 * world * n * sizeof(unsigned long long);
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-__global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(const float* x, float* y, int n,
-                                                                  int rank, int world, void* const* bufs,
-                                                                  unsigned* counter) {
-    __shared__ unsigned s_epoch;
-    __shared__ int s_ok;
+__global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(const float* x, float* y, int n, int rank,
+                                                                  int world, void* const* bufs, unsigned* counter) {
     const int tid = threadIdx.x;
-    if (tid == 0) {
-        s_epoch = *counter + 1u;
-        s_ok = 1;
-    }
-    __syncthreads();
-    const unsigned epoch = s_epoch;
+    pdl_wait();  // x is the previous kernel's output; nothing is stored before it completed
+    const unsigned epoch = *counter + 1u;
     const int half = (int)(epoch & 1u);
-    const size_t sb = ar_slots_bytes(world, n);
-    // 1. this rank's partial into slot [rank] of every rank's buffer (vectorised when n % 4 == 0)
-    for (int p = 0; p < world; p++) {
-        float* dst = reinterpret_cast<float*>(bufs[p]) + ((size_t)half * world + rank) * n;
-        if ((n & 3) == 0) {
-            const float4* s4 = reinterpret_cast<const float4*>(x);
-            float4* d4 = reinterpret_cast<float4*>(dst);
-            for (int i = tid; i < n / 4; i += kArThreads) d4[i] = s4[i];
-        } else {
-            for (int i = tid; i < n; i += kArThreads) dst[i] = x[i];
-        }
-    }
-    __threadfence_system();  // each thread's stores, at system scope
-    __syncthreads();
-    // 2. publish: raise this rank's flag in every rank's buffer (release, system scope)
-    if (tid == 0) {
+    const unsigned long long tag = (unsigned long long)epoch << 32;
+    // 1. this rank's partial, tagged, into slot [rank] of every rank's buffer
+    for (int i = tid; i < n; i += kArThreads) {
+        const unsigned long long w = tag | __float_as_uint(x[i]);
         for (int p = 0; p < world; p++) {
-            unsigned* flags = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(bufs[p]) + sb);
-            st_release_sys(flags + half * world + rank, epoch);
+            unsigned long long* dst = reinterpret_cast<unsigned long long*>(bufs[p]) + ((size_t)half * world + rank) * n;
+            st_relaxed_sys_u64(dst + i, w);
         }
     }
-    // 3. wait for every rank's flag in this rank's own buffer (bounded)
-    if (tid < world) {
-        const unsigned* flags = reinterpret_cast<const unsigned*>(reinterpret_cast<const uint8_t*>(bufs[rank]) + sb);
-        const unsigned* f = flags + half * world + tid;
-        if (ld_acquire_sys(f) != epoch) {
-            const uint64_t t0 = global_ns();
-            while (ld_acquire_sys(f) != epoch) {
+    pdl_launch_dependents();
+    __syncthreads();
+    // 2-3. poll this rank's own buffer until every slot of this thread's elements
+    // carries the epoch (bounded), and sum in rank order
+    const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(bufs[rank]) + (size_t)half * world * n;
+    uint64_t t0 = 0;
+    bool ok = true;
+    for (int i = tid; i < n && ok; i += kArThreads) {
+        float v = 0.f;
+        for (int r = 0; r < world && ok; r++) {
+            const unsigned long long* src = mine + (size_t)r * n + i;
+            unsigned long long w = ld_relaxed_sys_u64(src);
+            while ((unsigned)(w >> 32) != epoch) {
+                if (t0 == 0) t0 = global_ns();
                 if (global_ns() - t0 > kWaitLimitNs) {
                     atomicOr(&g_comm_status, kStatusTimeout);
-                    s_ok = 0;
+                    ok = false;
                     break;
                 }
-                __nanosleep(64);
+                __nanosleep(32);
+                w = ld_relaxed_sys_u64(src);
             }
+            v += __uint_as_float((unsigned)w);
         }
+        if (ok) y[i] = v;
     }
     __syncthreads();
-    // 4. sum the slots in rank order (identical on every rank)
-    if (s_ok) {
-        const float* mine = reinterpret_cast<const float*>(bufs[rank]) + (size_t)half * world * n;
-        for (int i = tid; i < n; i += kArThreads) {
-            float v = 0.f;
-            for (int r = 0; r < world; r++) v += __ldcv(mine + (size_t)r * n + i);
-            y[i] = v;
-        }
-    }
-    __syncthreads();
-    if (tid == 0) *counter = epoch;
+    if (tid == 0) *counter = epoch;  // the next call's epoch, also after a timeout
 }
 
 }  // namespace g4b
@@ -120,22 +105,35 @@ using namespace g4b;
 extern "C" {
 
 size_t g4b_allreduce_buffer_bytes(int world, int n) {
-    if (world < 1 || world > kArMaxWorld || n < 1) return 0;
-    return ar_slots_bytes(world, n) + (size_t)2 * world * sizeof(unsigned);
+    if (world < 1 || world > kArMaxWorld || n < 1 || n > (1 << 24)) return 0;
+    return ar_buffer_bytes(world, n);
 }
 
 int g4b_allreduce_f32(const float* x, float* y, int n, int rank, int world, void* const* bufs_dev, unsigned* counter,
-                      g4b_stream_t stream) {
+                      unsigned flags, g4b_stream_t stream) {
     G4B_ENTRY("allreduce_f32");
+    G4B_REQUIRE((flags & ~(unsigned)G4B_GEMV_PDL) == 0, G4B_E_ARG, "allreduce_f32: unknown flags 0x%x", flags);
     G4B_REQUIRE(x && y && bufs_dev && counter, G4B_E_ARG, "allreduce_f32: NULL pointer");
     G4B_REQUIRE(world >= 1 && world <= kArMaxWorld && rank >= 0 && rank < world, G4B_E_ARG,
                 "allreduce_f32: rank %d / world %d (1..%d ranks)", rank, world, kArMaxWorld);
     G4B_REQUIRE(n >= 1 && n <= (1 << 24), G4B_E_SHAPE, "allreduce_f32: n=%d", n);
-    G4B_REQUIRE(aligned16(x) && aligned16(y), G4B_E_ALIGN, "allreduce_f32: x and y must be 16-byte aligned");
+    G4B_REQUIRE(((uintptr_t)x & 3u) == 0 && ((uintptr_t)y & 3u) == 0, G4B_E_ALIGN,
+                "allreduce_f32: x and y must be 4-byte aligned");
     int st = check_device(nullptr);
     if (st != G4B_OK) return st;
-    allreduce_f32_kernel<<<1, kArThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(x, y, n, rank, world, bufs_dev,
-                                                                                       counter);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(kArThreads);
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    if (flags & G4B_GEMV_PDL) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, allreduce_f32_kernel, x, y, n, rank, world, bufs_dev, counter);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "allreduce_f32: launch: %s", cudaGetErrorString(e));
     count_launch();
     return launch_status("allreduce_f32");
 }

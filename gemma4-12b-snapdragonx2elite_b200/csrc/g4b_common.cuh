@@ -37,10 +37,15 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // A 2-D tiled TMA descriptor for a row-major [dim1, dim0] array (dim0
 // innermost, rows stride1_bytes apart) with a box of [box1, box0] elements.
-// Encoded once per distinct argument set and cached (the encoding is a pure
-// function of its inputs); returns G4B_OK or an error status.
+// `promo` is the L2 fill size of the box's row segments: the GEMV weight
+// boxes are 128 bytes wide and read once, so they use 128-byte fills (a
+// 256-byte fill would also fetch the neighbouring column strip, which another
+// CTA reads much later, after L2 has evicted it: 1.36x the bytes from DRAM on
+// the lm_head GEMV).  Encoded once per distinct argument set and cached (the
+// encoding is a pure function of its inputs); returns G4B_OK or an error status.
 int tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
-                  uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle);
+                  uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle,
+                  CUtensorMapL2promotion promo = CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 
 #define G4B_ENTRY(opname)                                  \
     g4b::clear_error();                                    \

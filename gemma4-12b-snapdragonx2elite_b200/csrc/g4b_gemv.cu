@@ -28,6 +28,7 @@
 //     reduce.comp dispatch fused into the GEMV.
 #include <algorithm>
 #include <mutex>
+#include <vector>
 #include <utility>
 
 #include "g4b_tcgen05.cuh"
@@ -1026,6 +1027,495 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
     }
 }
 
+// ---------------------------------------------------------------- GEMV chains
+// A chain of M = 1 GEMV steps run by one persistent launch (g4b_gemv_chain_*):
+// the engine's recorded command buffer of gemv() dispatches with a barrier
+// after each (src/vk_engine.py:254-290, bar() at :261).  Step j reads x only
+// after every column tile of step j-1 has been written (a per-step count of
+// written tiles); the weight stream runs on from one step into the next.
+//
+// Each step carries its own partition of (tile, k-chunk) items over the CTAs,
+// chosen on the host: CTA c owns the contiguous items [range[c], range[c+1]).
+// For the small decode GEMVs the host prefers tile-aligned ranges (no CTA
+// straddles two shared tiles), so a CTA never runs its items one tile after
+// another with a split-K flush and a deferred reduction in between.
+struct ChainStep {
+    const void* x;
+    TcSeg seg0, seg1, seg2;
+    const int* range;  // [G + 1]: CTA c < G owns items [range[c], range[c+1]); item = tile * noct + k-chunk
+    const int* cspan;  // [ntiles][2]: first and last CTA owning items of tile t
+    int nseg, K, noct, ntiles, G, pad_;
+};
+static_assert(sizeof(ChainStep) % 8 == 0, "ChainStep is copied as 32-bit words");
+
+struct ChainArgs {
+    const ChainStep* steps;   // [nsteps], device memory
+    const CUtensorMap* maps;  // [nsteps][2 * kTcMaxSeg]: weight maps, then scale maps; device memory
+    unsigned* sync;           // [nsteps] tiles written per step, then the exit count and the abort word
+    float* partial;           // [2 * G][kStTN]: CTA c's partials of its first and its last tile
+    unsigned* counters;       // [maxtiles] split-K arrivals per tile
+    int nsteps, stage_bytes, s_bytes, maxtiles;
+};
+
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait until *count >= need (acquire).  Gives up (false) on the
+// CTA's or the chain's abort word, or after kWaitLimitNs (raising both).
+__device__ __forceinline__ bool chain_wait_count(const unsigned* count, unsigned need, unsigned* gabort,
+                                                 volatile int* abort) {
+    if (ld_acquire_gpu_u32(count) >= need) return true;
+    const uint64_t t0 = global_ns();
+    for (int spin = 0;; spin++) {
+        if (spin > 4096) __nanosleep(64);  // a step boundary normally resolves within the spin
+        if (ld_acquire_gpu_u32(count) >= need) return true;
+        if (*abort || *(volatile unsigned*)gabort) {
+            *abort = 1;
+            return false;
+        }
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort = 1;
+            atomicOr(&g_gemv_status, kStatusTimeout);
+            atomicExch(gabort, 1u);
+            return false;
+        }
+    }
+}
+
+// One persistent grid of one CTA per SM (a cooperative launch: every CTA is
+// resident, so the steps can wait on one another).  Warp roles as in
+// gemv_i4_m1_kernel; the activation warp stores x with plain loads (x was
+// written by other SMs during this launch) and arrives on the stage's full
+// barrier itself.
+template <bool XF32, int SFMT, bool YF32>
+__global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __grid_constant__ ChainArgs ch) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ uint64_t bars[2 * kM1Stages];
+    __shared__ float red[2][kM1Groups][kStTN];  // double-buffered: consecutive flushes never share it
+    __shared__ unsigned s_last;
+    __shared__ int s_pending;                    // shared tile this CTA must still reduce (-1: none)
+    __shared__ int s_issued, s_xdone;
+    __shared__ int s_abort;
+    __shared__ __align__(16) uint32_t s_zero[32];  // B-fragment source for lanes that feed zeros
+    __shared__ __align__(8) ChainStep s_step[2];   // the consumers' current and next step
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = blockIdx.x;
+    volatile int* abort_flag = &s_abort;
+    constexpr int esz = XF32 ? 4 : 2;
+    constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
+    constexpr int kStepWords = (int)(sizeof(ChainStep) / 4);
+    const int nsteps = ch.nsteps, stage_bytes = ch.stage_bytes, s_bytes = ch.s_bytes;
+    float* const partial = ch.partial;
+    unsigned* const counters = ch.counters;
+    unsigned* const gabort = ch.sync + nsteps + 1;
+    // the swizzle pattern repeats every 1024 bytes: align the stages to it
+    const uint32_t raw0 = smem_u32(smem_raw);
+    const uint32_t smem0 = (raw0 + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (smem0 - raw0);
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (kM1Stages + s); };
+    // this CTA's items of a step
+    auto my_range = [&](const ChainStep& d, int& ib, int& ie) {
+        if (c < d.G) {
+            ib = __ldg(d.range + c);
+            ie = __ldg(d.range + c + 1);
+        } else {
+            ib = ie = 0;
+        }
+    };
+    const int pw = kM1Consumers / 32;  // first producer warp
+
+    if (tid == 0) {
+        for (int s = 0; s < kM1Stages; s++) {
+            mbar_init(full_bar(s), 2);  // the TMA producer's arrival (with the bytes) + the activation warp's
+            mbar_init(empty_bar(s), kM1WarpsPerGroup);
+        }
+        s_abort = 0;
+        s_issued = 0;
+        s_xdone = 0;
+        s_pending = -1;
+        fence_mbar_init();
+    }
+    if (tid < 32) s_zero[tid] = 0u;
+    if (tid < kStepWords) reinterpret_cast<uint32_t*>(&s_step[0])[tid] = __ldg(reinterpret_cast<const uint32_t*>(ch.steps) + tid);
+    __syncthreads();
+
+    if (warp == pw) {
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            int i = 0;  // this CTA's item number over all steps
+            bool stop = false;
+            for (int sg = 0; sg < 2 * kTcMaxSeg; sg++) prefetch_tensor_map(ch.maps + sg);
+            for (int j = 0; j < nsteps && !stop; j++) {
+                const ChainStep d = ch.steps[j];
+                const CUtensorMap* wm = ch.maps + (size_t)j * 2 * kTcMaxSeg;
+                const CUtensorMap* sm = wm + kTcMaxSeg;
+                // the maps were copied in before the launch and never change during it
+                if (j + 1 < nsteps)
+                    for (int sg = 0; sg < 2 * kTcMaxSeg; sg++) prefetch_tensor_map(wm + 2 * kTcMaxSeg + sg);
+                int ibeg, iend;
+                my_range(d, ibeg, iend);
+                int t = ibeg / d.noct, o = ibeg - t * d.noct;
+                for (int it = ibeg; it < iend; ++it, ++i) {
+                    const int s = m1_stage(i);
+                    // after an abort the consumers release stages without reading them: issue nothing more
+                    if (*abort_flag ||
+                        (i >= kM1Stages && !mbar_wait(empty_bar(s), m1_parity(i) ^ 1u, abort_flag, &g_gemv_status))) {
+                        stop = true;
+                        break;
+                    }
+                    const int sg = tc_seg_of(d, t);
+                    const int lt = t - tc_seg(d, sg).tile0;
+                    mbar_arrive_expect_tx(full_bar(s), kM1WBytes + s_bytes);
+                    const uint32_t st = smem0 + (uint32_t)s * stage_bytes;
+                    tma_load_2d(st, &wm[sg], lt * (kStTN / 8), o * kM1Rows, full_bar(s), pol);
+                    tma_load_2d(st + kM1WBytes, &sm[sg], lt * (kStTN * ssz / 8), o * 8, full_bar(s), pol);
+                    if (++o == d.noct) {
+                        o = 0;
+                        ++t;
+                    }
+                }
+            }
+            s_issued = i;
+        }
+    } else if (warp == pw + 1) {
+        // x slices by plain loads (L2, not L1: x was written by other SMs during this launch)
+        int i = 0;
+        bool stop = false;
+        for (int j = 0; j < nsteps && !stop; j++) {
+            const ChainStep* dj = ch.steps + j;
+            const int noct = dj->noct;
+            const uint8_t* x = reinterpret_cast<const uint8_t*>(dj->x);
+            int ibeg, iend;
+            my_range(*dj, ibeg, iend);
+            if (iend > ibeg && j > 0) {
+                const bool ok = chain_wait_count(&ch.sync[j - 1], (unsigned)ch.steps[j - 1].ntiles, gabort, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) break;
+            }
+            int o = ibeg % noct;
+            for (int it = ibeg; it < iend; ++it, ++i) {
+                const int s = m1_stage(i);
+                if (i >= kM1Stages) {
+                    bool ok = true;
+                    if (lane == 0) ok = mbar_wait(empty_bar(s), m1_parity(i) ^ 1u, abort_flag, &g_gemv_status);
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                        stop = true;
+                        break;
+                    }
+                }
+                const uint8_t* src = x + (size_t)o * kM1Rows * esz;
+                uint8_t* dst = smem + (size_t)s * stage_bytes + kM1WBytes + s_bytes;
+                #pragma unroll
+                for (int b = lane * 16; b < kM1Rows * esz; b += 512)
+                    *reinterpret_cast<uint4*>(dst + b) = __ldcg(reinterpret_cast<const uint4*>(src + b));
+                __syncwarp();
+                if (lane == 0) mbar_arrive(full_bar(s));
+                if (++o == noct) o = 0;
+            }
+        }
+        if (lane == 0) s_xdone = i;
+    } else {
+        const int g = lane >> 2, q = lane & 3, ctid = tid;
+        const int grp = warp / kM1WarpsPerGroup, seg = warp % kM1WarpsPerGroup;  // 16-byte column segment
+        const int colA = 32 * seg + 4 * g;  // this lane's columns: colA + j (j = 0, 1) and colA + 2 + j
+        // ldmatrix.x4: lane L addresses row L%8 of matrix L/8; matrix m = (step p + m/2, k-pair m%2)
+        const int lm = lane >> 3, lrr = lane & 7, lq = lrr >> 1, le = lrr & 1;
+        const int lds = lm >> 1, lh = lm & 1;
+        constexpr int NPASS = XF32 ? 2 : 1;   // f32 x: two passes of 4 blocks
+        constexpr int NSTEP = XF32 ? 8 : 16;  // mma steps per pass
+        constexpr int RMUL = XF32 ? 4 : 2;    // rows advanced per step
+        int nflush = 0;
+        int ibase = 0;       // this CTA's items in earlier steps
+        unsigned ndone = 0;  // ctid 0: tiles of the current step whose y this CTA wrote
+
+        for (int j = 0; j < nsteps; j++) {
+            // every consumer is done with step j-1, whose descriptor slot now takes step j+1's
+            named_bar_sync(1, kM1Consumers);
+            if (j + 1 < nsteps && ctid < kStepWords)
+                reinterpret_cast<uint32_t*>(&s_step[(j + 1) & 1])[ctid] =
+                    __ldg(reinterpret_cast<const uint32_t*>(ch.steps + j + 1) + ctid);
+            const ChainStep& d = s_step[j & 1];
+            int ibeg, iend;
+            my_range(d, ibeg, iend);
+            // y[n] of the tile's segment, scaled by its e4m3 inverse scale
+            auto write_y = [&](int t, int col, float v) {
+                const TcSeg& sgm = tc_seg(d, tc_seg_of(d, t));
+                const int n = (t - sgm.tile0) * kStTN + col;
+                const float inv = SFMT == G4B_SCALE_E4M3 ? sgm.inv : 1.0f;
+                if (n < sgm.N) {
+                    if (YF32) ((float*)sgm.y)[n] = v * inv;
+                    else ((__half*)sgm.y)[n] = __float2half_rn(v * inv);
+                }
+            };
+            float acc[2][2];
+            const int t_first = ibeg / d.noct, t_last = iend > ibeg ? (iend - 1) / d.noct : t_first - 1;
+            // partial slot of CTA cc's share of tile t: its first tile or its last
+            auto slot_of = [&](int cc, int t) { return 2 * cc + (t == __ldg(d.range + cc) / d.noct ? 0 : 1); };
+            // Sum a shared tile's partials in CTA order (deterministic) and write y.
+            auto reduce_tile = [&](int t) {
+                const int c_first = __ldg(d.cspan + 2 * t), c_last = __ldg(d.cspan + 2 * t + 1);
+                if (ctid < kStTN) {
+                    const int col = ctid;
+                    float v = 0.f;
+                    for (int k0 = c_first; k0 <= c_last; k0 += 8) {
+                        float pv[8];
+                        #pragma unroll
+                        for (int k = 0; k < 8; k++) {
+                            pv[k] = 0.f;
+                            if (k0 + k <= c_last) pv[k] = __ldcg(&partial[(size_t)slot_of(k0 + k, t) * kStTN + col]);
+                        }
+                        #pragma unroll
+                        for (int k = 0; k < 8; k++)
+                            if (k0 + k <= c_last) v += pv[k];
+                    }
+                    write_y(t, col, v);
+                }
+                if (ctid == 0) counters[t] = 0u;  // ready for the next step
+            };
+
+            for (int t = t_first; t <= t_last; ++t) {
+                acc[0][0] = acc[0][1] = acc[1][0] = acc[1][1] = 0.f;
+                const int tb = max(ibeg, t * d.noct), te = min(iend, (t + 1) * d.noct);
+                int it = tb + ((grp - (ibase + tb - ibeg) % kM1Groups + kM1Groups) % kM1Groups);
+                for (; it < te; it += kM1Groups) {
+                    const int i = ibase + (it - ibeg);
+                    const int s = m1_stage(i);
+                    if (!mbar_wait(full_bar(s), m1_parity(i), abort_flag, &g_gemv_status)) {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(empty_bar(s));
+                        continue;
+                    }
+                    const uint32_t st_u = smem0 + (uint32_t)s * stage_bytes;
+                    const uint8_t* st = smem + (size_t)s * stage_bytes;
+                    const uint8_t* sc = st + kM1WBytes;
+                    const uint8_t* xs = sc + s_bytes;
+                    // block sums X[b] of the stage's 8 blocks: lane l sums rows 8l..8l+7
+                    float xsum;
+                    if constexpr (XF32) {
+                        const float4 v0 = *reinterpret_cast<const float4*>(xs + lane * 32);
+                        const float4 v1 = *reinterpret_cast<const float4*>(xs + lane * 32 + 16);
+                        xsum = ((((((v0.x + v0.y) + v0.z) + v0.w) + v1.x) + v1.y) + v1.z) + v1.w;
+                    } else {
+                        const uint4 v = *reinterpret_cast<const uint4*>(xs + lane * 16);
+                        xsum = ((((((h_lo(v.x) + h_hi(v.x)) + h_lo(v.y)) + h_hi(v.y)) + h_lo(v.z)) + h_hi(v.z)) + h_lo(v.w)) +
+                               h_hi(v.w);
+                    }
+                    xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+                    xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
+                    #pragma unroll 1
+                    for (int pass = 0; pass < NPASS; pass++) {
+                        // ldmatrix row of this lane: block and rotated row (swizzle phase differs per lane)
+                        const int lblk = XF32 ? 4 * pass + lq : lq + 4 * lh;
+                        const int lrot = RMUL * lds + 2 * lq + le + ((XF32 && lh) ? 2 : 0);
+                        const uint32_t lbase = st_u + (uint32_t)(lblk * 32 * 128);
+                        // row offsets for the 4 step phases (steps p = 4m + d advance the row by 8m (f16) / 16m (f32))
+                        uint32_t roff[4], swz[4];
+                        #pragma unroll
+                        for (int d = 0; d < 4; d++) {
+                            const int r = (RMUL * d + lrot) & 31;
+                            roff[d] = (uint32_t)(r * 128);
+                            swz[d] = (uint32_t)((seg ^ (r & 7)) << 4);
+                        }
+                        // B-fragment sources: lanes that feed zeros read a zeroed area instead
+                        uint32_t xb0, xb1, xoff;
+                        if constexpr (XF32) {
+                            const bool mine = (g >> 1) == q;
+                            xb0 = mine ? smem_u32(xs) + (uint32_t)((4 * pass + q) * 128) : smem_u32(s_zero);
+                            xb1 = xb0;
+                            xoff = (uint32_t)(8 * q);
+                        } else {
+                            xb0 = g == q ? smem_u32(xs) + (uint32_t)(q * 64) : smem_u32(s_zero);
+                            xb1 = g == q + 4 ? smem_u32(xs) + (uint32_t)((q + 4) * 64) : smem_u32(s_zero);
+                            xoff = (uint32_t)(4 * q);
+                        }
+                        float C[2][4];
+                        #pragma unroll
+                        for (int k = 0; k < 2; k++) C[k][0] = C[k][1] = C[k][2] = C[k][3] = 0.f;
+                        #pragma unroll
+                        for (int p = 0; p < NSTEP; p += 2) {
+                            const int d = p & 3, mrow = (p >> 2) * (RMUL == 2 ? 1024 : 2048);
+                            const uint32_t addr = lbase + (((roff[d] + (uint32_t)mrow) & 4095u) | swz[d]);
+                            uint32_t ra0, rb0, ra1, rb1;
+                            ldsm_x4_trans(addr, ra0, rb0, ra1, rb1);
+                            #pragma unroll
+                            for (int ss = 0; ss < 2; ss++) {
+                                const uint32_t RA = ss ? ra1 : ra0, RB = ss ? rb1 : rb0;
+                                const int pp = p + ss;
+                                uint32_t b0, b1;
+                                if constexpr (XF32) {
+                                    const uint32_t o0 = (xoff + 16u * pp) & 127u, o1 = (xoff + 16u * pp + 8u) & 127u;
+                                    float2 xa, xb;
+                                    asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(xa.x), "=f"(xa.y) : "r"(xb0 + o0));
+                                    asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(xb.x), "=f"(xb.y) : "r"(xb1 + o1));
+                                    const bool lo = (g & 1) != 0;
+                                    b0 = split_pair(xa.x, xa.y, lo);
+                                    b1 = split_pair(xb.x, xb.y, lo);
+                                } else {
+                                    const uint32_t o = (xoff + 4u * pp) & 63u;
+                                    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(xb0 + o));
+                                    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(xb1 + o));
+                                }
+                                const uint32_t RA8 = RA >> 8, RB8 = RB >> 8;
+                                mma_16816(C[0], RA & 0x000F000Fu, RA8 & 0x000F000Fu, RB & 0x000F000Fu, RB8 & 0x000F000Fu, b0, b1);
+                                mma_16816(C[1], RA & 0x00F000F0u, RA8 & 0x00F000F0u, RB & 0x00F000F0u, RB8 & 0x00F000F0u, b0, b1);
+                            }
+                        }
+                        // per-block scale, 2^E and -8 X correction, in f32
+                        int blk0, blk1;
+                        if constexpr (XF32) { blk0 = 4 * pass + q; blk1 = blk0; } else { blk0 = 2 * q; blk1 = 2 * q + 1; }
+                        const float X0 = __shfl_sync(0xffffffffu, xsum, 4 * blk0);
+                        const float X1 = __shfl_sync(0xffffffffu, xsum, 4 * blk1);
+                        // scales of columns colA .. colA+3 in blocks blk0 / blk1
+                        float s0[4], s1[4];
+                        if constexpr (SFMT == G4B_SCALE_F16) {
+                            const uint2 u0 = *reinterpret_cast<const uint2*>(sc + (blk0 * kStTN + colA) * 2);
+                            const uint2 u1 = *reinterpret_cast<const uint2*>(sc + (blk1 * kStTN + colA) * 2);
+                            s0[0] = h_lo(u0.x); s0[1] = h_hi(u0.x); s0[2] = h_lo(u0.y); s0[3] = h_hi(u0.y);
+                            s1[0] = h_lo(u1.x); s1[1] = h_hi(u1.x); s1[2] = h_lo(u1.y); s1[3] = h_hi(u1.y);
+                        } else {
+                            const uint32_t u0 = *reinterpret_cast<const uint32_t*>(sc + blk0 * kStTN + colA);
+                            const uint32_t u1 = *reinterpret_cast<const uint32_t*>(sc + blk1 * kStTN + colA);
+                            uint32_t h;
+                            h = e4m3x2_to_f16x2((uint16_t)(u0 & 0xffffu)); s0[0] = h_lo(h); s0[1] = h_hi(h);
+                            h = e4m3x2_to_f16x2((uint16_t)(u0 >> 16));     s0[2] = h_lo(h); s0[3] = h_hi(h);
+                            h = e4m3x2_to_f16x2((uint16_t)(u1 & 0xffffu)); s1[0] = h_lo(h); s1[1] = h_hi(h);
+                            h = e4m3x2_to_f16x2((uint16_t)(u1 >> 16));     s1[2] = h_lo(h); s1[3] = h_hi(h);
+                        }
+                        #pragma unroll
+                        for (int j = 0; j < 2; j++) {
+                            const float E = j ? 1048576.0f : 16777216.0f;  // 2^20 (high nibble) / 2^24 (low nibble)
+                            // C[j][0..1]: column colA + j; C[j][2..3]: column colA + 2 + j
+                            if constexpr (XF32) {
+                                acc[j][0] = fmaf(s0[j], fmaf(C[j][0] + C[j][1], E, -8.0f * X0), acc[j][0]);
+                                acc[j][1] = fmaf(s0[2 + j], fmaf(C[j][2] + C[j][3], E, -8.0f * X0), acc[j][1]);
+                            } else {
+                                acc[j][0] = fmaf(s0[j], fmaf(C[j][0], E, -8.0f * X0), acc[j][0]);
+                                acc[j][0] = fmaf(s1[j], fmaf(C[j][1], E, -8.0f * X1), acc[j][0]);
+                                acc[j][1] = fmaf(s0[2 + j], fmaf(C[j][2], E, -8.0f * X0), acc[j][1]);
+                                acc[j][1] = fmaf(s1[2 + j], fmaf(C[j][3], E, -8.0f * X1), acc[j][1]);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(empty_bar(s));
+                }
+                // ---- flush tile t: quad sum (the lanes of a quad hold different blocks), group sum, CTA share
+                #pragma unroll
+                for (int k = 0; k < 2; k++)
+                    #pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        float v = acc[k][h];
+                        v += __shfl_xor_sync(0xffffffffu, v, 1);
+                        v += __shfl_xor_sync(0xffffffffu, v, 2);
+                        acc[k][h] = v;
+                    }
+                const int rb = nflush++ & 1;
+                if (q == 0) {
+                    #pragma unroll
+                    for (int jj = 0; jj < 2; jj++) {
+                        red[rb][grp][colA + jj] = acc[jj][0];
+                        red[rb][grp][colA + 2 + jj] = acc[jj][1];
+                    }
+                }
+                named_bar_sync(1, kM1Consumers);
+                // the tile is this CTA's alone when the CTA owns all its k-chunks
+                const bool single = ibeg <= t * d.noct && iend >= (t + 1) * d.noct;
+                const bool ok = !*abort_flag;
+                if (ctid < kStTN && ok) {
+                    const int col = ctid;
+                    float v = red[rb][0][col];
+                    #pragma unroll
+                    for (int gg = 1; gg < kM1Groups; gg++) v += red[rb][gg][col];
+                    if (single) write_y(t, col, v);
+                    else partial[(size_t)(2 * c + (t == t_first ? 0 : 1)) * kStTN + col] = v;
+                }
+                if (single) {
+                    if (ctid == 0 && ok) ndone++;
+                } else {
+                    // publish this CTA's partial: one thread fences for the CTA (after the barrier) and
+                    // arrives on the tile's counter; the last of the tile's CTAs to arrive reduces it
+                    named_bar_sync(1, kM1Consumers);
+                    const unsigned sharers = (unsigned)(__ldg(d.cspan + 2 * t + 1) - __ldg(d.cspan + 2 * t));
+                    if (t < t_last) {
+                        // not our final tile: do not stall the other consumers on the atomic; if we
+                        // turn out to be the last arriver, the reduction runs after our last item
+                        if (ctid == 0 && ok) {
+                            __threadfence();
+                            if (atomicAdd(&counters[t], 1u) == sharers) s_pending = t;
+                        }
+                    } else {
+                        if (ctid == 0) {
+                            unsigned last = 0;
+                            if (ok) {
+                                __threadfence();
+                                last = atomicAdd(&counters[t], 1u) == sharers ? 1u : 0u;
+                            }
+                            s_last = last;
+                        }
+                        named_bar_sync(1, kM1Consumers);
+                        if (s_last) {
+                            __threadfence();
+                            reduce_tile(t);
+                            if (ctid == 0) ndone++;
+                        }
+                    }
+                }
+            }
+            // the deferred reduction of an earlier tile this CTA was the last to finish
+            named_bar_sync(1, kM1Consumers);
+            if (s_pending >= 0 && !*abort_flag) {
+                __threadfence();
+                reduce_tile(s_pending);
+                if (ctid == 0) ndone++;
+            }
+            // every y this CTA wrote in step j is stored: count its tiles as written
+            named_bar_sync(1, kM1Consumers);
+            if (ctid == 0) {
+                s_pending = -1;
+                if (ndone) {
+                    __threadfence();
+                    atomicAdd(&ch.sync[j], ndone);
+                }
+                ndone = 0;
+                if (*abort_flag) atomicExch(gabort, 1u);
+            }
+            ibase += iend - ibeg;
+        }
+    }
+
+    __syncthreads();
+    if (tid == 0 && *abort_flag) {
+        // wait (bounded) for the copies still in flight into this CTA's shared memory; an item
+        // whose x the activation warp never stored still needs that warp's arrival
+        const int issued = s_issued;
+        for (int i = max(0, issued - kM1Stages); i < issued; i++) {
+            if (i >= s_xdone) mbar_arrive(full_bar(m1_stage(i)));
+            const uint64_t t0 = global_ns();
+            while (!mbar_try_wait(full_bar(m1_stage(i)), m1_parity(i)) && global_ns() - t0 < kWaitLimitNs) {
+            }
+        }
+    }
+    if (tid == 0) {
+        if (*abort_flag) atomicExch(gabort, 1u);
+        __threadfence();
+        if (atomicAdd(&ch.sync[nsteps], 1u) == gridDim.x - 1u) {
+            // the last CTA out: every CTA is past all its waits, so the chain's counts can be
+            // cleared for the next launch (and, after an abort, the split-K arrival counters)
+            __threadfence();
+            const bool aborted = *(volatile unsigned*)gabort != 0u;
+            for (int j = 0; j < nsteps; j++) ch.sync[j] = 0u;
+            if (aborted)
+                for (int t = 0; t < ch.maxtiles; t++) counters[t] = 0u;
+            *gabort = 0u;
+            ch.sync[nsteps] = 0u;
+        }
+    }
+}
+
 struct M1Plan {
     int ntiles, noct, G, maxseg, stage_bytes, s_bytes;
     long long total;
@@ -1063,7 +1553,8 @@ static int launch_m1(const M1Args& a, const M1Plan& p, const uint32_t* const* wp
         const int k = i < a.nseg ? i : 0;  // unused slots repeat segment 0's maps
         const int N = tc_seg(a, k).N;
         int st = tensor_map_2d(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, wps[k], (uint64_t)N / 8, (uint64_t)a.K,
-                               (uint64_t)N / 2, kStTN / 8, kM1Rows, CU_TENSOR_MAP_SWIZZLE_128B);
+                               (uint64_t)N / 2, kStTN / 8, kM1Rows, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
         if (st != G4B_OK) return st;
         st = tensor_map_2d(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, scales[k], (uint64_t)N * ssz / 8,
                            (uint64_t)a.K / 32, (uint64_t)N * ssz, kStTN * ssz / 8, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -1583,7 +2074,8 @@ static int launch_tc(const TcArgs& a, const TcPlan& p, const uint32_t* const* wp
         const int k = i < a.nseg ? i : 0;  // unused slots repeat segment 0's maps
         const int N = k == 0 ? a.seg0.N : (k == 1 ? a.seg1.N : a.seg2.N);
         int st = tensor_map_2d(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, wps[k], (uint64_t)N / 8, (uint64_t)a.K,
-                               (uint64_t)N / 2, kTcTN / 8, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+                               (uint64_t)N / 2, kTcTN / 8, kTcRows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
         if (st != G4B_OK) return st;
         st = tensor_map_2d(&maps.s[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, scales[k], (uint64_t)N * ssz / 8,
                            (uint64_t)a.K / 32, (uint64_t)N * ssz, kTcTN * ssz / 8, 2, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -1778,7 +2270,8 @@ static int launch_stream(const StreamArgs& a, const StreamPlan& p, const uint32_
                          cudaStream_t s) {
     CUtensorMap wmap, smap;
     int st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, wp, (uint64_t)a.N / 8, (uint64_t)a.K,
-                           (uint64_t)a.N / 2, kStTN / 8, kStRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+                           (uint64_t)a.N / 2, kStTN / 8, kStRows, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
     if (st != G4B_OK) return st;
     constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
     st = tensor_map_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT64, scales, (uint64_t)a.N * ssz / 8, (uint64_t)a.K / 32,
@@ -2159,6 +2652,308 @@ int g4b_gemv_i4_fused(const void* x, int x_dtype, int nseg, const g4b_gemv_segme
                                reinterpret_cast<cudaStream_t>(stream), "gemv_i4_fused");
     t_pdl = false;
     return st;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ GEMV chains
+struct g4b_gemv_chain {
+    int device = -1, nsteps = 0, x_dtype = 0, scale_fmt = 0, y_dtype = 0;
+    int grid = 0, stage_bytes = 0, s_bytes = 0, maxtiles = 0;
+    size_t smem = 0, sync_bytes = 0, ws_bytes = 0;
+    // device: [nsteps][6] CUtensorMap, then [nsteps] ChainStep, then the steps' range / cspan tables
+    void* plan = nullptr;
+};
+
+namespace g4b {
+
+constexpr int kChainMaxSteps = 1 << 16;
+
+static size_t chain_maps_bytes(int nsteps) { return (size_t)nsteps * 2 * kTcMaxSeg * sizeof(CUtensorMap); }
+
+// The partition of one step's items over the CTAs: range[c] .. range[c+1] for
+// c < G (contiguous, item = tile * noct + k-chunk).  Two candidates:
+//   balanced      CTA c owns [c*T/G, (c+1)*T/G): the fewest items per CTA,
+//                 but a CTA may straddle two shared tiles, and then flushes
+//                 twice and may run a deferred reduction;
+//   tile-aligned  whole tiles per CTA when there are at least as many tiles
+//                 as CTAs, otherwise each tile's k-chunks split evenly over
+//                 G/ntiles CTAs: no CTA straddles a shared tile.
+// The tile-aligned one is taken unless it costs more than one item over the
+// balanced one's longest range plus a straddle.
+static std::vector<int> chain_partition(int ntiles, int noct, int sms) {
+    const long long total = (long long)ntiles * noct;
+    const int G = (int)std::max<long long>(1, std::min<long long>(std::min(sms, kMaxCtas), total));
+    std::vector<int> bal(G + 1), ta;
+    for (int c = 0; c <= G; c++) bal[c] = (int)((long long)c * total / G);
+    int max_bal = 0;
+    bool straddle = false;
+    for (int c = 0; c < G; c++) {
+        max_bal = std::max(max_bal, bal[c + 1] - bal[c]);
+        const int tf = bal[c] / noct, tl = (bal[c + 1] - 1) / noct;
+        if (tl > tf && (bal[c] % noct != 0 || bal[c + 1] % noct != 0)) straddle = true;
+    }
+    if (ntiles >= G) {
+        ta.resize(G + 1);
+        for (int c = 0; c <= G; c++) ta[c] = (int)((long long)c * ntiles / G) * noct;
+    } else {
+        ta.push_back(0);
+        const int q = G / ntiles, r = G % ntiles;
+        for (int t = 0; t < ntiles; t++) {
+            const int n = std::min(noct, q + (t < r ? 1 : 0));
+            for (int k = 1; k <= n; k++) ta.push_back(t * noct + (int)((long long)k * noct / n));
+        }
+    }
+    int max_ta = 0;
+    for (size_t c = 0; c + 1 < ta.size(); c++) max_ta = std::max(max_ta, ta[c + 1] - ta[c]);
+    return max_ta <= max_bal + (straddle ? 1 : 0) ? ta : bal;
+}
+
+template <bool XF32, int SFMT, bool YF32>
+static int chain_prepare_kernel(size_t smem, int* resident) {
+    auto kern = gemv_i4_chain_kernel<XF32, SFMT, YF32>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(resident, kern, kM1Threads, smem);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain: occupancy query: %s", cudaGetErrorString(e));
+    return G4B_OK;
+}
+
+static int chain_prepare(bool xf32, int sfmt, bool yf32, size_t smem, int* resident) {
+    if (xf32) {
+        if (sfmt == G4B_SCALE_F16) return yf32 ? chain_prepare_kernel<true, G4B_SCALE_F16, true>(smem, resident) : chain_prepare_kernel<true, G4B_SCALE_F16, false>(smem, resident);
+        return yf32 ? chain_prepare_kernel<true, G4B_SCALE_E4M3, true>(smem, resident) : chain_prepare_kernel<true, G4B_SCALE_E4M3, false>(smem, resident);
+    }
+    if (sfmt == G4B_SCALE_F16) return yf32 ? chain_prepare_kernel<false, G4B_SCALE_F16, true>(smem, resident) : chain_prepare_kernel<false, G4B_SCALE_F16, false>(smem, resident);
+    return yf32 ? chain_prepare_kernel<false, G4B_SCALE_E4M3, true>(smem, resident) : chain_prepare_kernel<false, G4B_SCALE_E4M3, false>(smem, resident);
+}
+
+template <bool XF32, int SFMT, bool YF32>
+static cudaError_t chain_launch_kernel(const g4b_gemv_chain* c, const ChainArgs& ch, cudaStream_t s) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(c->grid);
+    cfg.blockDim = dim3(kM1Threads);
+    cfg.dynamicSmemBytes = c->smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the steps wait on one another
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv_i4_chain_kernel<XF32, SFMT, YF32>, ch);
+}
+
+static cudaError_t chain_launch(const g4b_gemv_chain* c, const ChainArgs& ch, cudaStream_t s) {
+    const bool xf32 = c->x_dtype == G4B_DT_F32, yf32 = c->y_dtype == G4B_DT_F32;
+    if (xf32) {
+        if (c->scale_fmt == G4B_SCALE_F16) return yf32 ? chain_launch_kernel<true, G4B_SCALE_F16, true>(c, ch, s) : chain_launch_kernel<true, G4B_SCALE_F16, false>(c, ch, s);
+        return yf32 ? chain_launch_kernel<true, G4B_SCALE_E4M3, true>(c, ch, s) : chain_launch_kernel<true, G4B_SCALE_E4M3, false>(c, ch, s);
+    }
+    if (c->scale_fmt == G4B_SCALE_F16) return yf32 ? chain_launch_kernel<false, G4B_SCALE_F16, true>(c, ch, s) : chain_launch_kernel<false, G4B_SCALE_F16, false>(c, ch, s);
+    return yf32 ? chain_launch_kernel<false, G4B_SCALE_E4M3, true>(c, ch, s) : chain_launch_kernel<false, G4B_SCALE_E4M3, false>(c, ch, s);
+}
+
+}  // namespace g4b
+
+extern "C" {
+
+int g4b_gemv_chain_create(const g4b_gemv_chain_step* steps, int nsteps, int x_dtype, int scale_fmt, int y_dtype,
+                          g4b_gemv_chain** chain) {
+    G4B_ENTRY("gemv_chain_create");
+    G4B_REQUIRE(steps && chain, G4B_E_ARG, "gemv_chain_create: NULL pointer argument");
+    *chain = nullptr;
+    G4B_REQUIRE(nsteps >= 1 && nsteps <= kChainMaxSteps, G4B_E_ARG, "gemv_chain_create: nsteps=%d (1..%d)", nsteps,
+                kChainMaxSteps);
+    G4B_REQUIRE(x_dtype == G4B_DT_F32 || x_dtype == G4B_DT_F16, G4B_E_ARG, "gemv_chain_create: bad x_dtype %d",
+                x_dtype);
+    G4B_REQUIRE(y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16, G4B_E_ARG, "gemv_chain_create: bad y_dtype %d",
+                y_dtype);
+    G4B_REQUIRE(scale_fmt == G4B_SCALE_F16 || scale_fmt == G4B_SCALE_E4M3, G4B_E_ARG,
+                "gemv_chain_create: bad scale_fmt %d", scale_fmt);
+    for (int j = 0; j < nsteps; j++) {
+        const g4b_gemv_chain_step& st = steps[j];
+        G4B_REQUIRE(st.x, G4B_E_ARG, "gemv_chain_create: step %d has a NULL x", j);
+        G4B_REQUIRE(aligned16(st.x), G4B_E_ALIGN, "gemv_chain_create: step %d x must be 16-byte aligned", j);
+        G4B_REQUIRE(st.nseg >= 1 && st.nseg <= kTcMaxSeg, G4B_E_ARG, "gemv_chain_create: step %d nseg=%d (1..%d)", j,
+                    st.nseg, kTcMaxSeg);
+        G4B_REQUIRE(st.K > 0 && st.K % 256 == 0, G4B_E_SHAPE, "gemv_chain_create: step %d K=%d must be a multiple of 256",
+                    j, st.K);
+        int ntiles = 0;
+        for (int i = 0; i < st.nseg; i++) {
+            const g4b_gemv_segment& g = st.seg[i];
+            G4B_REQUIRE(g.wp && g.scales && g.y, G4B_E_ARG, "gemv_chain_create: step %d segment %d has a NULL pointer",
+                        j, i);
+            G4B_REQUIRE(g.N > 0 && g.N % 32 == 0, G4B_E_SHAPE,
+                        "gemv_chain_create: step %d segment %d N=%d must be a multiple of 32", j, i, g.N);
+            G4B_REQUIRE(aligned16(g.wp) && aligned16(g.scales), G4B_E_ALIGN,
+                        "gemv_chain_create: step %d segment %d wp and scales must be 16-byte aligned", j, i);
+            G4B_REQUIRE(((uintptr_t)g.y & (y_dtype == G4B_DT_F32 ? 3u : 1u)) == 0, G4B_E_ALIGN,
+                        "gemv_chain_create: step %d segment %d y misaligned", j, i);
+            ntiles += (g.N + kStTN - 1) / kStTN;
+        }
+        G4B_REQUIRE(ntiles <= kGemvMaxTiles, G4B_E_SHAPE, "gemv_chain_create: step %d has %d column tiles (max %d)", j,
+                    ntiles, kGemvMaxTiles);
+        G4B_REQUIRE((long long)ntiles * (st.K / 256) < (1LL << 30), G4B_E_SHAPE,
+                    "gemv_chain_create: step %d has too many weight tiles", j);
+    }
+    int sms = 0;
+    int st = check_device(&sms);
+    if (st != G4B_OK) return st;
+    int attr = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&attr, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess || !attr)
+        return fail(G4B_E_CUDA, "gemv_chain_create: device %d has no cooperative launch", dev);
+
+    const bool xf32 = x_dtype == G4B_DT_F32;
+    const int ssz = scale_fmt == G4B_SCALE_F16 ? 2 : 1;
+    std::vector<ChainStep> hsteps((size_t)nsteps);
+    std::vector<CUtensorMap> hmaps((size_t)nsteps * 2 * kTcMaxSeg);
+    std::vector<int> tables;           // every step's range[G + 1] and cspan[ntiles][2]
+    std::vector<size_t> range_at(nsteps), cspan_at(nsteps);
+    int grid = 1, maxtiles = 0;
+    for (int j = 0; j < nsteps; j++) {
+        const g4b_gemv_chain_step& cs = steps[j];
+        ChainStep& d = hsteps[j];
+        d = ChainStep{};
+        d.x = cs.x;
+        TcSeg* dst[kTcMaxSeg] = {&d.seg0, &d.seg1, &d.seg2};
+        const uint32_t* wps[kTcMaxSeg];
+        const void* scs[kTcMaxSeg];
+        int tile0 = 0;
+        for (int i = 0; i < kTcMaxSeg; i++) {
+            if (i < cs.nseg) {
+                dst[i]->y = cs.seg[i].y;
+                dst[i]->inv = cs.seg[i].inv;
+                dst[i]->N = cs.seg[i].N;
+                dst[i]->tile0 = tile0;
+                tile0 += (cs.seg[i].N + kStTN - 1) / kStTN;
+                wps[i] = cs.seg[i].wp;
+                scs[i] = cs.seg[i].scales;
+            } else {
+                *dst[i] = *dst[0];
+                dst[i]->tile0 = 1 << 30;  // never reached
+                wps[i] = cs.seg[0].wp;
+                scs[i] = cs.seg[0].scales;
+            }
+        }
+        d.nseg = cs.nseg;
+        d.K = cs.K;
+        d.noct = cs.K / 256;
+        d.ntiles = tile0;
+        const std::vector<int> range = chain_partition(d.ntiles, d.noct, sms);
+        d.G = (int)range.size() - 1;
+        range_at[j] = tables.size();
+        tables.insert(tables.end(), range.begin(), range.end());
+        cspan_at[j] = tables.size();
+        std::vector<int> cspan((size_t)2 * d.ntiles);
+        for (int cc = 0; cc < d.G; cc++) {
+            if (range[cc + 1] <= range[cc]) continue;
+            const int tf = range[cc] / d.noct, tl = (range[cc + 1] - 1) / d.noct;
+            // CTAs come in item order: the last CTA to touch a tile is the latest; the first is the one
+            // whose range holds the tile's first k-chunk
+            for (int t = tf; t <= tl; t++) {
+                cspan[2 * t + 1] = cc;
+                if (t != tf || range[cc] % d.noct == 0) cspan[2 * t] = cc;
+            }
+        }
+        tables.insert(tables.end(), cspan.begin(), cspan.end());
+        grid = std::max(grid, d.G);
+        maxtiles = std::max(maxtiles, d.ntiles);
+        CUtensorMap* wm = &hmaps[(size_t)j * 2 * kTcMaxSeg];
+        for (int i = 0; i < kTcMaxSeg; i++) {
+            const int k = i < cs.nseg ? i : 0;
+            const int N = cs.seg[k].N;
+            st = tensor_map_2d(&wm[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, wps[k], (uint64_t)N / 8, (uint64_t)cs.K,
+                               (uint64_t)N / 2, kStTN / 8, kM1Rows, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
+            if (st != G4B_OK) return st;
+            st = tensor_map_2d(&wm[kTcMaxSeg + i], CU_TENSOR_MAP_DATA_TYPE_UINT64, scs[k], (uint64_t)N * ssz / 8,
+                               (uint64_t)cs.K / 32, (uint64_t)N * ssz, kStTN * ssz / 8, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (st != G4B_OK) return st;
+        }
+    }
+    const int stage_bytes = (kM1WBytes + 8 * kStTN * ssz + kM1Rows * (xf32 ? 4 : 2) + 1023) & ~1023;
+    const size_t smem = (size_t)kM1Stages * stage_bytes + 1024;
+    int resident = 0;
+    st = chain_prepare(xf32, scale_fmt, y_dtype == G4B_DT_F32, smem, &resident);
+    if (st != G4B_OK) return st;
+    G4B_REQUIRE(resident >= 1 && grid <= sms * resident, G4B_E_CUDA,
+                "gemv_chain_create: %d CTAs cannot all be resident (%d per SM, %d SMs)", grid, resident, sms);
+
+    const size_t maps_bytes = chain_maps_bytes(nsteps);
+    const size_t steps_bytes = (size_t)nsteps * sizeof(ChainStep);
+    const size_t plan_bytes = maps_bytes + steps_bytes + tables.size() * sizeof(int);
+    void* plan = nullptr;
+    cudaError_t e = cudaMalloc(&plan, plan_bytes);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain_create: cudaMalloc: %s", cudaGetErrorString(e));
+    const int* tables_dev = reinterpret_cast<const int*>(reinterpret_cast<uint8_t*>(plan) + maps_bytes + steps_bytes);
+    for (int j = 0; j < nsteps; j++) {
+        hsteps[j].range = tables_dev + range_at[j];
+        hsteps[j].cspan = tables_dev + cspan_at[j];
+    }
+    std::vector<uint8_t> host(plan_bytes);
+    memcpy(host.data(), hmaps.data(), maps_bytes);
+    memcpy(host.data() + maps_bytes, hsteps.data(), steps_bytes);
+    memcpy(host.data() + maps_bytes + steps_bytes, tables.data(), tables.size() * sizeof(int));
+    e = cudaMemcpy(plan, host.data(), plan_bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(plan);
+        return fail(G4B_E_CUDA, "gemv_chain_create: cudaMemcpy: %s", cudaGetErrorString(e));
+    }
+    g4b_gemv_chain* c = new g4b_gemv_chain();
+    c->device = dev;
+    c->nsteps = nsteps;
+    c->x_dtype = x_dtype;
+    c->scale_fmt = scale_fmt;
+    c->y_dtype = y_dtype;
+    c->grid = grid;
+    c->stage_bytes = stage_bytes;
+    c->s_bytes = 8 * kStTN * ssz;
+    c->maxtiles = maxtiles;
+    c->smem = smem;
+    c->sync_bytes = ((size_t)(nsteps + 2) * sizeof(unsigned) + 255) & ~(size_t)255;
+    c->ws_bytes = kGemvCounterBytes + c->sync_bytes + (size_t)2 * grid * kStTN * sizeof(float);
+    c->plan = plan;
+    *chain = c;
+    return G4B_OK;
+}
+
+size_t g4b_gemv_chain_workspace_bytes(const g4b_gemv_chain* chain) { return chain ? chain->ws_bytes : 0; }
+
+int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_bytes, g4b_stream_t stream) {
+    G4B_ENTRY("gemv_chain_run");
+    G4B_REQUIRE(chain && chain->plan, G4B_E_ARG, "gemv_chain_run: NULL chain");
+    G4B_REQUIRE(workspace && ws_bytes >= chain->ws_bytes, G4B_E_WORKSPACE,
+                "gemv_chain_run: needs %zu bytes of workspace, got %zu", chain->ws_bytes, workspace ? ws_bytes : 0);
+    G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "gemv_chain_run: workspace must be 16-byte aligned");
+    int st = check_device(nullptr);
+    if (st != G4B_OK) return st;
+    int dev = -1;
+    cudaGetDevice(&dev);
+    G4B_REQUIRE(dev == chain->device, G4B_E_ARG, "gemv_chain_run: chain built on device %d, current device %d",
+                chain->device, dev);
+    ChainArgs ch{};
+    ch.maps = reinterpret_cast<const CUtensorMap*>(chain->plan);
+    ch.steps = reinterpret_cast<const ChainStep*>(reinterpret_cast<const uint8_t*>(chain->plan) +
+                                                  chain_maps_bytes(chain->nsteps));
+    ch.counters = reinterpret_cast<unsigned*>(workspace);
+    ch.sync = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(workspace) + kGemvCounterBytes);
+    ch.partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kGemvCounterBytes + chain->sync_bytes);
+    ch.nsteps = chain->nsteps;
+    ch.stage_bytes = chain->stage_bytes;
+    ch.s_bytes = chain->s_bytes;
+    ch.maxtiles = chain->maxtiles;
+    cudaError_t e = chain_launch(chain, ch, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain_run: launch: %s", cudaGetErrorString(e));
+    count_launch();
+    return launch_status("gemv_chain_run");
+}
+
+void g4b_gemv_chain_destroy(g4b_gemv_chain* chain) {
+    if (!chain) return;
+    if (chain->plan) cudaFree(chain->plan);
+    delete chain;
 }
 
 int g4b_gemv_i4_noalloc(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,

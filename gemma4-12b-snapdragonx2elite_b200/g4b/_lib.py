@@ -68,7 +68,7 @@ SIGNATURES = {
     "g4b_gemm_i4_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g4b_gemm_i4": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "g4b_allreduce_buffer_bytes": (_Z, [_I, _I]),
-    "g4b_allreduce_f32": (_I, [_P, _P, _I, _I, _I, _P, _P, _P]),
+    "g4b_allreduce_f32": (_I, [_P, _P, _I, _I, _I, _P, _P, C.c_uint, _P]),
     "g4b_comm_alloc": (_I, [_Z, C.POINTER(_P)]),
     "g4b_comm_free": (_I, [_P]),
     "g4b_ipc_handle": (_I, [_P, _P]),
@@ -76,12 +76,21 @@ SIGNATURES = {
     "g4b_ipc_close": (_I, [_P]),
     "g4b_gemm_w8a8": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _P]),
     "g4b_gemm_w4a8": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _P]),
+    "g4b_gemv_chain_create": (_I, [_P, _I, _I, _I, _I, C.POINTER(_P)]),
+    "g4b_gemv_chain_workspace_bytes": (_Z, [_P]),
+    "g4b_gemv_chain_run": (_I, [_P, _P, _Z, _P]),
+    "g4b_gemv_chain_destroy": (None, [_P]),
 }
 
 
 class GemvSegment(C.Structure):
     """struct g4b_gemv_segment (include/g4b.h)."""
     _fields_ = [("wp", C.c_void_p), ("scales", C.c_void_p), ("inv", C.c_float), ("y", C.c_void_p), ("N", C.c_int)]
+
+
+class GemvChainStep(C.Structure):
+    """struct g4b_gemv_chain_step (include/g4b.h)."""
+    _fields_ = [("x", C.c_void_p), ("K", C.c_int), ("nseg", C.c_int), ("seg", GemvSegment * 3)]
 
 
 class G4BError(RuntimeError):

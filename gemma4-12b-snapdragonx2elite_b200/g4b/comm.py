@@ -52,15 +52,17 @@ class PeerAllReduce:
         dist.barrier(group=group)
 
     def __call__(self, t: torch.Tensor, out: Optional[torch.Tensor] = None,
-                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
-        """Sum of t over the ranks, in place unless `out` is given (f32, n elements)."""
+                 stream: Optional[torch.cuda.Stream] = None, pdl: bool = False) -> torch.Tensor:
+        """Sum of t over the ranks, in place unless `out` is given (f32, n elements).
+        pdl: launch with programmatic dependent launch (the kernel may start
+        while its predecessor runs, and lets its successor start early)."""
         if t.dtype != torch.float32 or t.numel() != self.n or not t.is_contiguous():
             raise ValueError("PeerAllReduce: f32 contiguous tensor of n elements expected")
         y = t if out is None else out
         s = stream if stream is not None else torch.cuda.current_stream(t.device)
         L.check("g4b_allreduce_f32", self.lib.g4b_allreduce_f32(
             t.data_ptr(), y.data_ptr(), self.n, self.rank, self.world, self.ptrs.data_ptr(),
-            self.counter.data_ptr(), s.cuda_stream))
+            self.counter.data_ptr(), 1 if pdl else 0, s.cuda_stream))
         return y
 
     def close(self) -> None:

@@ -169,6 +169,66 @@ def gemv_i4_fused(x: torch.Tensor, ws_: list, outs: Optional[list] = None, out_d
     return outs
 
 
+class GemvChain:
+    """A recorded chain of M = 1 GEMV steps run as one persistent launch
+    (g4b_gemv_chain_*): the engine's per-token command buffer of gemv()
+    dispatches with a barrier after each.  Each step is (x, [weights], [outs]):
+    1 to 3 GEMVs that read x; a step may read any earlier step's output.
+    The tensors named in the steps must stay alive while the chain is used;
+    `run` reads their current contents on every call."""
+
+    def __init__(self, steps: list, device: Optional[torch.device] = None):
+        if not steps:
+            raise ValueError("GemvChain: no steps")
+        self.lib = L.load()
+        x0, w0, o0 = steps[0]
+        self.device = x0.device if device is None else device
+        self._keep = []
+        arr = (L.GemvChainStep * len(steps))()
+        fmt = w0[0].scale_fmt
+        for j, (x, ws_, outs) in enumerate(steps):
+            _need(x, "x")
+            if not 1 <= len(ws_) <= 3 or len(outs) != len(ws_):
+                raise ValueError(f"GemvChain: step {j} needs 1 to 3 weights and one output per weight")
+            if x.dtype != x0.dtype or any(o.dtype != o0[0].dtype for o in outs):
+                raise ValueError("GemvChain: all steps share the x dtype and the output dtype")
+            if any(w.K != x.numel() or w.scale_fmt != fmt for w in ws_):
+                raise ValueError(f"GemvChain: step {j} weights must have K = x.numel() and one scale format")
+            for o in outs:
+                _need(o, "out")
+            arr[j].x = _ptr(x)
+            arr[j].K = x.numel()
+            arr[j].nseg = len(ws_)
+            for i, (w, o) in enumerate(zip(ws_, outs)):
+                arr[j].seg[i] = L.GemvSegment(_ptr(w.wp), _ptr(w.scales), w.inv, _ptr(o), w.N)
+            self._keep.append((x, ws_, outs))
+        h = ctypes.c_void_p()
+        L.check("g4b_gemv_chain_create", self.lib.g4b_gemv_chain_create(
+            ctypes.cast(arr, ctypes.c_void_p), len(steps), _DT[x0.dtype], fmt, _DT[o0[0].dtype], ctypes.byref(h)))
+        self.handle = h.value
+        self.nsteps = len(steps)
+        self.workspace_bytes = int(self.lib.g4b_gemv_chain_workspace_bytes(self.handle))
+        self.workspace = torch.zeros(self.workspace_bytes + 256, dtype=torch.uint8, device=self.device)
+
+    def run(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        if self.handle is None:
+            raise RuntimeError("GemvChain: closed")
+        sh = _stream_handle(stream, self.device)
+        L.check("g4b_gemv_chain_run", self.lib.g4b_gemv_chain_run(
+            self.handle, _ptr(self.workspace), self.workspace.numel(), sh))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None:
+            self.lib.g4b_gemv_chain_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def gemm_i4(X: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None,
             out_dtype: torch.dtype = torch.float16, stream: Optional[torch.cuda.Stream] = None,
             workspace: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -180,6 +180,41 @@ G4B_API int g4b_gemv_i4_fused(const void* x, int x_dtype, int nseg, const g4b_ge
                               int y_dtype, int K, void* workspace, size_t ws_bytes, unsigned flags,
                               g4b_stream_t stream);
 
+/* A recorded chain of M = 1 GEMV steps run by ONE persistent launch: the
+ * engine's per-token command buffer of gemv() dispatches with a barrier after
+ * each (src/vk_engine.py:254-290, bar() at :261).  Step j may read what any
+ * earlier step wrote; a step starts reading x only after every column tile of
+ * the step before it has been written.  The weight stream does not wait: a
+ * step's packed words and scales are in flight while the previous step
+ * finishes, so no launch ramp or split-K tail sits between the GEMVs.
+ * Every step's y is bit-identical to g4b_gemv_i4_fused (or g4b_gemv_i4) on
+ * the same x.
+ *
+ *   create   validates the steps, encodes their TMA descriptors and copies the
+ *            plan to device memory (setup time: allocates and synchronises);
+ *            all steps share x_dtype, scale_fmt and y_dtype; per step
+ *            1 <= nseg <= 3, K % 256 == 0, every N % 32 == 0, x and the
+ *            weights 16-byte aligned.  The buffers named in the steps must
+ *            stay allocated while the chain is used.
+ *   run      one launch on `stream` (cooperative: every CTA resident); the
+ *            workspace (g4b_gemv_chain_workspace_bytes, 16-byte aligned) is
+ *            zero-filled once before first use and left zero by every run.
+ *            Never allocates or synchronises; capturable in a CUDA graph.
+ *   destroy  frees the plan. */
+typedef struct g4b_gemv_chain g4b_gemv_chain;
+typedef struct g4b_gemv_chain_step {
+    const void* x;                 /* [K] activations of this step */
+    int K;
+    int nseg;
+    g4b_gemv_segment seg[3];
+} g4b_gemv_chain_step;
+
+G4B_API int g4b_gemv_chain_create(const g4b_gemv_chain_step* steps, int nsteps, int x_dtype, int scale_fmt,
+                                  int y_dtype, g4b_gemv_chain** chain);
+G4B_API size_t g4b_gemv_chain_workspace_bytes(const g4b_gemv_chain* chain);
+G4B_API int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_bytes, g4b_stream_t stream);
+G4B_API void g4b_gemv_chain_destroy(g4b_gemv_chain* chain);
+
 /* Split-K partial reduction, vk/reduce.comp:8-12:
  *     y[n] = sum_{c=0}^{split-1} partial[c*N + n]   (c ascending, f32)
  * Exposed on its own for parity with the reference's reduce dispatch
@@ -282,23 +317,26 @@ G4B_API int g4b_gemm_w4a8(const int8_t* A8, const uint32_t* wp, const uint16_t* 
 /* The all-reduce after the row-parallel o and down GEMVs of a tensor-parallel
  * decode -- the cross-GPU counterpart of vk/reduce.comp:8-12 (the reference
  * runs on one GPU and has no collective).  One kernel, over NVLink peer
- * memory: each rank stores x into slot [rank] of every rank's exchange buffer,
- * raises a flag there (release, system scope), waits for all flags in its own
- * buffer (acquire; bounded, 2 s, then the kernel status word is raised) and
+ * memory: each rank stores every element of x, paired with the call's epoch in
+ * one 64-bit word, into slot [rank] of every rank's exchange buffer; each
+ * thread then polls its elements of all slots in its own buffer until they
+ * carry the epoch (bounded, 2 s, then the kernel status word is raised) and
  * writes y = the slots summed in rank order, identical bits on every rank.
- * In-place (x == y) is allowed.  For the 15 KB per-layer reductions of a
- * batch-1 decode this is latency-bound, where NCCL's general algorithms are not
- * tuned for it.
+ * No fence or flag round trip is needed.  In-place (x == y) is allowed.  For
+ * the 15 KB per-layer reductions of a batch-1 decode this is latency-bound,
+ * where NCCL's general algorithms are not tuned for it.
  *   bufs_dev  device array of `world` pointers: bufs_dev[r] = rank r's exchange
  *             buffer of g4b_allreduce_buffer_bytes(world, n) bytes, from
  *             g4b_comm_alloc (zero-filled), mapped into this process with
  *             g4b_ipc_open (own buffer: its own pointer)
  *   counter   this rank's device u32 call counter (zero-filled once); every rank
  *             makes the same calls in the same order (stream order, graphs too)
- * 1 <= world <= 8; n % 4 == 0 gives vectorised stores. */
+ *   flags     0 or G4B_GEMV_PDL (the kernel waits for its predecessor before it
+ *             reads x or stores anything, and lets its successor launch early)
+ * 1 <= world <= 8. */
 G4B_API size_t g4b_allreduce_buffer_bytes(int world, int n);
 G4B_API int g4b_allreduce_f32(const float* x, float* y, int n, int rank, int world, void* const* bufs_dev,
-                              unsigned* counter, g4b_stream_t stream);
+                              unsigned* counter, unsigned flags, g4b_stream_t stream);
 
 /* Setup-time helpers for the exchange buffers (never on the hot path):
  * cudaMalloc + zero fill, cudaFree, and CUDA IPC export / import / close

@@ -83,7 +83,7 @@ def main():
     def gemv_fused(x, ws, outs):
         ops.gemv_i4_fused(x, ws, outs=outs, stream=stream, pdl=True)
 
-    all_reduce = (lambda t: peer(t, stream=stream)) if peer is not None else (lambda t: dist.all_reduce(t))
+    all_reduce = (lambda t: peer(t, stream=stream, pdl=True)) if peer is not None else (lambda t: dist.all_reduce(t))
     dec = tp.TPDecoder(layers=mine, lm_head=lm, gemv=gemv, all_reduce=all_reduce,
                        all_gather=lambda out, t: dist.all_gather_into_tensor(out, t),
                        new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=dev),
