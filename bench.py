@@ -235,10 +235,13 @@ def main():
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="tensor-parallel stream: the per-layer all-reduce as one kernel over NVLink peer memory "
                          "(g4b_allreduce_f32, default) or NCCL's")
-    ap.add_argument("--schedule", default="launches", choices=["chain", "launches"],
-                    help="stream: launches (default) runs one launch per (fused) GEMV, chained by programmatic "
-                         "dependent launch; chain runs the token's GEMVs as one persistent launch "
-                         "(g4b_gemv_chain: each step waits for every tile of the step before it)")
+    ap.add_argument("--shape", default="config0", choices=["config0", "lm_head"],
+                    help="gemv workload: config0 = W[15360, 3840] (configs[0]); lm_head = W[262144, 3840]")
+    ap.add_argument("--schedule", default="chain", choices=["chain", "launches"],
+                    help="stream: chain (default) runs the token's GEMVs as one persistent launch "
+                         "(g4b_gemv_chain: each step waits for every tile of the step before it; tensor parallel: "
+                         "the all-reduces run inside it); launches runs one launch per (fused) GEMV, chained by "
+                         "programmatic dependent launch")
     ap.add_argument("--unfused", action="store_true",
                     help="stream: launch all 337 GEMVs separately, each on its own x, instead of fusing "
                          "q|k|v and gate|up (which read the same x in a decode step)")
@@ -279,7 +282,19 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     L.load()
 
-    if args.workload == "gemv":
+    if args.workload == "gemv" and args.shape == "lm_head":
+        # configs[1]'s largest GEMV on its own: W[262144, 3840] (566 MB > L2)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(0)
+        W = torch.randn((VOCAB, HIDDEN), generator=gen, device=device).mul_(0.02)
+        model = [("lm_head", qz.quant_device(W, pf=False, fp8=fp8, prefill_i8=False))]
+        del W
+        torch.cuda.empty_cache()
+        config.update({"workload": "configs[1] lm_head GEMV W[262144, 3840], batch 1, f16 x/y",
+                       "l2": "566 MB of weights > 126 MB L2, no flush needed"})
+        config.pop("layers", None)
+        metric = "int4 GEMV HBM GB/s (W[262144, 3840], batch 1)"
+    elif args.workload == "gemv":
         # one [15360, 3840] GEMV; R weight copies rotated so that
         # successive launches read different HBM (R * 33 MB > 126 MB L2)
         R = 8
@@ -452,7 +467,8 @@ def main():
             if use_chain:
                 roofline["traffic"] = int(round(t["traffic_ratio"] * step_bytes))
             else:
-                roofline["traffic"] = t.get("bytes_per_launch_scaled", {}).get(args.workload)
+                key = "lm_head" if args.workload == "gemv" and args.shape == "lm_head" else args.workload
+                roofline["traffic"] = t.get("bytes_per_launch_scaled", {}).get(key)
             roofline["traffic_note"] = t.get("note")
         except Exception:
             pass
@@ -916,14 +932,30 @@ def run_tp(args):
                        new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=device),
                        hidden=HIDDEN, vocab=VOCAB, world=world, gemv_fused=gemv_fused)
     x = torch.randn((HIDDEN,), generator=gen, device=device)
+    use_chain = args.schedule == "chain"
+    chain = chain_k = xchg = None
+    if use_chain:
+        # one persistent launch per token and rank; the all-reduces run inside it over NVLink
+        dec.bufs["part"] = torch.zeros(HIDDEN, dtype=torch.float32, device=device)
+        steps = tp.chain_steps(layers, lm, x, dec.bufs, L.CHAIN_ALLREDUCE)
+        xchg = comm.PeerBuffers(ops.GemvChain.exchange_bytes(steps, world), device)
+        chain = ops.GemvChain(steps, exchange=xchg)
+
+        def token():
+            chain.run(stream)
+            launches[0] += 1
+            dist.all_gather_into_tensor(dec.bufs["logits"], dec.bufs["logits_local"])
+    else:
+        def token():
+            dec.step(x)
     with torch.cuda.stream(stream):
         for _ in range(max(1, args.warmup)):
-            dec.step(x)
+            token()
     stream.synchronize()
     launches[0] = 0
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        dec.step(x)
+        token()
     per_step = launches[0]
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -955,10 +987,20 @@ def run_tp(args):
                          all_gather=lambda out, t: None,
                          new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=device),
                          hidden=HIDDEN, vocab=VOCAB, world=world, gemv_fused=gemv_fused)
+    if use_chain:
+        # the same chain with each all-reduced step's local partial as the next step's x
+        dec_k.bufs["part"] = torch.zeros(HIDDEN, dtype=torch.float32, device=device)
+        ksteps = [(st[0] if st[0] is not None else dec_k.bufs["part"], st[1], st[2])
+                  for st in tp.chain_steps(layers, lm, x, dec_k.bufs, 0)]
+        ksteps[0] = (x, ksteps[0][1], ksteps[0][2])
+        chain_k = ops.GemvChain(ksteps)
+        kstep = lambda: chain_k.run(stream)  # noqa: E731
+    else:
+        kstep = lambda: dec_k.step(x)  # noqa: E731
     with torch.cuda.stream(stream):
-        dec_k.step(x)
+        kstep()
     with torch.cuda.graph(graph_k, stream=stream):
-        dec_k.step(x)
+        kstep()
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             graph_k.replay()
@@ -980,7 +1022,8 @@ def run_tp(args):
     per_gpu_kern = float(mb.item()) / (ms_kern / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(per_gpu_kern, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(per_gpu_kern / peak, 4), "traffic": None, "peak_source": src,
-                "kernel": "gemv_i4_m1_kernel (per GPU, collectives removed)",
+                "kernel": ("gemv_i4_chain_kernel" if use_chain else "gemv_i4_m1_kernel") +
+                          " (per GPU, collectives removed)",
                 "kernels_only_aggregate_gbs": round(full_bytes / (ms_kern / 1e3) / 1e9, 1)}
 
     # e2e: hidden state in from pinned host memory, gathered logits back, every step
@@ -1007,9 +1050,13 @@ def run_tp(args):
             "config": {"workload": "configs[4]: the configs[1] stream tensor-parallel over the GPUs",
                        "scales": args.scales, "layers": args.layers, "parallelism": f"tp{world}",
                        "sharding": "q/k/v/gate/up/lm_head by output columns, o/down by input rows (256-aligned "
-                                   "shards); q|k|v and gate|up fused launches; 2 all-reduces per layer + "
+                                   "shards); q|k|v and gate|up fused; 2 all-reduces per layer + "
                                    "logits all-gather (NCCL), inside one CUDA graph",
-                       "allreduce": "g4b_allreduce_f32 over NVLink peer memory" if peer is not None else "NCCL",
+                       "schedule": ("one persistent GEMV-chain launch per token, all-reduces inside it "
+                                    "(g4b_gemv_chain_create_tp)" if use_chain else
+                                    "one launch per (fused) GEMV"),
+                       "allreduce": ("in-chain, NVLink peer stores of {value, epoch} words" if use_chain else
+                                     "g4b_allreduce_f32 over NVLink peer memory" if peer is not None else "NCCL"),
                        "l2": "working set per GPU > 126 MB L2, no flush needed"},
             "roofline": roofline, "cpu_baseline": None,
             "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": HIDDEN * 4,
@@ -1020,6 +1067,10 @@ def run_tp(args):
     dist.barrier()
     if peer is not None:
         peer.close()
+    if chain is not None:
+        chain.close()
+        chain_k.close()
+        xchg.close()
     dist.destroy_process_group()
 
 

@@ -673,8 +673,62 @@ struct M1Args {
     unsigned* counters;  // [ntiles]
     TcSeg seg0, seg1, seg2;
     int nseg, K, noct, ntiles, G, maxseg, stage_bytes, s_bytes;
+    int mode;            // partition of the items over the CTAs (kM1Balanced ...)
     long long total;
 };
+
+// How an M = 1 launch splits its total = ntiles * noct items (item = tile *
+// noct + k-chunk) over its G CTAs; every CTA owns one contiguous range.
+//   balanced     CTA c owns [c*T/G, (c+1)*T/G): the fewest items per CTA, but
+//                a CTA can straddle two shared tiles (two split-K flushes, the
+//                items of one tile after the other's);
+//   tile split   ntiles < G: tile t's k-chunks split evenly over n_t CTAs,
+//                n_t = G/ntiles, one more for the first G%ntiles tiles;
+//   whole tiles  ntiles >= G: CTA c owns tiles [c*ntiles/G, (c+1)*ntiles/G).
+constexpr int kM1Balanced = 0;
+constexpr int kM1TileSplit = 1;
+constexpr int kM1WholeTiles = 2;
+
+__host__ __device__ __forceinline__ void m1_range(int mode, long long total, int ntiles, int noct, int G, int c,
+                                                  long long& ib, long long& ie) {
+    if (mode == kM1TileSplit) {
+        const int q = G / ntiles, r = G % ntiles;
+        int t, k, n;
+        if (c < r * (q + 1)) {
+            t = c / (q + 1);
+            k = c - t * (q + 1);
+            n = q + 1;
+        } else {
+            const int c2 = c - r * (q + 1);
+            t = r + c2 / q;
+            k = c2 - (t - r) * q;
+            n = q;
+        }
+        ib = (long long)t * noct + k * noct / n;
+        ie = (long long)t * noct + (k + 1) * noct / n;
+    } else if (mode == kM1WholeTiles) {
+        ib = (long long)c * ntiles / G * noct;
+        ie = (long long)(c + 1) * ntiles / G * noct;
+    } else {
+        ib = (long long)c * total / G;
+        ie = (long long)(c + 1) * total / G;
+    }
+}
+
+// The first and last CTA that own items of tile t (whole tiles: one CTA).
+__host__ __device__ __forceinline__ void m1_span(int mode, long long total, int ntiles, int noct, int G, long long t,
+                                                 long long& cf, long long& cl) {
+    if (mode == kM1TileSplit) {
+        const int q = G / ntiles, r = G % ntiles;
+        cf = t < r ? t * (q + 1) : (long long)r * (q + 1) + (t - r) * q;
+        cl = cf + q + (t < r ? 1 : 0) - 1;
+    } else if (mode == kM1WholeTiles) {
+        cf = cl = 0;  // never needed: every tile is single-owned
+    } else {
+        cf = ((t * noct + 1) * G - 1) / total;
+        cl = (((t + 1) * noct) * G - 1) / total;
+    }
+}
 
 __device__ __forceinline__ uint32_t nib_sub(uint32_t P, int j) {
     const uint32_t src = (j >= 2) ? (P >> 8) : P;
@@ -710,8 +764,8 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (kM1Stages + s); };
     // balanced contiguous item ranges: CTA c owns [c*T/G, (c+1)*T/G)
-    const long long ibeg = (long long)blockIdx.x * a.total / a.G;
-    const long long iend = (long long)(blockIdx.x + 1) * a.total / a.G;
+    long long ibeg, iend;
+    m1_range(a.mode, a.total, a.ntiles, a.noct, a.G, blockIdx.x, ibeg, iend);
     const int pw = kM1Consumers / 32;  // first producer warp
 
     if (tid == 0) {
@@ -726,8 +780,11 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
     }
     if (tid < 32) s_zero[tid] = 0u;
     // the split-K reduction needs every CTA's first tile: one division per CTA, here, in parallel
-    for (int c = tid; c < a.G; c += blockDim.x)
-        s_ftile[c] = (int)(((long long)c * a.total / a.G) / a.noct);
+    for (int c = tid; c < a.G; c += blockDim.x) {
+        long long ib, ie;
+        m1_range(a.mode, a.total, a.ntiles, a.noct, a.G, c, ib, ie);
+        s_ftile[c] = (int)(ib / a.noct);
+    }
     __syncthreads();
     pdl_launch_dependents();
 
@@ -791,8 +848,8 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
         const long long t_first = ibeg / a.noct, t_last = iend > ibeg ? (iend - 1) / a.noct : t_first - 1;
         // Sum a shared tile's partials in CTA order (deterministic) and write y.
         auto reduce_tile = [&](long long t) {
-            const long long c_first = ((t * a.noct + 1) * a.G - 1) / a.total;
-            const long long c_last = (((t + 1) * a.noct) * a.G - 1) / a.total;
+            long long c_first, c_last;
+            m1_span(a.mode, a.total, a.ntiles, a.noct, a.G, t, c_first, c_last);
             const int nseg = (int)(c_last - c_first + 1);
             if (ctid < kStTN) {
                 const int col = ctid;
@@ -964,9 +1021,10 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
             }
             named_bar_sync(1, kM1Consumers);
             const int c = blockIdx.x;
-            const long long c_first = ((t * a.noct + 1) * a.G - 1) / a.total;
-            const long long c_last = (((t + 1) * a.noct) * a.G - 1) / a.total;
-            const bool single = c_first == c_last;
+            // a tile is this CTA's alone when the CTA owns all its k-chunks
+            const bool single = ibeg <= t * a.noct && iend >= (t + 1) * a.noct;
+            long long c_first = 0, c_last = 0;
+            if (!single) m1_span(a.mode, a.total, a.ntiles, a.noct, a.G, t, c_first, c_last);
             const bool ok = !*abort_flag;
             const long long slot = (long long)c * a.maxseg + (t - ibeg / a.noct);
             if (ctid < kStTN && ok) {
@@ -981,39 +1039,25 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
                 }
             }
             if (!single) {
-                // publish this CTA's partial: one thread fences for the CTA (after the barrier) and
-                // arrives on the tile's counter; the last of the tile's CTAs to arrive reduces it
+                // publish this CTA's partial: one thread arrives for the CTA (after the barrier) with an
+                // acquire-release add on the tile's counter; the last of the tile's CTAs to arrive reduces it
                 named_bar_sync(1, kM1Consumers);
                 if (t < t_last) {
                     // not our final tile: do not stall the other consumers on the atomic; if we
                     // turn out to be the last arriver, the reduction runs after our last item
-                    if (ctid == 0 && ok) {
-                        __threadfence();
-                        if (atomicAdd(&a.counters[t], 1u) == (unsigned)(c_last - c_first)) s_pending = t;
-                    }
+                    if (ctid == 0 && ok && atom_add_acq_rel_gpu(&a.counters[t], 1u) == (unsigned)(c_last - c_first))
+                        s_pending = t;
                 } else {
-                    if (ctid == 0) {
-                        unsigned last = 0;
-                        if (ok) {
-                            __threadfence();
-                            last = atomicAdd(&a.counters[t], 1u) == (unsigned)(c_last - c_first) ? 1u : 0u;
-                        }
-                        s_last = last;
-                    }
+                    if (ctid == 0)
+                        s_last = ok && atom_add_acq_rel_gpu(&a.counters[t], 1u) == (unsigned)(c_last - c_first) ? 1u : 0u;
                     named_bar_sync(1, kM1Consumers);
-                    if (s_last) {
-                        __threadfence();
-                        reduce_tile(t);
-                    }
+                    if (s_last) reduce_tile(t);
                 }
             }
         }
         // the deferred reduction of an earlier tile this CTA was the last to finish
         named_bar_sync(1, kM1Consumers);
-        if (s_pending >= 0 && !*abort_flag) {
-            __threadfence();
-            reduce_tile(s_pending);
-        }
+        if (s_pending >= 0 && !*abort_flag) reduce_tile(s_pending);
     }
 
     __syncthreads();
@@ -1043,8 +1087,13 @@ struct ChainStep {
     const void* x;
     TcSeg seg0, seg1, seg2;
     const int* range;  // [G + 1]: CTA c < G owns items [range[c], range[c+1]); item = tile * noct + k-chunk
-    const int* cspan;  // [ntiles][2]: first and last CTA owning items of tile t
-    int nseg, K, noct, ntiles, G, pad_;
+    const int* cspan;  // [ntiles][2]: first and last CTA owning items of tile t (bit 31 of the first:
+                       // that CTA's range starts in an earlier tile)
+    int nseg, K, noct, ntiles, G;
+    // tensor parallel: yreg >= 0: every written y value of segment 0 is also pushed, tagged with the
+    // run's epoch, into slot [rank] of region yreg of every rank's exchange buffer; xreg >= 0: x is
+    // the rank-order sum of the world slots of region xreg (the all-reduce of the previous step's y)
+    int xreg, yreg, pad_;
 };
 static_assert(sizeof(ChainStep) % 8 == 0, "ChainStep is copied as 32-bit words");
 
@@ -1052,10 +1101,23 @@ struct ChainArgs {
     const ChainStep* steps;   // [nsteps], device memory
     const CUtensorMap* maps;  // [nsteps][2 * kTcMaxSeg]: weight maps, then scale maps; device memory
     unsigned* sync;           // [nsteps] tiles written per step, then the exit count and the abort word
-    float* partial;           // [2 * G][kStTN]: CTA c's partials of its first and its last tile
-    unsigned* counters;       // [maxtiles] split-K arrivals per tile
-    int nsteps, stage_bytes, s_bytes, maxtiles;
+    float* partial;           // [2][2 * G][kStTN]: CTA c's partials of its first and its last tile,
+                              // by step parity
+    unsigned* counters;       // [2][maxtiles] split-K arrivals per tile, by step parity
+    unsigned long long* const* peers;  // [world] exchange buffers (this rank's own at [rank]); null if world 1
+    int nsteps, stage_bytes, s_bytes, maxtiles, G, rank, world;
 };
+
+// exchange-buffer words: {f32 bits (low), run epoch (high)}; a 64-bit aligned
+// access is single-copy atomic, so a word that carries the epoch carries its value
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 
 __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned* p) {
     unsigned v;
@@ -1101,6 +1163,7 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
     __shared__ int s_abort;
     __shared__ __align__(16) uint32_t s_zero[32];  // B-fragment source for lanes that feed zeros
     __shared__ __align__(8) ChainStep s_step[2];   // the consumers' current and next step
+    __shared__ unsigned long long* s_peers[8];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x;
     volatile int* abort_flag = &s_abort;
@@ -1108,9 +1171,9 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
     constexpr int ssz = SFMT == G4B_SCALE_F16 ? 2 : 1;
     constexpr int kStepWords = (int)(sizeof(ChainStep) / 4);
     const int nsteps = ch.nsteps, stage_bytes = ch.stage_bytes, s_bytes = ch.s_bytes;
-    float* const partial = ch.partial;
-    unsigned* const counters = ch.counters;
     unsigned* const gabort = ch.sync + nsteps + 1;
+    // this run's epoch (the last CTA of the previous run advanced the count)
+    const unsigned epoch = *(volatile unsigned*)(ch.sync + nsteps + 2) + 1u;
     // the swizzle pattern repeats every 1024 bytes: align the stages to it
     const uint32_t raw0 = smem_u32(smem_raw);
     const uint32_t smem0 = (raw0 + 1023u) & ~1023u;
@@ -1142,6 +1205,7 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
     }
     if (tid < 32) s_zero[tid] = 0u;
     if (tid < kStepWords) reinterpret_cast<uint32_t*>(&s_step[0])[tid] = __ldg(reinterpret_cast<const uint32_t*>(ch.steps) + tid);
+    if (tid < ch.world && ch.peers) s_peers[tid] = ch.peers[tid];
     __syncthreads();
 
     if (warp == pw) {
@@ -1188,11 +1252,12 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
         bool stop = false;
         for (int j = 0; j < nsteps && !stop; j++) {
             const ChainStep* dj = ch.steps + j;
-            const int noct = dj->noct;
+            const int noct = dj->noct, K = dj->K, xreg = dj->xreg;
             const uint8_t* x = reinterpret_cast<const uint8_t*>(dj->x);
             int ibeg, iend;
             my_range(*dj, ibeg, iend);
-            if (iend > ibeg && j > 0) {
+            // an all-reduce input carries its own readiness (the epoch in every word): no step wait
+            if (iend > ibeg && j > 0 && xreg < 0) {
                 const bool ok = chain_wait_count(&ch.sync[j - 1], (unsigned)ch.steps[j - 1].ntiles, gabort, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) break;
             }
@@ -1207,11 +1272,61 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
                         break;
                     }
                 }
-                const uint8_t* src = x + (size_t)o * kM1Rows * esz;
                 uint8_t* dst = smem + (size_t)s * stage_bytes + kM1WBytes + s_bytes;
-                #pragma unroll
-                for (int b = lane * 16; b < kM1Rows * esz; b += 512)
-                    *reinterpret_cast<uint4*>(dst + b) = __ldcg(reinterpret_cast<const uint4*>(src + b));
+                if (xreg < 0) {
+                    const uint8_t* src = x + (size_t)o * kM1Rows * esz;
+                    #pragma unroll
+                    for (int b = lane * 16; b < kM1Rows * esz; b += 512)
+                        *reinterpret_cast<uint4*>(dst + b) = __ldcg(reinterpret_cast<const uint4*>(src + b));
+                } else {
+                    // rows o*256 + 8*lane .. +8: the world ranks' words, polled until they carry this
+                    // run's epoch (bounded), summed in rank order
+                    const unsigned long long* base = s_peers[ch.rank] + xreg + (size_t)o * kM1Rows + 8 * lane;
+                    float v[8];
+                    #pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] = 0.f;
+                    bool ok = true;
+                    uint64_t t0 = 0;
+                    for (int r = 0; r < ch.world && ok; r++) {
+                        const unsigned long long* src = base + (size_t)r * K;
+                        #pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            unsigned long long w = ld_relaxed_sys_u64(src + e);
+                            while ((unsigned)(w >> 32) != epoch) {
+                                if (t0 == 0) t0 = global_ns();
+                                if (*abort_flag || *(volatile unsigned*)gabort) {
+                                    ok = false;
+                                    break;
+                                }
+                                if (global_ns() - t0 > kWaitLimitNs) {
+                                    atomicOr(&g_gemv_status, kStatusTimeout);
+                                    atomicExch(gabort, 1u);
+                                    ok = false;
+                                    break;
+                                }
+                                w = ld_relaxed_sys_u64(src + e);
+                            }
+                            v[e] += __uint_as_float((unsigned)w);
+                        }
+                    }
+                    if (!__all_sync(0xffffffffu, ok)) {
+                        if (lane == 0) *abort_flag = 1;
+                        stop = true;
+                        break;
+                    }
+                    if constexpr (XF32) {
+                        float4* d4 = reinterpret_cast<float4*>(dst + 32 * lane);
+                        d4[0] = make_float4(v[0], v[1], v[2], v[3]);
+                        d4[1] = make_float4(v[4], v[5], v[6], v[7]);
+                    } else {
+                        uint4 h;
+                        h.x = pack_half2(__float2half_rn(v[0]), __float2half_rn(v[1]));
+                        h.y = pack_half2(__float2half_rn(v[2]), __float2half_rn(v[3]));
+                        h.z = pack_half2(__float2half_rn(v[4]), __float2half_rn(v[5]));
+                        h.w = pack_half2(__float2half_rn(v[6]), __float2half_rn(v[7]));
+                        *reinterpret_cast<uint4*>(dst + 16 * lane) = h;
+                    }
+                }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(full_bar(s));
                 if (++o == noct) o = 0;
@@ -1233,6 +1348,10 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
         unsigned ndone = 0;  // ctid 0: tiles of the current step whose y this CTA wrote
 
         for (int j = 0; j < nsteps; j++) {
+            // step j's partials and arrival counters are step j-2's: every tile of step j-2 (its
+            // reductions included) is written before they are reused (normally long since)
+            if (j >= 2 && ctid == 0)
+                chain_wait_count(&ch.sync[j - 2], (unsigned)ch.steps[j - 2].ntiles, gabort, abort_flag);
             // every consumer is done with step j-1, whose descriptor slot now takes step j+1's
             named_bar_sync(1, kM1Consumers);
             if (j + 1 < nsteps && ctid < kStepWords)
@@ -1241,23 +1360,33 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
             const ChainStep& d = s_step[j & 1];
             int ibeg, iend;
             my_range(d, ibeg, iend);
-            // y[n] of the tile's segment, scaled by its e4m3 inverse scale
+            float* const partial = ch.partial + (size_t)(j & 1) * 2 * ch.G * kStTN;
+            unsigned* const counters = ch.counters + (size_t)(j & 1) * ch.maxtiles;
+            // y[n] of the tile's segment, scaled by its e4m3 inverse scale; a step whose y is
+            // all-reduced also pushes the value to slot [rank] of every rank's exchange region
             auto write_y = [&](int t, int col, float v) {
                 const TcSeg& sgm = tc_seg(d, tc_seg_of(d, t));
                 const int n = (t - sgm.tile0) * kStTN + col;
                 const float inv = SFMT == G4B_SCALE_E4M3 ? sgm.inv : 1.0f;
                 if (n < sgm.N) {
-                    if (YF32) ((float*)sgm.y)[n] = v * inv;
-                    else ((__half*)sgm.y)[n] = __float2half_rn(v * inv);
+                    const float y = v * inv;
+                    if (YF32) ((float*)sgm.y)[n] = y;
+                    else ((__half*)sgm.y)[n] = __float2half_rn(y);
+                    if (d.yreg >= 0) {
+                        const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(y);
+                        const size_t at = (size_t)d.yreg + (size_t)ch.rank * sgm.N + n;
+                        for (int p = 0; p < ch.world; p++) st_relaxed_sys_u64(s_peers[p] + at, w);
+                    }
                 }
             };
             float acc[2][2];
             const int t_first = ibeg / d.noct, t_last = iend > ibeg ? (iend - 1) / d.noct : t_first - 1;
-            // partial slot of CTA cc's share of tile t: its first tile or its last
-            auto slot_of = [&](int cc, int t) { return 2 * cc + (t == __ldg(d.range + cc) / d.noct ? 0 : 1); };
-            // Sum a shared tile's partials in CTA order (deterministic) and write y.
+            // Sum a shared tile's partials in CTA order (deterministic) and write y.  CTA cc keeps
+            // its share of its first tile in slot 2cc and of its last in 2cc + 1; only the tile's first
+            // CTA can have started in an earlier tile (bit 31 of cspan[2t]), every later one starts in t.
             auto reduce_tile = [&](int t) {
-                const int c_first = __ldg(d.cspan + 2 * t), c_last = __ldg(d.cspan + 2 * t + 1);
+                const unsigned f = (unsigned)__ldg(d.cspan + 2 * t);
+                const int c_first = (int)(f & 0x7fffffffu), c_last = __ldg(d.cspan + 2 * t + 1);
                 if (ctid < kStTN) {
                     const int col = ctid;
                     float v = 0.f;
@@ -1266,7 +1395,9 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
                         #pragma unroll
                         for (int k = 0; k < 8; k++) {
                             pv[k] = 0.f;
-                            if (k0 + k <= c_last) pv[k] = __ldcg(&partial[(size_t)slot_of(k0 + k, t) * kStTN + col]);
+                            const int cc = k0 + k;
+                            const int sl = 2 * cc + (cc == c_first ? (int)(f >> 31) : 0);
+                            if (cc <= c_last) pv[k] = __ldcg(&partial[(size_t)sl * kStTN + col]);
                         }
                         #pragma unroll
                         for (int k = 0; k < 8; k++)
@@ -1436,29 +1567,19 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
                 if (single) {
                     if (ctid == 0 && ok) ndone++;
                 } else {
-                    // publish this CTA's partial: one thread fences for the CTA (after the barrier) and
-                    // arrives on the tile's counter; the last of the tile's CTAs to arrive reduces it
+                    // publish this CTA's partial: one thread arrives for the CTA (after the barrier) with an
+                    // acquire-release add on the tile's counter; the last of the tile's CTAs to arrive reduces it
                     named_bar_sync(1, kM1Consumers);
-                    const unsigned sharers = (unsigned)(__ldg(d.cspan + 2 * t + 1) - __ldg(d.cspan + 2 * t));
+                    const unsigned sharers =
+                        (unsigned)(__ldg(d.cspan + 2 * t + 1) - (int)((unsigned)__ldg(d.cspan + 2 * t) & 0x7fffffffu));
                     if (t < t_last) {
                         // not our final tile: do not stall the other consumers on the atomic; if we
                         // turn out to be the last arriver, the reduction runs after our last item
-                        if (ctid == 0 && ok) {
-                            __threadfence();
-                            if (atomicAdd(&counters[t], 1u) == sharers) s_pending = t;
-                        }
+                        if (ctid == 0 && ok && atom_add_acq_rel_gpu(&counters[t], 1u) == sharers) s_pending = t;
                     } else {
-                        if (ctid == 0) {
-                            unsigned last = 0;
-                            if (ok) {
-                                __threadfence();
-                                last = atomicAdd(&counters[t], 1u) == sharers ? 1u : 0u;
-                            }
-                            s_last = last;
-                        }
+                        if (ctid == 0) s_last = ok && atom_add_acq_rel_gpu(&counters[t], 1u) == sharers ? 1u : 0u;
                         named_bar_sync(1, kM1Consumers);
                         if (s_last) {
-                            __threadfence();
                             reduce_tile(t);
                             if (ctid == 0) ndone++;
                         }
@@ -1468,7 +1589,6 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
             // the deferred reduction of an earlier tile this CTA was the last to finish
             named_bar_sync(1, kM1Consumers);
             if (s_pending >= 0 && !*abort_flag) {
-                __threadfence();
                 reduce_tile(s_pending);
                 if (ctid == 0) ndone++;
             }
@@ -1476,10 +1596,7 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
             named_bar_sync(1, kM1Consumers);
             if (ctid == 0) {
                 s_pending = -1;
-                if (ndone) {
-                    __threadfence();
-                    atomicAdd(&ch.sync[j], ndone);
-                }
+                if (ndone) red_add_release_gpu(&ch.sync[j], ndone);
                 ndone = 0;
                 if (*abort_flag) atomicExch(gabort, 1u);
             }
@@ -1509,15 +1626,16 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
             const bool aborted = *(volatile unsigned*)gabort != 0u;
             for (int j = 0; j < nsteps; j++) ch.sync[j] = 0u;
             if (aborted)
-                for (int t = 0; t < ch.maxtiles; t++) counters[t] = 0u;
+                for (int t = 0; t < 2 * ch.maxtiles; t++) ch.counters[t] = 0u;
             *gabort = 0u;
+            ch.sync[nsteps + 2] = epoch;  // the next run's epoch is one more
             ch.sync[nsteps] = 0u;
         }
     }
 }
 
 struct M1Plan {
-    int ntiles, noct, G, maxseg, stage_bytes, s_bytes;
+    int ntiles, noct, G, maxseg, stage_bytes, s_bytes, mode;
     long long total;
     size_t smem, ws_bytes;
 };
@@ -1529,15 +1647,34 @@ static M1Plan m1_plan(int nseg, const int* Ns, int K, int sms, bool xf32, int sf
     for (int i = 0; i < nseg; i++) p.ntiles += (Ns[i] + kStTN - 1) / kStTN;
     p.total = (long long)p.ntiles * p.noct;
     p.G = (int)std::max<long long>(1, std::min<long long>(std::min(std::max(sms, 1), kMaxCtas), p.total));
-    const long long lmax = (p.total + p.G - 1) / p.G;
-    p.maxseg = (int)((lmax + p.noct - 1) / p.noct + 1);
     p.s_bytes = 8 * kStTN * (sfmt == G4B_SCALE_F16 ? 2 : 1);
     p.stage_bytes = (kM1WBytes + p.s_bytes + kM1Rows * (xf32 ? 4 : 2) + 1023) & ~1023;  // swizzle atoms stay aligned
     p.smem = (size_t)kM1Stages * p.stage_bytes + 1024;                                     // + base alignment slack
+    // the tile-aligned partition unless it costs more than one item over the balanced one's longest range
+    // plus a straddle (a CTA running two shared tiles one after the other)
+    const long long max_bal = (p.total + p.G - 1) / p.G;
+    bool straddle = false;
+    for (int c = 0; c < p.G && !straddle; c++) {
+        const long long ib = (long long)c * p.total / p.G, ie = (long long)(c + 1) * p.total / p.G;
+        if ((ie - 1) / p.noct > ib / p.noct && (ib % p.noct || ie % p.noct)) straddle = true;
+    }
+    const int ta_mode = p.ntiles >= p.G ? kM1WholeTiles : kM1TileSplit;
+    long long max_ta = 0;
+    for (int c = 0; c < p.G; c++) {
+        long long ib, ie;
+        m1_range(ta_mode, p.total, p.ntiles, p.noct, p.G, c, ib, ie);
+        max_ta = std::max(max_ta, ie - ib);
+    }
+    p.mode = max_ta <= max_bal + (straddle ? 1 : 0) ? ta_mode : kM1Balanced;
+    // partial slots per CTA: the most tiles a CTA's range touches, plus one (balanced ranges)
+    p.maxseg = p.mode == kM1Balanced ? (int)((max_bal + p.noct - 1) / p.noct + 1) : 1;
     // a tile is split across CTAs unless every CTA boundary falls on a tile boundary
     bool multi = false;
-    for (int c = 1; c < p.G && !multi; c++)
-        if (((long long)c * p.total / p.G) % p.noct) multi = true;
+    for (int c = 0; c < p.G && !multi; c++) {
+        long long ib, ie;
+        m1_range(p.mode, p.total, p.ntiles, p.noct, p.G, c, ib, ie);
+        if (ib % p.noct || ie % p.noct) multi = true;
+    }
     if (multi) p.ws_bytes = kGemvCounterBytes + (((size_t)p.G * p.maxseg * kStTN * sizeof(float) + 255) & ~(size_t)255);
     return p;
 }
@@ -2207,6 +2344,7 @@ static int run_m1(const void* x, int x_dtype, int nseg, const g4b_gemv_segment* 
     a.ntiles = p.ntiles;
     a.G = p.G;
     a.maxseg = p.maxseg;
+    a.mode = p.mode;
     a.total = p.total;
     a.stage_bytes = p.stage_bytes;
     a.s_bytes = p.s_bytes;
@@ -2659,8 +2797,9 @@ int g4b_gemv_i4_fused(const void* x, int x_dtype, int nseg, const g4b_gemv_segme
 // ------------------------------------------------------------ GEMV chains
 struct g4b_gemv_chain {
     int device = -1, nsteps = 0, x_dtype = 0, scale_fmt = 0, y_dtype = 0;
-    int grid = 0, stage_bytes = 0, s_bytes = 0, maxtiles = 0;
-    size_t smem = 0, sync_bytes = 0, ws_bytes = 0;
+    int grid = 0, stage_bytes = 0, s_bytes = 0, maxtiles = 0, rank = 0, world = 1;
+    size_t smem = 0, counter_bytes = 0, sync_bytes = 0, ws_bytes = 0;
+    void* const* peers = nullptr;  // device array of the world exchange buffers (tensor parallel)
     // device: [nsteps][6] CUtensorMap, then [nsteps] ChainStep, then the steps' range / cspan tables
     void* plan = nullptr;
 };
@@ -2755,13 +2894,39 @@ static cudaError_t chain_launch(const g4b_gemv_chain* c, const ChainArgs& ch, cu
 
 }  // namespace g4b
 
+// Exchange-buffer words (u64) the steps' all-reduces need: world slots of N
+// words per flagged step; -1 if the flags are inconsistent.
+static long long chain_exchange_words(const g4b_gemv_chain_step* steps, int nsteps, int world) {
+    long long words = 0;
+    for (int j = 0; j < nsteps; j++) {
+        if (!(steps[j].flags & G4B_CHAIN_ALLREDUCE)) continue;
+        if (j + 1 >= nsteps || steps[j].nseg != 1 || steps[j + 1].K != steps[j].seg[0].N) return -1;
+        words += (long long)world * steps[j].seg[0].N;
+    }
+    return words;
+}
+
 extern "C" {
+
+size_t g4b_gemv_chain_exchange_bytes(const g4b_gemv_chain_step* steps, int nsteps, int world) {
+    if (!steps || nsteps < 1 || world < 1 || world > 8) return 0;
+    const long long w = chain_exchange_words(steps, nsteps, world);
+    return w < 0 ? 0 : (size_t)w * sizeof(unsigned long long);
+}
 
 int g4b_gemv_chain_create(const g4b_gemv_chain_step* steps, int nsteps, int x_dtype, int scale_fmt, int y_dtype,
                           g4b_gemv_chain** chain) {
+    return g4b_gemv_chain_create_tp(steps, nsteps, x_dtype, scale_fmt, y_dtype, nullptr, 0, 1, 0, chain);
+}
+
+int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x_dtype, int scale_fmt, int y_dtype,
+                             void* const* peers_dev, int rank, int world, size_t exchange_bytes,
+                             g4b_gemv_chain** chain) {
     G4B_ENTRY("gemv_chain_create");
     G4B_REQUIRE(steps && chain, G4B_E_ARG, "gemv_chain_create: NULL pointer argument");
     *chain = nullptr;
+    G4B_REQUIRE(world >= 1 && world <= 8 && rank >= 0 && rank < world, G4B_E_ARG,
+                "gemv_chain_create: rank %d / world %d (1..8 ranks)", rank, world);
     G4B_REQUIRE(nsteps >= 1 && nsteps <= kChainMaxSteps, G4B_E_ARG, "gemv_chain_create: nsteps=%d (1..%d)", nsteps,
                 kChainMaxSteps);
     G4B_REQUIRE(x_dtype == G4B_DT_F32 || x_dtype == G4B_DT_F16, G4B_E_ARG, "gemv_chain_create: bad x_dtype %d",
@@ -2770,10 +2935,22 @@ int g4b_gemv_chain_create(const g4b_gemv_chain_step* steps, int nsteps, int x_dt
                 y_dtype);
     G4B_REQUIRE(scale_fmt == G4B_SCALE_F16 || scale_fmt == G4B_SCALE_E4M3, G4B_E_ARG,
                 "gemv_chain_create: bad scale_fmt %d", scale_fmt);
+    const long long xwords = chain_exchange_words(steps, nsteps, world);
+    G4B_REQUIRE(xwords >= 0, G4B_E_ARG,
+                "gemv_chain_create: an all-reduced step needs one segment and a next step with K = its N");
+    G4B_REQUIRE(xwords == 0 || (peers_dev && world > 1), G4B_E_ARG,
+                "gemv_chain_create: all-reduced steps need the exchange buffers of 2 or more ranks");
+    G4B_REQUIRE((size_t)xwords * sizeof(unsigned long long) <= exchange_bytes || xwords == 0, G4B_E_WORKSPACE,
+                "gemv_chain_create: the all-reduces need %lld exchange bytes, got %zu",
+                xwords * (long long)sizeof(unsigned long long), exchange_bytes);
     for (int j = 0; j < nsteps; j++) {
         const g4b_gemv_chain_step& st = steps[j];
-        G4B_REQUIRE(st.x, G4B_E_ARG, "gemv_chain_create: step %d has a NULL x", j);
-        G4B_REQUIRE(aligned16(st.x), G4B_E_ALIGN, "gemv_chain_create: step %d x must be 16-byte aligned", j);
+        G4B_REQUIRE((st.flags & ~(unsigned)G4B_CHAIN_ALLREDUCE) == 0, G4B_E_ARG,
+                    "gemv_chain_create: step %d has unknown flags 0x%x", j, st.flags);
+        const bool x_from_peers = j > 0 && (steps[j - 1].flags & G4B_CHAIN_ALLREDUCE);
+        G4B_REQUIRE(st.x || x_from_peers, G4B_E_ARG, "gemv_chain_create: step %d has a NULL x", j);
+        G4B_REQUIRE(x_from_peers || aligned16(st.x), G4B_E_ALIGN,
+                    "gemv_chain_create: step %d x must be 16-byte aligned", j);
         G4B_REQUIRE(st.nseg >= 1 && st.nseg <= kTcMaxSeg, G4B_E_ARG, "gemv_chain_create: step %d nseg=%d (1..%d)", j,
                     st.nseg, kTcMaxSeg);
         G4B_REQUIRE(st.K > 0 && st.K % 256 == 0, G4B_E_SHAPE, "gemv_chain_create: step %d K=%d must be a multiple of 256",
@@ -2812,11 +2989,19 @@ int g4b_gemv_chain_create(const g4b_gemv_chain_step* steps, int nsteps, int x_dt
     std::vector<int> tables;           // every step's range[G + 1] and cspan[ntiles][2]
     std::vector<size_t> range_at(nsteps), cspan_at(nsteps);
     int grid = 1, maxtiles = 0;
+    long long region = 0;  // next free exchange word
     for (int j = 0; j < nsteps; j++) {
         const g4b_gemv_chain_step& cs = steps[j];
         ChainStep& d = hsteps[j];
         d = ChainStep{};
         d.x = cs.x;
+        d.xreg = -1;
+        d.yreg = -1;
+        if (j > 0 && (steps[j - 1].flags & G4B_CHAIN_ALLREDUCE)) d.xreg = hsteps[j - 1].yreg;
+        if (cs.flags & G4B_CHAIN_ALLREDUCE) {
+            d.yreg = (int)region;
+            region += (long long)world * cs.seg[0].N;
+        }
         TcSeg* dst[kTcMaxSeg] = {&d.seg0, &d.seg1, &d.seg2};
         const uint32_t* wps[kTcMaxSeg];
         const void* scs[kTcMaxSeg];
@@ -2854,7 +3039,8 @@ int g4b_gemv_chain_create(const g4b_gemv_chain_step* steps, int nsteps, int x_dt
             // whose range holds the tile's first k-chunk
             for (int t = tf; t <= tl; t++) {
                 cspan[2 * t + 1] = cc;
-                if (t != tf || range[cc] % d.noct == 0) cspan[2 * t] = cc;
+                if (t != tf) cspan[2 * t] = cc | (int)0x80000000u;  // cc's share of t sits in its last slot
+                else if (range[cc] % d.noct == 0) cspan[2 * t] = cc;
             }
         }
         tables.insert(tables.end(), cspan.begin(), cspan.end());
@@ -2912,9 +3098,13 @@ int g4b_gemv_chain_create(const g4b_gemv_chain_step* steps, int nsteps, int x_dt
     c->s_bytes = 8 * kStTN * ssz;
     c->maxtiles = maxtiles;
     c->smem = smem;
-    c->sync_bytes = ((size_t)(nsteps + 2) * sizeof(unsigned) + 255) & ~(size_t)255;
-    c->ws_bytes = kGemvCounterBytes + c->sync_bytes + (size_t)2 * grid * kStTN * sizeof(float);
+    c->counter_bytes = ((size_t)2 * maxtiles * sizeof(unsigned) + 255) & ~(size_t)255;
+    c->sync_bytes = ((size_t)(nsteps + 3) * sizeof(unsigned) + 255) & ~(size_t)255;
+    c->ws_bytes = c->counter_bytes + c->sync_bytes + (size_t)2 * 2 * grid * kStTN * sizeof(float);
     c->plan = plan;
+    c->peers = peers_dev;
+    c->rank = rank;
+    c->world = world;
     *chain = c;
     return G4B_OK;
 }
@@ -2937,13 +3127,18 @@ int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_b
     ch.maps = reinterpret_cast<const CUtensorMap*>(chain->plan);
     ch.steps = reinterpret_cast<const ChainStep*>(reinterpret_cast<const uint8_t*>(chain->plan) +
                                                   chain_maps_bytes(chain->nsteps));
-    ch.counters = reinterpret_cast<unsigned*>(workspace);
-    ch.sync = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(workspace) + kGemvCounterBytes);
-    ch.partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + kGemvCounterBytes + chain->sync_bytes);
+    uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+    ch.counters = reinterpret_cast<unsigned*>(ws);
+    ch.sync = reinterpret_cast<unsigned*>(ws + chain->counter_bytes);
+    ch.partial = reinterpret_cast<float*>(ws + chain->counter_bytes + chain->sync_bytes);
+    ch.peers = reinterpret_cast<unsigned long long* const*>(chain->peers);
     ch.nsteps = chain->nsteps;
     ch.stage_bytes = chain->stage_bytes;
     ch.s_bytes = chain->s_bytes;
     ch.maxtiles = chain->maxtiles;
+    ch.G = chain->grid;
+    ch.rank = chain->rank;
+    ch.world = chain->world;
     cudaError_t e = chain_launch(chain, ch, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain_run: launch: %s", cudaGetErrorString(e));
     count_launch();

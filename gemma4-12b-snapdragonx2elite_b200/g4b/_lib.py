@@ -24,6 +24,7 @@ G4B_E_WORKSPACE = -7
 G4B_E_TIMEOUT = -8
 
 GEMV_PDL = 1
+CHAIN_ALLREDUCE = 1
 DT_F32 = 0
 DT_F16 = 1
 SCALE_F16 = 0
@@ -77,6 +78,8 @@ SIGNATURES = {
     "g4b_gemm_w8a8": (_I, [_P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _P]),
     "g4b_gemm_w4a8": (_I, [_P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _I, _P]),
     "g4b_gemv_chain_create": (_I, [_P, _I, _I, _I, _I, C.POINTER(_P)]),
+    "g4b_gemv_chain_exchange_bytes": (_Z, [_P, _I, _I]),
+    "g4b_gemv_chain_create_tp": (_I, [_P, _I, _I, _I, _I, _P, _I, _I, _Z, C.POINTER(_P)]),
     "g4b_gemv_chain_workspace_bytes": (_Z, [_P]),
     "g4b_gemv_chain_run": (_I, [_P, _P, _Z, _P]),
     "g4b_gemv_chain_destroy": (None, [_P]),
@@ -90,7 +93,8 @@ class GemvSegment(C.Structure):
 
 class GemvChainStep(C.Structure):
     """struct g4b_gemv_chain_step (include/g4b.h)."""
-    _fields_ = [("x", C.c_void_p), ("K", C.c_int), ("nseg", C.c_int), ("seg", GemvSegment * 3)]
+    _fields_ = [("x", C.c_void_p), ("K", C.c_int), ("nseg", C.c_int), ("seg", GemvSegment * 3),
+                ("flags", C.c_uint)]
 
 
 class G4BError(RuntimeError):

@@ -172,39 +172,69 @@ def gemv_i4_fused(x: torch.Tensor, ws_: list, outs: Optional[list] = None, out_d
 class GemvChain:
     """A recorded chain of M = 1 GEMV steps run as one persistent launch
     (g4b_gemv_chain_*): the engine's per-token command buffer of gemv()
-    dispatches with a barrier after each.  Each step is (x, [weights], [outs]):
-    1 to 3 GEMVs that read x; a step may read any earlier step's output.
+    dispatches with a barrier after each.  Each step is (x, [weights], [outs])
+    or (x, [weights], [outs], flags): 1 to 3 GEMVs that read x; a step may read
+    any earlier step's output.  Tensor parallel: with `exchange` (a
+    g4b.comm.PeerBuffers of exchange_bytes(steps, world) bytes), a step flagged
+    L.CHAIN_ALLREDUCE (one weight) has its output summed over the ranks inside
+    the launch, and the next step (x = None) reads that sum as its x.
     The tensors named in the steps must stay alive while the chain is used;
     `run` reads their current contents on every call."""
 
-    def __init__(self, steps: list, device: Optional[torch.device] = None):
+    @staticmethod
+    def exchange_bytes(steps: list, world: int) -> int:
+        return sum(8 * world * st[1][0].N for st in steps if len(st) > 3 and st[3] & L.CHAIN_ALLREDUCE)
+
+    def __init__(self, steps: list, device: Optional[torch.device] = None, exchange=None):
         if not steps:
             raise ValueError("GemvChain: no steps")
         self.lib = L.load()
-        x0, w0, o0 = steps[0]
+        x0, w0, o0 = steps[0][:3]
+        if x0 is None:
+            raise ValueError("GemvChain: the first step needs its x")
         self.device = x0.device if device is None else device
         self._keep = []
         arr = (L.GemvChainStep * len(steps))()
         fmt = w0[0].scale_fmt
-        for j, (x, ws_, outs) in enumerate(steps):
-            _need(x, "x")
+        prev_flags = 0
+        for j, st in enumerate(steps):
+            x, ws_, outs = st[:3]
+            flags = st[3] if len(st) > 3 else 0
             if not 1 <= len(ws_) <= 3 or len(outs) != len(ws_):
                 raise ValueError(f"GemvChain: step {j} needs 1 to 3 weights and one output per weight")
-            if x.dtype != x0.dtype or any(o.dtype != o0[0].dtype for o in outs):
-                raise ValueError("GemvChain: all steps share the x dtype and the output dtype")
-            if any(w.K != x.numel() or w.scale_fmt != fmt for w in ws_):
+            if x is None:
+                if not prev_flags & L.CHAIN_ALLREDUCE:
+                    raise ValueError(f"GemvChain: step {j} has no x and does not follow an all-reduced step")
+                K = ws_[0].K
+            else:
+                _need(x, "x")
+                if x.dtype != x0.dtype:
+                    raise ValueError("GemvChain: all steps share the x dtype")
+                K = x.numel()
+            if any(o.dtype != o0[0].dtype for o in outs):
+                raise ValueError("GemvChain: all steps share the output dtype")
+            if any(w.K != K or w.scale_fmt != fmt for w in ws_):
                 raise ValueError(f"GemvChain: step {j} weights must have K = x.numel() and one scale format")
             for o in outs:
                 _need(o, "out")
-            arr[j].x = _ptr(x)
-            arr[j].K = x.numel()
+            arr[j].x = _ptr(x) if x is not None else None
+            arr[j].K = K
             arr[j].nseg = len(ws_)
+            arr[j].flags = flags
             for i, (w, o) in enumerate(zip(ws_, outs)):
                 arr[j].seg[i] = L.GemvSegment(_ptr(w.wp), _ptr(w.scales), w.inv, _ptr(o), w.N)
             self._keep.append((x, ws_, outs))
+            prev_flags = flags
         h = ctypes.c_void_p()
-        L.check("g4b_gemv_chain_create", self.lib.g4b_gemv_chain_create(
-            ctypes.cast(arr, ctypes.c_void_p), len(steps), _DT[x0.dtype], fmt, _DT[o0[0].dtype], ctypes.byref(h)))
+        if exchange is None:
+            L.check("g4b_gemv_chain_create", self.lib.g4b_gemv_chain_create(
+                ctypes.cast(arr, ctypes.c_void_p), len(steps), _DT[x0.dtype], fmt, _DT[o0[0].dtype],
+                ctypes.byref(h)))
+        else:
+            self._keep.append(exchange)
+            L.check("g4b_gemv_chain_create_tp", self.lib.g4b_gemv_chain_create_tp(
+                ctypes.cast(arr, ctypes.c_void_p), len(steps), _DT[x0.dtype], fmt, _DT[o0[0].dtype],
+                exchange.ptrs.data_ptr(), exchange.rank, exchange.world, exchange.nbytes, ctypes.byref(h)))
         self.handle = h.value
         self.nsteps = len(steps)
         self.workspace_bytes = int(self.lib.g4b_gemv_chain_workspace_bytes(self.handle))

@@ -164,6 +164,26 @@ class TPDecoder:
         return b["logits"]
 
 
+def chain_steps(layers: List[TPLayer], lm_head, h, bufs: dict, allreduce_flag: int) -> list:
+    """One token of the tensor-parallel decode as GEMV chain steps
+    (g4b.ops.GemvChain): per layer q|k|v on the replicated hidden state, o on
+    this rank's q shard with its output all-reduced inside the chain, gate|up
+    on that sum, down on this rank's gate shard, all-reduced again; lm_head
+    last on the final sum.  `h` is the first layer's input (f32, hidden long);
+    `bufs` holds the per-rank outputs ("q", "k", "v", "part", "gate", "up",
+    "logits_local").  The logits all-gather follows the chain."""
+    steps = []
+    x = h
+    for L in layers:
+        steps.append((x, [L.q, L.k, L.v], [bufs["q"], bufs["k"], bufs["v"]]))
+        steps.append((bufs["q"], [L.o], [bufs["part"]], allreduce_flag))
+        steps.append((None, [L.gate, L.up], [bufs["gate"], bufs["up"]]))
+        steps.append((bufs["gate"], [L.down], [bufs["part"]], allreduce_flag))
+        x = None
+    steps.append((None, [lm_head], [bufs["logits_local"]]))
+    return steps
+
+
 def decode_reference(layers_full, lm_full, x, gemv_full):
     """The same chain on one device with unsharded weights (the check for TPDecoder)."""
     h = x

@@ -186,31 +186,50 @@ G4B_API int g4b_gemv_i4_fused(const void* x, int x_dtype, int nseg, const g4b_ge
  * earlier step wrote; a step starts reading x only after every column tile of
  * the step before it has been written.  The weight stream does not wait: a
  * step's packed words and scales are in flight while the previous step
- * finishes, so no launch ramp or split-K tail sits between the GEMVs.
- * Every step's y is bit-identical to g4b_gemv_i4_fused (or g4b_gemv_i4) on
- * the same x.
+ * finishes.  Each step's y equals g4b_gemv_i4_fused (or g4b_gemv_i4) on the
+ * same x up to f32 summation order; one chain gives the same bits every run.
  *
- *   create   validates the steps, encodes their TMA descriptors and copies the
- *            plan to device memory (setup time: allocates and synchronises);
- *            all steps share x_dtype, scale_fmt and y_dtype; per step
- *            1 <= nseg <= 3, K % 256 == 0, every N % 32 == 0, x and the
- *            weights 16-byte aligned.  The buffers named in the steps must
- *            stay allocated while the chain is used.
+ *   create   validates the steps, encodes their TMA descriptors, picks each
+ *            step's partition of work over the SMs and copies the plan to
+ *            device memory (setup time: allocates and synchronises); all steps
+ *            share x_dtype, scale_fmt and y_dtype; per step 1 <= nseg <= 3,
+ *            K % 256 == 0, every N % 32 == 0, x and the weights 16-byte
+ *            aligned.  The buffers named in the steps must stay allocated
+ *            while the chain is used.
  *   run      one launch on `stream` (cooperative: every CTA resident); the
  *            workspace (g4b_gemv_chain_workspace_bytes, 16-byte aligned) is
- *            zero-filled once before first use and left zero by every run.
- *            Never allocates or synchronises; capturable in a CUDA graph.
- *   destroy  frees the plan. */
+ *            zero-filled once before first use.  Never allocates or
+ *            synchronises; capturable in a CUDA graph.
+ *   destroy  frees the plan.
+ *
+ * Tensor parallel (create_tp): a step flagged G4B_CHAIN_ALLREDUCE (one
+ * segment: a row-parallel o / down shard) has its y summed over the `world`
+ * ranks inside the launch -- the cross-GPU counterpart of vk/reduce.comp:8-12.
+ * Every y value it writes is also stored, paired with the run's epoch in one
+ * 64-bit word, into slot [rank] of that all-reduce's region of every rank's
+ * exchange buffer (NVLink peer stores); the next step (K = that N; its x is
+ * ignored) reads each 256-row slice of x as the rank-order sum of the world
+ * slots once every word carries the epoch.  peers_dev is a device array of the
+ * world exchange buffers (this rank's own at [rank]: g4b_comm_alloc, mapped
+ * with g4b_ipc_open), each g4b_gemv_chain_exchange_bytes long and zero-filled
+ * once; every rank runs the same chain the same number of times.  Waits are
+ * bounded (2 s, then the kernel status word is raised). */
+#define G4B_CHAIN_ALLREDUCE 1u
 typedef struct g4b_gemv_chain g4b_gemv_chain;
 typedef struct g4b_gemv_chain_step {
-    const void* x;                 /* [K] activations of this step */
+    const void* x;                 /* [K] activations of this step (ignored after an all-reduced step) */
     int K;
     int nseg;
     g4b_gemv_segment seg[3];
+    unsigned flags;                /* 0 or G4B_CHAIN_ALLREDUCE */
 } g4b_gemv_chain_step;
 
 G4B_API int g4b_gemv_chain_create(const g4b_gemv_chain_step* steps, int nsteps, int x_dtype, int scale_fmt,
                                   int y_dtype, g4b_gemv_chain** chain);
+G4B_API size_t g4b_gemv_chain_exchange_bytes(const g4b_gemv_chain_step* steps, int nsteps, int world);
+G4B_API int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x_dtype, int scale_fmt,
+                                     int y_dtype, void* const* peers_dev, int rank, int world,
+                                     size_t exchange_bytes, g4b_gemv_chain** chain);
 G4B_API size_t g4b_gemv_chain_workspace_bytes(const g4b_gemv_chain* chain);
 G4B_API int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_bytes, g4b_stream_t stream);
 G4B_API void g4b_gemv_chain_destroy(g4b_gemv_chain* chain);

@@ -1,4 +1,4 @@
-"""Tensor-parallel decode on 2 GPUs (g4b.tp over NCCL), when the box has them.
+"""Tensor-parallel decode on 2 GPUs (g4b.tp), when the box has them.
 
 Runs tests/tp_worker.py under torch.distributed.run with 2 ranks: every rank
 streams its column / row shards of a 2-layer stack with g4b_gemv_i4 and two
@@ -27,10 +27,13 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("fp8,allreduce", [(False, "nccl"), (True, "nccl"), (False, "peer")])
+@pytest.mark.parametrize("fp8,allreduce", [(False, "nccl"), (True, "nccl"), (False, "peer"), (False, "chain"),
+                                           (True, "chain")])
 def test_tp_decode_two_gpus(fp8, allreduce):
     """allreduce="peer" also checks g4b_allreduce_f32 on its own: identical bits
-    on both ranks, equal to NCCL's sum, across repeated calls."""
+    on both ranks, equal to NCCL's sum, across repeated calls.  allreduce="chain"
+    runs each rank's token as one GEMV chain with the all-reduces inside it
+    (g4b_gemv_chain_create_tp), eager and replayed in a graph."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     env = dict(os.environ, TP_FP8="1" if fp8 else "0", TP_ALLREDUCE=allreduce)

@@ -140,3 +140,22 @@ def test_split_covers_and_rejects():
     with pytest.raises(ValueError):
         tp.split_range(256, 2, 0, 256)   # one unit cannot go to two ranks
     assert tp.validate_world(3840, 4096, 2048, 15360, 262144, 8) is None
+
+
+def test_chain_steps_layout():
+    """tp.chain_steps: per layer q|k|v, o (all-reduced), gate|up on the sum
+    (no x), down (all-reduced), then lm_head on the final sum."""
+    class W:
+        def __init__(self, N, K):
+            self.N, self.K = N, K
+    L = tp.TPLayer(q=W(512, 256), k=W(256, 256), v=W(256, 256), o=W(256, 512), gate=W(1024, 256),
+                   up=W(1024, 256), down=W(256, 1024))
+    bufs = {k: k for k in ("q", "k", "v", "part", "gate", "up", "logits_local")}
+    steps = tp.chain_steps([L, L], W(4096, 256), "h", bufs, 1)
+    assert len(steps) == 9
+    assert steps[0][0] == "h" and steps[4][0] is None and steps[8][0] is None
+    assert [len(st) > 3 and st[3] == 1 for st in steps] == [False, True, False, True] * 2 + [False]
+    assert steps[1][0] == "q" and steps[3][0] == "gate"
+    for j, st in enumerate(steps):
+        if len(st) > 3 and st[3]:
+            assert len(st[1]) == 1 and steps[j + 1][1][0].K == st[1][0].N

@@ -32,6 +32,7 @@ def main():
     dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
     L.load()
     fp8 = os.environ.get("TP_FP8") == "1"
+    use_chain = os.environ.get("TP_ALLREDUCE", "nccl") == "chain"
     use_peer = os.environ.get("TP_ALLREDUCE", "nccl") == "peer"
     peer = comm.PeerAllReduce(H, dev) if use_peer else None
     if peer is not None:
@@ -89,13 +90,29 @@ def main():
                        new_buffer=lambda n: torch.zeros(n, dtype=torch.float32, device=dev),
                        hidden=H, vocab=VOCAB, world=world, gemv_fused=gemv_fused)
     x = torch.randn((H,), generator=gen, device=dev)
+    xchg = None
+    if use_chain:
+        # the whole token as one persistent launch per rank, all-reduces inside it
+        b = dec.bufs
+        b["part"] = torch.zeros(H, dtype=torch.float32, device=dev)
+        steps = tp.chain_steps(mine, lm, x, b, L.CHAIN_ALLREDUCE)
+        xchg = comm.PeerBuffers(ops.GemvChain.exchange_bytes(steps, world), dev)
+        chain = ops.GemvChain(steps, exchange=xchg)
+
+        def step(_x):
+            chain.run(stream)
+            dist.all_gather_into_tensor(b["logits"], b["logits_local"])
+            return b["logits"]
+    else:
+        step = dec.step
     with torch.cuda.stream(stream):
-        logits = dec.step(x).clone()
+        logits = step(x).clone()
         # the same step captured in a CUDA graph (collectives included) and replayed
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            dec.step(x)
-        g.replay()
+            step(x)
+        for _ in range(3):
+            g.replay()
     stream.synchronize()
     replay = dec.bufs["logits"].clone()
     ok = torch.tensor([1], device=dev)
@@ -113,6 +130,9 @@ def main():
     del g
     if peer is not None:
         peer.close()
+    if xchg is not None:
+        chain.close()
+        xchg.close()
     dist.destroy_process_group()
     sys.exit(0 if ok.item() == 1 else 1)
 
