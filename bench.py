@@ -48,6 +48,9 @@ NQ, NKV = 16 * 256, 8 * 256
 LAYER_SHAPES = [("q", NQ, HIDDEN), ("k", NKV, HIDDEN), ("v", NKV, HIDDEN), ("o", HIDDEN, NQ),
                 ("gate", FFN, HIDDEN), ("up", FFN, HIDDEN), ("down", HIDDEN, FFN)]
 LM_HEAD = ("lm_head", VOCAB, HIDDEN)
+# tensor-parallel stream defaults: the schedule and all-reduce confirmed on 2 GPUs
+TP_DEFAULT_SCHEDULE = "launches"
+TP_DEFAULT_ALLREDUCE = "nccl"
 
 
 def stream_shapes(layers=LAYERS):
@@ -232,16 +235,16 @@ def main():
     ap.add_argument("--workload", default="stream", choices=["stream", "gemv", "prefill"] + list(GEMM_WORKLOADS),
                     help="stream: configs[1] decode weight stream (default); gemv: configs[0] single GEMV; "
                          "gemm_i4 / gemm_i4_down: configs[2] W4A16 prefill GEMM; w8a8 / w4a8: configs[3]")
-    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
-                    help="tensor-parallel stream: the per-layer all-reduce as one kernel over NVLink peer memory "
-                         "(g4b_allreduce_f32, default) or NCCL's")
+    ap.add_argument("--allreduce", default=None, choices=["peer", "nccl"],
+                    help="tensor-parallel stream with --schedule launches: the per-layer all-reduce as one kernel "
+                         f"over NVLink peer memory (g4b_allreduce_f32) or NCCL's (default: {TP_DEFAULT_ALLREDUCE})")
     ap.add_argument("--shape", default="config0", choices=["config0", "lm_head"],
                     help="gemv workload: config0 = W[15360, 3840] (configs[0]); lm_head = W[262144, 3840]")
-    ap.add_argument("--schedule", default="chain", choices=["chain", "launches"],
-                    help="stream: chain (default) runs the token's GEMVs as one persistent launch "
-                         "(g4b_gemv_chain: each step waits for every tile of the step before it; tensor parallel: "
-                         "the all-reduces run inside it); launches runs one launch per (fused) GEMV, chained by "
-                         "programmatic dependent launch")
+    ap.add_argument("--schedule", default=None, choices=["chain", "launches"],
+                    help="stream: chain runs the token's GEMVs as one persistent launch (g4b_gemv_chain: each "
+                         "step waits for every tile of the step before it; tensor parallel: the all-reduces run "
+                         "inside it); launches runs one launch per (fused) GEMV, chained by programmatic dependent "
+                         f"launch (default: chain on one GPU, {TP_DEFAULT_SCHEDULE} tensor parallel)")
     ap.add_argument("--unfused", action="store_true",
                     help="stream: launch all 337 GEMVs separately, each on its own x, instead of fusing "
                          "q|k|v and gate|up (which read the same x in a decode step)")
@@ -249,6 +252,12 @@ def main():
                     help="N > 1: tp (default) shards the stream's output columns / input rows over the GPUs "
                          "with NCCL all-reduces per layer; replicas streams a full copy per GPU")
     args = ap.parse_args()
+    tp_run = (args.workload == "stream" and int(os.environ.get("WORLD_SIZE", "1")) > 1
+              and args.parallel != "replicas")
+    if args.schedule is None:
+        args.schedule = TP_DEFAULT_SCHEDULE if tp_run else "chain"
+    if args.allreduce is None:
+        args.allreduce = TP_DEFAULT_ALLREDUCE
     if args.workload in GEMM_WORKLOADS:
         return run_gemm(args)
     if args.workload == "prefill":
@@ -455,7 +464,7 @@ def main():
         peak_src = "of fallback"
     roofline = {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(kern_gbs / peak, 4), "traffic": None, "peak_source": peak_src,
-                "kernel": "gemv_i4_m1_kernel<CHAIN>" if use_chain else "gemv_i4_m1_kernel",
+                "kernel": "gemv_i4_chain_kernel" if use_chain else "gemv_i4_m1_kernel",
                 "launches_timed": args.steps * len(ev_groups),
                 "avg_launch_us": round(kern_ms * 1e3 / (args.steps * len(ev_groups)), 3),
                 "per_shape_gbs": {k: round(v[2] * v[1] / (v[0] / 1e3) / 1e9, 1) for k, v in per_shape.items()},
@@ -465,7 +474,7 @@ def main():
         try:
             t = json.load(open(tp))
             if use_chain:
-                roofline["traffic"] = int(round(t["traffic_ratio"] * step_bytes))
+                roofline["traffic"] = int(round(t.get("chain_traffic_ratio", t["traffic_ratio"]) * step_bytes))
             else:
                 key = "lm_head" if args.workload == "gemv" and args.shape == "lm_head" else args.workload
                 roofline["traffic"] = t.get("bytes_per_launch_scaled", {}).get(key)
