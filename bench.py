@@ -48,8 +48,9 @@ NQ, NKV = 16 * 256, 8 * 256
 LAYER_SHAPES = [("q", NQ, HIDDEN), ("k", NKV, HIDDEN), ("v", NKV, HIDDEN), ("o", HIDDEN, NQ),
                 ("gate", FFN, HIDDEN), ("up", FFN, HIDDEN), ("down", HIDDEN, FFN)]
 LM_HEAD = ("lm_head", VOCAB, HIDDEN)
-# tensor-parallel stream defaults: the schedule and all-reduce confirmed on 2 GPUs
-TP_DEFAULT_SCHEDULE = "launches"
+# tensor-parallel stream defaults: one chain launch per token with the all-reduces inside it (fastest on 2 GPUs);
+# --schedule launches uses NCCL's all-reduce unless --allreduce peer
+TP_DEFAULT_SCHEDULE = "chain"
 TP_DEFAULT_ALLREDUCE = "nccl"
 
 

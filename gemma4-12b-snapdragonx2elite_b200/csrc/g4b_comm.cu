@@ -71,16 +71,30 @@ __global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(const float* 
     pdl_launch_dependents();
     __syncthreads();
     // 2-3. poll this rank's own buffer until every slot of this thread's elements
-    // carries the epoch (bounded), and sum in rank order
+    // carries the epoch (bounded), and sum in rank order.  A chunk's words are
+    // all loaded at once (one round trip); only words still without the epoch
+    // are loaded again.
     const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(bufs[rank]) + (size_t)half * world * n;
+    constexpr int kChunk = 8;  // elements per thread per round trip
     uint64_t t0 = 0;
     bool ok = true;
-    for (int i = tid; i < n && ok; i += kArThreads) {
-        float v = 0.f;
+    for (int i0 = tid; i0 < n && ok; i0 += kChunk * kArThreads) {
+        float v[kChunk];
+        #pragma unroll
+        for (int e = 0; e < kChunk; e++) v[e] = 0.f;
         for (int r = 0; r < world && ok; r++) {
-            const unsigned long long* src = mine + (size_t)r * n + i;
-            unsigned long long w = ld_relaxed_sys_u64(src);
-            while ((unsigned)(w >> 32) != epoch) {
+            const unsigned long long* src = mine + (size_t)r * n;
+            unsigned long long w[kChunk];
+            #pragma unroll
+            for (int e = 0; e < kChunk; e++) {
+                const int i = i0 + e * kArThreads;
+                w[e] = i < n ? ld_relaxed_sys_u64(src + i) : tag;
+            }
+            for (;;) {
+                bool all = true;
+                #pragma unroll
+                for (int e = 0; e < kChunk; e++) all = all && (unsigned)(w[e] >> 32) == epoch;
+                if (all) break;
                 if (t0 == 0) t0 = global_ns();
                 if (global_ns() - t0 > kWaitLimitNs) {
                     atomicOr(&g_comm_status, kStatusTimeout);
@@ -88,11 +102,22 @@ __global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(const float* 
                     break;
                 }
                 __nanosleep(32);
-                w = ld_relaxed_sys_u64(src);
+                #pragma unroll
+                for (int e = 0; e < kChunk; e++) {
+                    const int i = i0 + e * kArThreads;
+                    if ((unsigned)(w[e] >> 32) != epoch && i < n) w[e] = ld_relaxed_sys_u64(src + i);
+                }
             }
-            v += __uint_as_float((unsigned)w);
+            #pragma unroll
+            for (int e = 0; e < kChunk; e++) v[e] += __uint_as_float((unsigned)w[e]);
         }
-        if (ok) y[i] = v;
+        if (ok) {
+            #pragma unroll
+            for (int e = 0; e < kChunk; e++) {
+                const int i = i0 + e * kArThreads;
+                if (i < n) y[i] = v[e];
+            }
+        }
     }
     __syncthreads();
     if (tid == 0) *counter = epoch;  // the next call's epoch, also after a timeout

@@ -1280,7 +1280,8 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
                         *reinterpret_cast<uint4*>(dst + b) = __ldcg(reinterpret_cast<const uint4*>(src + b));
                 } else {
                     // rows o*256 + 8*lane .. +8: the world ranks' words, polled until they carry this
-                    // run's epoch (bounded), summed in rank order
+                    // run's epoch (bounded), summed in rank order.  A rank's 8 words are loaded at once
+                    // (one round trip); only words still without the epoch are loaded again.
                     const unsigned long long* base = s_peers[ch.rank] + xreg + (size_t)o * kM1Rows + 8 * lane;
                     float v[8];
                     #pragma unroll
@@ -1289,25 +1290,31 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
                     uint64_t t0 = 0;
                     for (int r = 0; r < ch.world && ok; r++) {
                         const unsigned long long* src = base + (size_t)r * K;
+                        unsigned long long w[8];
                         #pragma unroll
-                        for (int e = 0; e < 8; e++) {
-                            unsigned long long w = ld_relaxed_sys_u64(src + e);
-                            while ((unsigned)(w >> 32) != epoch) {
-                                if (t0 == 0) t0 = global_ns();
-                                if (*abort_flag || *(volatile unsigned*)gabort) {
-                                    ok = false;
-                                    break;
-                                }
-                                if (global_ns() - t0 > kWaitLimitNs) {
-                                    atomicOr(&g_gemv_status, kStatusTimeout);
-                                    atomicExch(gabort, 1u);
-                                    ok = false;
-                                    break;
-                                }
-                                w = ld_relaxed_sys_u64(src + e);
+                        for (int e = 0; e < 8; e++) w[e] = ld_relaxed_sys_u64(src + e);
+                        for (;;) {
+                            bool all = true;
+                            #pragma unroll
+                            for (int e = 0; e < 8; e++) all = all && (unsigned)(w[e] >> 32) == epoch;
+                            if (all) break;
+                            if (t0 == 0) t0 = global_ns();
+                            if (*abort_flag || *(volatile unsigned*)gabort) {
+                                ok = false;
+                                break;
                             }
-                            v[e] += __uint_as_float((unsigned)w);
+                            if (global_ns() - t0 > kWaitLimitNs) {
+                                atomicOr(&g_gemv_status, kStatusTimeout);
+                                atomicExch(gabort, 1u);
+                                ok = false;
+                                break;
+                            }
+                            #pragma unroll
+                            for (int e = 0; e < 8; e++)
+                                if ((unsigned)(w[e] >> 32) != epoch) w[e] = ld_relaxed_sys_u64(src + e);
                         }
+                        #pragma unroll
+                        for (int e = 0; e < 8; e++) v[e] += __uint_as_float((unsigned)w[e]);
                     }
                     if (!__all_sync(0xffffffffu, ok)) {
                         if (lane == 0) *abort_flag = 1;
