@@ -48,9 +48,10 @@ NQ, NKV = 16 * 256, 8 * 256
 LAYER_SHAPES = [("q", NQ, HIDDEN), ("k", NKV, HIDDEN), ("v", NKV, HIDDEN), ("o", HIDDEN, NQ),
                 ("gate", FFN, HIDDEN), ("up", FFN, HIDDEN), ("down", HIDDEN, FFN)]
 LM_HEAD = ("lm_head", VOCAB, HIDDEN)
-# tensor-parallel stream defaults: one chain launch per token with the all-reduces inside it (fastest on 2 GPUs);
-# --schedule launches uses NCCL's all-reduce unless --allreduce peer
-TP_DEFAULT_SCHEDULE = "chain"
+# tensor-parallel stream defaults: one chain launch per token with the all-reduces inside it where that has been
+# run on a B200 box (2 GPUs: the fastest schedule); wider worlds default to per-GEMV launches with NCCL's
+# all-reduce (--schedule chain selects the chain there too)
+TP_CHAIN_CONFIRMED_WORLDS = (2,)
 TP_DEFAULT_ALLREDUCE = "nccl"
 
 
@@ -245,7 +246,7 @@ def main():
                     help="stream: chain runs the token's GEMVs as one persistent launch (g4b_gemv_chain: each "
                          "step waits for every tile of the step before it; tensor parallel: the all-reduces run "
                          "inside it); launches runs one launch per (fused) GEMV, chained by programmatic dependent "
-                         f"launch (default: chain on one GPU, {TP_DEFAULT_SCHEDULE} tensor parallel)")
+                         "launch (default: chain on one GPU and tensor parallel over 2; launches over more)")
     ap.add_argument("--unfused", action="store_true",
                     help="stream: launch all 337 GEMVs separately, each on its own x, instead of fusing "
                          "q|k|v and gate|up (which read the same x in a decode step)")
@@ -256,7 +257,8 @@ def main():
     tp_run = (args.workload == "stream" and int(os.environ.get("WORLD_SIZE", "1")) > 1
               and args.parallel != "replicas")
     if args.schedule is None:
-        args.schedule = TP_DEFAULT_SCHEDULE if tp_run else "chain"
+        world_n = int(os.environ.get("WORLD_SIZE", "1"))
+        args.schedule = "chain" if not tp_run or world_n in TP_CHAIN_CONFIRMED_WORLDS else "launches"
     if args.allreduce is None:
         args.allreduce = TP_DEFAULT_ALLREDUCE
     if args.workload in GEMM_WORKLOADS:
