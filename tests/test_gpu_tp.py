@@ -42,3 +42,16 @@ def test_tp_decode_two_gpus(fp8, allreduce):
            os.path.join(HERE, "tp_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_tp_chain_decode_wider(world):
+    """The in-chain all-reduce over 4 and 8 ranks (skipped on smaller boxes)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    env = dict(os.environ, TP_FP8="0", TP_ALLREDUCE="chain")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           os.path.join(HERE, "tp_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

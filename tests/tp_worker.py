@@ -20,7 +20,8 @@ from g4b import comm, ops, tp  # noqa: E402
 from g4b import quant_gpu as qz  # noqa: E402
 from util import assert_close  # noqa: E402
 
-H, NQ, NKV, FFN, VOCAB, LAYERS = 1024, 1024, 512, 2048, 8192, 2
+# every column / row shard splits in 256-wide units over up to 8 ranks
+H, NQ, NKV, FFN, VOCAB, LAYERS = 1024, 2048, 2048, 4096, 8192, 2
 
 
 def main():
