@@ -224,6 +224,17 @@ def run_cpu_baseline(host_entries, fp8, seconds, oracle):
                 return done / dt / 1e9, n, done, dt
 
 
+def resolve_defaults(args, world: int) -> None:
+    """Fill the schedule and all-reduce the user left unset: the chain on one
+    GPU and for tensor parallelism over the confirmed worlds, per-GEMV launches
+    with NCCL's all-reduce over wider ones."""
+    tp_run = args.workload == "stream" and world > 1 and args.parallel != "replicas"
+    if args.schedule is None:
+        args.schedule = "chain" if not tp_run or world in TP_CHAIN_CONFIRMED_WORLDS else "launches"
+    if args.allreduce is None:
+        args.allreduce = TP_DEFAULT_ALLREDUCE
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -254,13 +265,7 @@ def main():
                     help="N > 1: tp (default) shards the stream's output columns / input rows over the GPUs "
                          "with NCCL all-reduces per layer; replicas streams a full copy per GPU")
     args = ap.parse_args()
-    tp_run = (args.workload == "stream" and int(os.environ.get("WORLD_SIZE", "1")) > 1
-              and args.parallel != "replicas")
-    if args.schedule is None:
-        world_n = int(os.environ.get("WORLD_SIZE", "1"))
-        args.schedule = "chain" if not tp_run or world_n in TP_CHAIN_CONFIRMED_WORLDS else "launches"
-    if args.allreduce is None:
-        args.allreduce = TP_DEFAULT_ALLREDUCE
+    resolve_defaults(args, int(os.environ.get("WORLD_SIZE", "1")))
     if args.workload in GEMM_WORKLOADS:
         return run_gemm(args)
     if args.workload == "prefill":
