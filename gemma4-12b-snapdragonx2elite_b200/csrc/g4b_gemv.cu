@@ -27,6 +27,7 @@
 //     them in slice order (deterministic), scales by inv and writes y -- the
 //     reduce.comp dispatch fused into the GEMV.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 #include <utility>
@@ -37,6 +38,11 @@ namespace g4b {
 
 // Launch flags of the current host call (set by g4b_gemv_i4_ex for its duration).
 static thread_local bool t_pdl = false;
+// Bytes at t_clear_ptr to zero on the launch stream right before the next
+// kernel launch of the current host call (g4b_gemv_i4_noalloc's counters):
+// enqueued only once every check has passed, so a rejected call launches nothing.
+static thread_local void* t_clear_ptr = nullptr;
+static thread_local size_t t_clear_bytes = 0;
 
 // Launch `kern` on `s`, with programmatic dependent launch when t_pdl is set:
 // the grid may then start while the previous kernel in the stream is still
@@ -45,6 +51,12 @@ static thread_local bool t_pdl = false;
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                             Args&&... args) {
+    if (t_clear_ptr) {
+        void* p = t_clear_ptr;
+        t_clear_ptr = nullptr;
+        const cudaError_t e = cudaMemsetAsync(p, 0, t_clear_bytes, s);
+        if (e != cudaSuccess) return e;
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -633,6 +645,7 @@ constexpr int kM1Stages = kM1Groups * kM1PerGroup;
 constexpr int kM1WarpsPerGroup = 8;
 constexpr int kM1Consumers = 32 * kM1WarpsPerGroup * kM1Groups;  // 512
 constexpr int kM1Threads = kM1Consumers + 64;      // + TMA producer warp + activation producer warp
+constexpr int kChainThreads = kM1Threads + 32;     // the chain adds an L2 prefetch warp
 
 // Up to three GEMVs that read the same x (the engine's q/k/v, or gate/up) run
 // as one launch: their column tiles are numbered one after another ("segments"),
@@ -1106,6 +1119,7 @@ struct ChainArgs {
     unsigned* counters;       // [2][maxtiles] split-K arrivals per tile, by step parity
     unsigned long long* const* peers;  // [world] exchange buffers (this rank's own at [rank]); null if world 1
     int nsteps, stage_bytes, s_bytes, maxtiles, G, rank, world;
+    int pf_items;             // L2 prefetch distance: items ahead of the TMA producer (0 = off)
 };
 
 // exchange-buffer words: {f32 bits (low), run epoch (high)}; a 64-bit aligned
@@ -1153,13 +1167,14 @@ __device__ __forceinline__ bool chain_wait_count(const unsigned* count, unsigned
 // written by other SMs during this launch) and arrives on the stage's full
 // barrier itself.
 template <bool XF32, int SFMT, bool YF32>
-__global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __grid_constant__ ChainArgs ch) {
+__global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const __grid_constant__ ChainArgs ch) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[2 * kM1Stages];
     __shared__ float red[2][kM1Groups][kStTN];  // double-buffered: consecutive flushes never share it
     __shared__ unsigned s_last;
     __shared__ int s_pending;                    // shared tile this CTA must still reduce (-1: none)
     __shared__ int s_issued, s_xdone;
+    __shared__ int s_prod, s_prod_done;          // items the TMA producer has issued; it has stopped
     __shared__ int s_abort;
     __shared__ __align__(16) uint32_t s_zero[32];  // B-fragment source for lanes that feed zeros
     __shared__ __align__(8) ChainStep s_step[2];   // the consumers' current and next step
@@ -1200,6 +1215,8 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
         s_abort = 0;
         s_issued = 0;
         s_xdone = 0;
+        s_prod = 0;
+        s_prod_done = 0;
         s_pending = -1;
         fence_mbar_init();
     }
@@ -1238,6 +1255,7 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
                     const uint32_t st = smem0 + (uint32_t)s * stage_bytes;
                     tma_load_2d(st, &wm[sg], lt * (kStTN / 8), o * kM1Rows, full_bar(s), pol);
                     tma_load_2d(st + kM1WBytes, &sm[sg], lt * (kStTN * ssz / 8), o * 8, full_bar(s), pol);
+                    *(volatile int*)&s_prod = i + 1;
                     if (++o == d.noct) {
                         o = 0;
                         ++t;
@@ -1245,6 +1263,48 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_chain_kernel(const __gr
                 }
             }
             s_issued = i;
+            *(volatile int*)&s_prod_done = 1;
+        }
+    } else if (warp == pw + 2) {
+        // L2 prefetch of the weight and scale tiles the TMA producer will load next.  A step
+        // boundary holds the consumers, and with them the producer once its stages are full;
+        // meanwhile HBM keeps streaming the coming items into L2, and their TMA loads then hit L2.
+        // This warp stays at most pf_items items ahead of the producer, skips items the producer
+        // has already issued, never holds anyone up, and stops with the producer.
+        if (lane == 0 && ch.pf_items > 0) {
+            int i = 0;
+            bool stop = false;
+            for (int j = 0; j < nsteps && !stop; j++) {
+                const ChainStep d = ch.steps[j];
+                const CUtensorMap* wm = ch.maps + (size_t)j * 2 * kTcMaxSeg;
+                const CUtensorMap* sm = wm + kTcMaxSeg;
+                int ibeg, iend;
+                my_range(d, ibeg, iend);
+                int t = ibeg / d.noct, o = ibeg - t * d.noct;
+                for (int it = ibeg; it < iend; ++it, ++i) {
+                    if (i >= *(volatile int*)&s_prod + ch.pf_items) {
+                        const uint64_t t0 = global_ns();
+                        while (i >= *(volatile int*)&s_prod + ch.pf_items) {
+                            if (*abort_flag || *(volatile int*)&s_prod_done || global_ns() - t0 > kWaitLimitNs) {
+                                stop = true;
+                                break;
+                            }
+                            __nanosleep(256);
+                        }
+                        if (stop) break;
+                    }
+                    if (i >= *(volatile int*)&s_prod) {
+                        const int sg = tc_seg_of(d, t);
+                        const int lt = t - tc_seg(d, sg).tile0;
+                        tma_prefetch_l2_2d(&wm[sg], lt * (kStTN / 8), o * kM1Rows);
+                        tma_prefetch_l2_2d(&sm[sg], lt * (kStTN * ssz / 8), o * 8);
+                    }
+                    if (++o == d.noct) {
+                        o = 0;
+                        ++t;
+                    }
+                }
+            }
         }
     } else if (warp == pw + 1) {
         // x slices by plain loads (L2, not L1: x was written by other SMs during this launch)
@@ -2651,9 +2711,11 @@ int g4b_gemv_i4_ex(const void* x, int x_dtype, int M, const uint32_t* wp, const 
     return st;
 }
 
-static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,
-                        float inv, void* y, int y_dtype, int N, int K, int split, void* workspace, size_t ws_bytes,
-                        g4b_stream_t stream) {
+// Every argument check of g4b_gemv_i4 that needs no workspace: pointers, enums,
+// sizes and alignment.  Shared with g4b_gemv_i4_noalloc, which runs it before it
+// queues anything.
+static int gemv_i4_check(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,
+                         void* y, int y_dtype, int N, int K, int split) {
     G4B_REQUIRE(x && wp && scales && y, G4B_E_ARG, "gemv_i4: NULL pointer argument");
     G4B_REQUIRE(x_dtype == G4B_DT_F32 || x_dtype == G4B_DT_F16, G4B_E_ARG, "gemv_i4: bad x_dtype %d", x_dtype);
     G4B_REQUIRE(y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16, G4B_E_ARG, "gemv_i4: bad y_dtype %d", y_dtype);
@@ -2668,8 +2730,17 @@ static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, c
     G4B_REQUIRE(aligned16(x) && aligned16(wp) && aligned16(scales), G4B_E_ALIGN,
                 "gemv_i4: x, wp and scales must be 16-byte aligned");
     G4B_REQUIRE(((uintptr_t)y & (y_dtype == G4B_DT_F32 ? 3u : 1u)) == 0, G4B_E_ALIGN, "gemv_i4: y misaligned");
+    return G4B_OK;
+}
+
+static int gemv_i4_impl(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,
+                        float inv, void* y, int y_dtype, int N, int K, int split, void* workspace, size_t ws_bytes,
+                        g4b_stream_t stream) {
+    int st = gemv_i4_check(x, x_dtype, M, wp, scales, scale_fmt, y, y_dtype, N, K, split);
+    if (st != G4B_OK) return st;
+    const int nblk = K / 32;
     int sms = 0;
-    int st = check_device(&sms);
+    st = check_device(&sms);
     if (st != G4B_OK) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const size_t xe = x_dtype == G4B_DT_F32 ? 4 : 2, ye = y_dtype == G4B_DT_F32 ? 4 : 2;
@@ -2805,6 +2876,7 @@ int g4b_gemv_i4_fused(const void* x, int x_dtype, int nseg, const g4b_gemv_segme
 struct g4b_gemv_chain {
     int device = -1, nsteps = 0, x_dtype = 0, scale_fmt = 0, y_dtype = 0;
     int grid = 0, stage_bytes = 0, s_bytes = 0, maxtiles = 0, rank = 0, world = 1;
+    int pf_items = 0;              // L2 prefetch distance in items (G4B_CHAIN_PREFETCH at create time)
     size_t smem = 0, counter_bytes = 0, sync_bytes = 0, ws_bytes = 0;
     void* const* peers = nullptr;  // device array of the world exchange buffers (tensor parallel)
     // device: [nsteps][6] CUtensorMap, then [nsteps] ChainStep, then the steps' range / cspan tables
@@ -2814,6 +2886,10 @@ struct g4b_gemv_chain {
 namespace g4b {
 
 constexpr int kChainMaxSteps = 1 << 16;
+// Default L2 prefetch distance of a chain: items (a 256 x 256 weight tile and its scales, 36 KB
+// with f16 scales) each CTA keeps in flight to L2 ahead of its TMA producer; 8 items over 148
+// SMs hold about 43 MB of the 126 MB L2.  G4B_CHAIN_PREFETCH=n at chain creation overrides it.
+constexpr int kChainPrefetchItems = 8;
 
 static size_t chain_maps_bytes(int nsteps) { return (size_t)nsteps * 2 * kTcMaxSeg * sizeof(CUtensorMap); }
 
@@ -2860,7 +2936,7 @@ static int chain_prepare_kernel(size_t smem, int* resident) {
     auto kern = gemv_i4_chain_kernel<XF32, SFMT, YF32>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(resident, kern, kM1Threads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(resident, kern, kChainThreads, smem);
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain: occupancy query: %s", cudaGetErrorString(e));
     return G4B_OK;
 }
@@ -2878,7 +2954,7 @@ template <bool XF32, int SFMT, bool YF32>
 static cudaError_t chain_launch_kernel(const g4b_gemv_chain* c, const ChainArgs& ch, cudaStream_t s) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(c->grid);
-    cfg.blockDim = dim3(kM1Threads);
+    cfg.blockDim = dim3(kChainThreads);
     cfg.dynamicSmemBytes = c->smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -3112,6 +3188,8 @@ int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x
     c->peers = peers_dev;
     c->rank = rank;
     c->world = world;
+    c->pf_items = kChainPrefetchItems;
+    if (const char* pf = getenv("G4B_CHAIN_PREFETCH")) c->pf_items = std::max(0, std::min(64, atoi(pf)));
     *chain = c;
     return G4B_OK;
 }
@@ -3146,6 +3224,7 @@ int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_b
     ch.G = chain->grid;
     ch.rank = chain->rank;
     ch.world = chain->world;
+    ch.pf_items = chain->pf_items;
     cudaError_t e = chain_launch(chain, ch, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain_run: launch: %s", cudaGetErrorString(e));
     count_launch();
@@ -3161,11 +3240,10 @@ void g4b_gemv_chain_destroy(g4b_gemv_chain* chain) {
 int g4b_gemv_i4_noalloc(const void* x, int x_dtype, int M, const uint32_t* wp, const void* scales, int scale_fmt,
                         float inv, void* y, int y_dtype, int N, int K, int split, g4b_stream_t stream) {
     G4B_ENTRY("gemv_i4_noalloc");
-    G4B_REQUIRE(M >= 1 && N > 0 && K > 0 && K % 32 == 0 && N % 16 == 0, G4B_E_SHAPE,
-                "gemv_i4_noalloc: M=%d N=%d K=%d (N %% 16, K %% 32 required)", M, N, K);
-    G4B_REQUIRE(split >= 0 && (split == 0 || (K / 32) % split == 0), G4B_E_SHAPE,
-                "gemv_i4_noalloc: split=%d must divide K/32=%d (or be 0)", split, K / 32);
-    int st = check_device(nullptr);
+    // every argument check first: a rejected call must not have queued the counter clear below
+    int st = gemv_i4_check(x, x_dtype, M, wp, scales, scale_fmt, y, y_dtype, N, K, split);
+    if (st != G4B_OK) return st;
+    st = check_device(nullptr);
     if (st != G4B_OK) return st;
     const size_t need = g4b_gemv_workspace_bytes(M, N, K, split);
     clear_error();
@@ -3178,12 +3256,15 @@ int g4b_gemv_i4_noalloc(const void* x, int x_dtype, int M, const uint32_t* wp, c
         st = noalloc_scratch(&ws);
         if (st != G4B_OK) return st;
         // the arrival counters at the front of the scratch must start at zero; a previous call
-        // leaves them zero, but one that gave up (kernel status) may not: clear them every call
-        cudaError_t e = cudaMemsetAsync(ws, 0, kGemvCounterBytes, reinterpret_cast<cudaStream_t>(stream));
-        if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_i4_noalloc: cudaMemsetAsync: %s", cudaGetErrorString(e));
+        // leaves them zero, but one that gave up (kernel status) may not.  The clear is queued by
+        // the kernel launch itself, after gemv_i4_impl's remaining checks have all passed.
+        t_clear_ptr = ws;
+        t_clear_bytes = kGemvCounterBytes;
     }
     t_pdl = false;
-    return gemv_i4_impl(x, x_dtype, M, wp, scales, scale_fmt, inv, y, y_dtype, N, K, split, ws, need, stream);
+    st = gemv_i4_impl(x, x_dtype, M, wp, scales, scale_fmt, inv, y, y_dtype, N, K, split, ws, need, stream);
+    t_clear_ptr = nullptr;  // unused if the call failed before its launch
+    return st;
 }
 
 int g4b_reduce_partials(const float* partial, float* y, int N, int split, g4b_stream_t stream) {

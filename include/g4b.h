@@ -144,8 +144,9 @@ G4B_API int g4b_gemv_i4_ex(const void* x, int x_dtype, int M,
  *     15360-wide GEMV) are rejected with G4B_E_WORKSPACE before anything runs.
  *   - The first call on each device looks the array's address up
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
- *   - Every call enqueues a small memset of the array's counters, then the
- *     same kernel as g4b_gemv_i4; nothing is allocated or freed.
+ *   - Every accepted call enqueues a small memset of the array's counters,
+ *     then the same kernel as g4b_gemv_i4; nothing is allocated or freed.
+ *     Arguments are checked first: a rejected call enqueues nothing.
  *   - All calls share the one array, which keeps the last call's contents:
  *     calls that can overlap on the GPU (different streams, or concurrent
  *     host threads without ordering) race on it.  Serialise them on one stream. */
