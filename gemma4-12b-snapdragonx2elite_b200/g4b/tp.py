@@ -171,16 +171,20 @@ def chain_steps(layers: List[TPLayer], lm_head, h, bufs: dict, allreduce_flag: i
     on that sum, down on this rank's gate shard, all-reduced again; lm_head
     last on the final sum.  `h` is the first layer's input (f32, hidden long);
     `bufs` holds the per-rank outputs ("q", "k", "v", "part", "gate", "up",
-    "logits_local").  The logits all-gather follows the chain."""
+    "logits_local").  The logits all-gather follows the chain.
+
+    allreduce_flag 0 (one rank, or the collectives left out): the o and down
+    outputs are not all-reduced, and the steps after them read "part" itself."""
     steps = []
     x = h
+    after = None if allreduce_flag else bufs["part"]
     for L in layers:
         steps.append((x, [L.q, L.k, L.v], [bufs["q"], bufs["k"], bufs["v"]]))
         steps.append((bufs["q"], [L.o], [bufs["part"]], allreduce_flag))
-        steps.append((None, [L.gate, L.up], [bufs["gate"], bufs["up"]]))
+        steps.append((after, [L.gate, L.up], [bufs["gate"], bufs["up"]]))
         steps.append((bufs["gate"], [L.down], [bufs["part"]], allreduce_flag))
-        x = None
-    steps.append((None, [lm_head], [bufs["logits_local"]]))
+        x = after
+    steps.append((after, [lm_head], [bufs["logits_local"]]))
     return steps
 
 
@@ -220,7 +224,14 @@ def shard_layer_shapes(shapes, world: int):
 
 
 def validate_world(hidden: int, nq: int, nkv: int, ffn: int, vocab: int, world: int) -> Optional[str]:
-    """None if the decode stack shards evenly over `world` ranks, else why not."""
+    """None if the decode stack shards over `world` ranks, else why not.
+
+    Every sharded size must split in units of 256.  The logits are gathered
+    with an equal-count all-gather, so the lm_head's column shards must also
+    be the same size on every rank (vocab a multiple of 256 * world); a world
+    that fails this is refused here, before any collective runs."""
+    if world < 1:
+        return f"tp: world size {world} must be at least 1"
     try:
         for n in (nq, nkv, ffn, vocab):
             split_range(n, world, 0, COL_ALIGN)
@@ -228,4 +239,7 @@ def validate_world(hidden: int, nq: int, nkv: int, ffn: int, vocab: int, world: 
             split_range(k, world, 0, ROW_ALIGN)
     except ValueError as e:
         return str(e)
+    if vocab % (COL_ALIGN * world):
+        return (f"tp: the logits all-gather needs equal shards, but vocab {vocab} does not split into {world} "
+                f"shards of whole {COL_ALIGN}-column units")
     return None

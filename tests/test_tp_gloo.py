@@ -142,6 +142,22 @@ def test_split_covers_and_rejects():
     assert tp.validate_world(3840, 4096, 2048, 15360, 262144, 8) is None
 
 
+@pytest.mark.parametrize("world", [3, 5, 6, 7])
+def test_world_with_unequal_logits_shards_is_refused(world):
+    """Worlds whose lm_head column shards would differ in size (262144 columns =
+    1024 units of 256 do not split evenly over 3, 5, 6 or 7 ranks) are refused
+    by validate_world, before any rank reaches the equal-count all-gather."""
+    spans = [tp.split_range(262144, world, r, tp.COL_ALIGN) for r in range(world)]
+    assert len({b - a for a, b in spans}) > 1
+    why = tp.validate_world(3840, 4096, 2048, 15360, 262144, world)
+    assert why is not None and "all-gather" in why
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_power_of_two_worlds_are_accepted(world):
+    assert tp.validate_world(3840, 4096, 2048, 15360, 262144, world) is None
+
+
 def test_chain_steps_layout():
     """tp.chain_steps: per layer q|k|v, o (all-reduced), gate|up on the sum
     (no x), down (all-reduced), then lm_head on the final sum."""

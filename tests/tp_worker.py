@@ -1,7 +1,9 @@
 """Worker for tests/test_gpu_tp.py: one rank of a tensor-parallel decode over
 NCCL (launched by torch.distributed.run).  Rank 0 also runs the same chain
-with the unsharded weights on its own GPU and compares (tests/util.py bar).
-Exit code 0 = match."""
+with the unsharded weights on its own GPU, and again on the host through the
+CPU oracle (oracle.gemv: vk/gemv.comp + vk/reduce.comp restated, on host
+copies of the unsharded packed weights), and compares the gathered logits
+with both (tests/util.py bar).  Exit code 0 = match."""
 import os
 import sys
 from datetime import timedelta
@@ -19,6 +21,17 @@ from g4b import _lib as L  # noqa: E402
 from g4b import comm, ops, tp  # noqa: E402
 from g4b import quant_gpu as qz  # noqa: E402
 from util import assert_close  # noqa: E402
+
+sys.path.insert(0, ROOT)
+import oracle as O  # noqa: E402
+
+
+def _oracle_gemv(h, w):
+    """The unsharded GEMV on the host: the oracle over w's packed words and scales."""
+    sc = w.scales.cpu().numpy()
+    sc = sc.view(np.uint16) if w.scale_fmt == L.SCALE_F16 else sc
+    return O.gemv(np.asarray(h, np.float32), w.wp.cpu().numpy().view(np.uint32), sc, w.scale_fmt, w.inv,
+                  w.N, w.K, w.split)
 
 # every column / row shard splits in 256-wide units over up to 8 ranks
 H, NQ, NKV, FFN, VOCAB, LAYERS = 1024, 2048, 2048, 4096, 8192, 2
@@ -120,8 +133,10 @@ def main():
     if rank == 0:
         ref = tp.decode_reference(full, lm_full, x, lambda h, w: ops.gemv_i4(h, w, out_dtype=torch.float32))
         torch.cuda.synchronize()
+        host = tp.decode_reference(full, lm_full, x.cpu().numpy(), _oracle_gemv)
         try:
             assert_close(logits.cpu().numpy(), ref.cpu().numpy(), f"TP world {world} vs unsharded")
+            assert_close(logits.cpu().numpy(), host, f"TP world {world} vs the CPU oracle")
             assert torch.equal(logits, replay), "graph replay differs from the eager step"
             assert L.query(L.Q_KERNEL_STATUS) == 0
         except AssertionError as e:
