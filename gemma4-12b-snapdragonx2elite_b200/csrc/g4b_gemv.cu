@@ -1114,9 +1114,8 @@ struct ChainArgs {
     const ChainStep* steps;   // [nsteps], device memory
     const CUtensorMap* maps;  // [nsteps][2 * kTcMaxSeg]: weight maps, then scale maps; device memory
     unsigned* sync;           // [nsteps] tiles written per step, then the exit count and the abort word
-    float* partial;           // [2][2 * G][kStTN]: CTA c's partials of its first and its last tile,
-                              // by step parity
-    unsigned* counters;       // [2][maxtiles] split-K arrivals per tile, by step parity
+    unsigned long long* partial;  // [2][2 * G][kStTN] {f32 bits, step tag} words: CTA c's partials of its
+                                  // first and its last tile, by step parity
     unsigned long long* const* peers;  // [world] exchange buffers (this rank's own at [rank]); null if world 1
     int nsteps, stage_bytes, s_bytes, maxtiles, G, rank, world;
     int pf_items;             // L2 prefetch distance: items ahead of the TMA producer (0 = off)
@@ -1130,6 +1129,15 @@ __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsign
 __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -1171,7 +1179,6 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[2 * kM1Stages];
     __shared__ float red[2][kM1Groups][kStTN];  // double-buffered: consecutive flushes never share it
-    __shared__ unsigned s_last;
     __shared__ int s_pending;                    // shared tile this CTA must still reduce (-1: none)
     __shared__ int s_issued, s_xdone;
     __shared__ int s_prod, s_prod_done;          // items the TMA producer has issued; it has stopped
@@ -1415,8 +1422,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
         unsigned ndone = 0;  // ctid 0: tiles of the current step whose y this CTA wrote
 
         for (int j = 0; j < nsteps; j++) {
-            // step j's partials and arrival counters are step j-2's: every tile of step j-2 (its
-            // reductions included) is written before they are reused (normally long since)
+            // step j's partial slots are step j-2's: every tile of step j-2 (its reductions
+            // included) is written before they are reused (normally long since)
             if (j >= 2 && ctid == 0)
                 chain_wait_count(&ch.sync[j - 2], (unsigned)ch.steps[j - 2].ntiles, gabort, abort_flag);
             // every consumer is done with step j-1, whose descriptor slot now takes step j+1's
@@ -1427,8 +1434,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
             const ChainStep& d = s_step[j & 1];
             int ibeg, iend;
             my_range(d, ibeg, iend);
-            float* const partial = ch.partial + (size_t)(j & 1) * 2 * ch.G * kStTN;
-            unsigned* const counters = ch.counters + (size_t)(j & 1) * ch.maxtiles;
+            unsigned long long* const partial = ch.partial + (size_t)(j & 1) * 2 * ch.G * kStTN;
+            // this step's tag in its partial words: distinct for every (run, step), so words left by the
+            // step two back (same buffer) or by an earlier run never pass for this step's
+            const unsigned tag = epoch * (unsigned)nsteps + (unsigned)j + 1u;
             // y[n] of the tile's segment, scaled by its e4m3 inverse scale; a step whose y is
             // all-reduced also pushes the value to slot [rank] of every rank's exchange region
             auto write_y = [&](int t, int col, float v) {
@@ -1448,31 +1457,60 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
             };
             float acc[2][2];
             const int t_first = ibeg / d.noct, t_last = iend > ibeg ? (iend - 1) / d.noct : t_first - 1;
-            // Sum a shared tile's partials in CTA order (deterministic) and write y.  CTA cc keeps
-            // its share of its first tile in slot 2cc and of its last in 2cc + 1; only the tile's first
-            // CTA can have started in an earlier tile (bit 31 of cspan[2t]), every later one starts in t.
+            // Sum a shared tile's partials in CTA order (deterministic) and write y.  The tile's
+            // reducer is the CTA holding its last k-chunk; each sharer stores its partial as {f32,
+            // tag} words and moves on, and the reducer polls the words until every one carries this
+            // step's tag (bounded) -- no fence, no atomic round trip.  CTA cc keeps its share of its
+            // first tile in slot 2cc and of its last in 2cc + 1; only the tile's first CTA can have
+            // started in an earlier tile (bit 31 of cspan[2t]), every later one starts in t.
             auto reduce_tile = [&](int t) {
                 const unsigned f = (unsigned)__ldg(d.cspan + 2 * t);
                 const int c_first = (int)(f & 0x7fffffffu), c_last = __ldg(d.cspan + 2 * t + 1);
                 if (ctid < kStTN) {
                     const int col = ctid;
                     float v = 0.f;
-                    for (int k0 = c_first; k0 <= c_last; k0 += 8) {
-                        float pv[8];
+                    bool ok = true;
+                    uint64_t t0 = 0;
+                    for (int k0 = c_first; k0 <= c_last && ok; k0 += 8) {
+                        unsigned long long w[8];
                         #pragma unroll
                         for (int k = 0; k < 8; k++) {
-                            pv[k] = 0.f;
                             const int cc = k0 + k;
                             const int sl = 2 * cc + (cc == c_first ? (int)(f >> 31) : 0);
-                            if (cc <= c_last) pv[k] = __ldcg(&partial[(size_t)sl * kStTN + col]);
+                            w[k] = cc <= c_last ? ld_relaxed_gpu_u64(&partial[(size_t)sl * kStTN + col])
+                                                : ((unsigned long long)tag << 32);
+                        }
+                        for (;;) {
+                            bool all = true;
+                            #pragma unroll
+                            for (int k = 0; k < 8; k++) all = all && (unsigned)(w[k] >> 32) == tag;
+                            if (all) break;
+                            if (t0 == 0) t0 = global_ns();
+                            if (*abort_flag || *(volatile unsigned*)gabort) {
+                                ok = false;
+                                break;
+                            }
+                            if (global_ns() - t0 > kWaitLimitNs) {
+                                atomicOr(&g_gemv_status, kStatusTimeout);
+                                atomicExch(gabort, 1u);
+                                *abort_flag = 1;
+                                ok = false;
+                                break;
+                            }
+                            #pragma unroll
+                            for (int k = 0; k < 8; k++) {
+                                const int cc = k0 + k;
+                                const int sl = 2 * cc + (cc == c_first ? (int)(f >> 31) : 0);
+                                if ((unsigned)(w[k] >> 32) != tag)
+                                    w[k] = ld_relaxed_gpu_u64(&partial[(size_t)sl * kStTN + col]);
+                            }
                         }
                         #pragma unroll
                         for (int k = 0; k < 8; k++)
-                            if (k0 + k <= c_last) v += pv[k];
+                            if (k0 + k <= c_last) v += __uint_as_float((unsigned)w[k]);
                     }
-                    write_y(t, col, v);
+                    if (ok) write_y(t, col, v);
                 }
-                if (ctid == 0) counters[t] = 0u;  // ready for the next step
             };
 
             for (int t = t_first; t <= t_last; ++t) {
@@ -1629,27 +1667,20 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                     #pragma unroll
                     for (int gg = 1; gg < kM1Groups; gg++) v += red[rb][gg][col];
                     if (single) write_y(t, col, v);
-                    else partial[(size_t)(2 * c + (t == t_first ? 0 : 1)) * kStTN + col] = v;
+                    else
+                        st_relaxed_gpu_u64(&partial[(size_t)(2 * c + (t == t_first ? 0 : 1)) * kStTN + col],
+                                           ((unsigned long long)tag << 32) | __float_as_uint(v));
                 }
                 if (single) {
                     if (ctid == 0 && ok) ndone++;
-                } else {
-                    // publish this CTA's partial: one thread arrives for the CTA (after the barrier) with an
-                    // acquire-release add on the tile's counter; the last of the tile's CTAs to arrive reduces it
-                    named_bar_sync(1, kM1Consumers);
-                    const unsigned sharers =
-                        (unsigned)(__ldg(d.cspan + 2 * t + 1) - (int)((unsigned)__ldg(d.cspan + 2 * t) & 0x7fffffffu));
+                } else if (__ldg(d.cspan + 2 * t + 1) == c && ok) {
+                    // this CTA holds the tile's last k-chunk: it reduces the tile, now if this is its final
+                    // tile, otherwise after its last item (the other consumers keep going meanwhile)
                     if (t < t_last) {
-                        // not our final tile: do not stall the other consumers on the atomic; if we
-                        // turn out to be the last arriver, the reduction runs after our last item
-                        if (ctid == 0 && ok && atom_add_acq_rel_gpu(&counters[t], 1u) == sharers) s_pending = t;
+                        if (ctid == 0) s_pending = t;
                     } else {
-                        if (ctid == 0) s_last = ok && atom_add_acq_rel_gpu(&counters[t], 1u) == sharers ? 1u : 0u;
-                        named_bar_sync(1, kM1Consumers);
-                        if (s_last) {
-                            reduce_tile(t);
-                            if (ctid == 0) ndone++;
-                        }
+                        reduce_tile(t);
+                        if (ctid == 0 && !*abort_flag) ndone++;
                     }
                 }
             }
@@ -1657,7 +1688,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
             named_bar_sync(1, kM1Consumers);
             if (s_pending >= 0 && !*abort_flag) {
                 reduce_tile(s_pending);
-                if (ctid == 0) ndone++;
+                if (ctid == 0 && !*abort_flag) ndone++;
             }
             // every y this CTA wrote in step j is stored: count its tiles as written
             named_bar_sync(1, kM1Consumers);
@@ -1688,12 +1719,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
         __threadfence();
         if (atomicAdd(&ch.sync[nsteps], 1u) == gridDim.x - 1u) {
             // the last CTA out: every CTA is past all its waits, so the chain's counts can be
-            // cleared for the next launch (and, after an abort, the split-K arrival counters)
+            // cleared for the next launch (partial words need no clearing: their tags name the run)
             __threadfence();
-            const bool aborted = *(volatile unsigned*)gabort != 0u;
             for (int j = 0; j < nsteps; j++) ch.sync[j] = 0u;
-            if (aborted)
-                for (int t = 0; t < 2 * ch.maxtiles; t++) ch.counters[t] = 0u;
             *gabort = 0u;
             ch.sync[nsteps + 2] = epoch;  // the next run's epoch is one more
             ch.sync[nsteps] = 0u;
@@ -2877,7 +2905,7 @@ struct g4b_gemv_chain {
     int device = -1, nsteps = 0, x_dtype = 0, scale_fmt = 0, y_dtype = 0;
     int grid = 0, stage_bytes = 0, s_bytes = 0, maxtiles = 0, rank = 0, world = 1;
     int pf_items = 0;              // L2 prefetch distance in items (G4B_CHAIN_PREFETCH at create time)
-    size_t smem = 0, counter_bytes = 0, sync_bytes = 0, ws_bytes = 0;
+    size_t smem = 0, sync_bytes = 0, ws_bytes = 0;
     void* const* peers = nullptr;  // device array of the world exchange buffers (tensor parallel)
     // device: [nsteps][6] CUtensorMap, then [nsteps] ChainStep, then the steps' range / cspan tables
     void* plan = nullptr;
@@ -3181,9 +3209,8 @@ int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x
     c->s_bytes = 8 * kStTN * ssz;
     c->maxtiles = maxtiles;
     c->smem = smem;
-    c->counter_bytes = ((size_t)2 * maxtiles * sizeof(unsigned) + 255) & ~(size_t)255;
     c->sync_bytes = ((size_t)(nsteps + 3) * sizeof(unsigned) + 255) & ~(size_t)255;
-    c->ws_bytes = c->counter_bytes + c->sync_bytes + (size_t)2 * 2 * grid * kStTN * sizeof(float);
+    c->ws_bytes = c->sync_bytes + (size_t)2 * 2 * grid * kStTN * sizeof(unsigned long long);
     c->plan = plan;
     c->peers = peers_dev;
     c->rank = rank;
@@ -3213,9 +3240,8 @@ int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_b
     ch.steps = reinterpret_cast<const ChainStep*>(reinterpret_cast<const uint8_t*>(chain->plan) +
                                                   chain_maps_bytes(chain->nsteps));
     uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-    ch.counters = reinterpret_cast<unsigned*>(ws);
-    ch.sync = reinterpret_cast<unsigned*>(ws + chain->counter_bytes);
-    ch.partial = reinterpret_cast<float*>(ws + chain->counter_bytes + chain->sync_bytes);
+    ch.sync = reinterpret_cast<unsigned*>(ws);
+    ch.partial = reinterpret_cast<unsigned long long*>(ws + chain->sync_bytes);
     ch.peers = reinterpret_cast<unsigned long long* const*>(chain->peers);
     ch.nsteps = chain->nsteps;
     ch.stage_bytes = chain->stage_bytes;
