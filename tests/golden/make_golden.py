@@ -17,10 +17,10 @@ byte-for-byte and saved to ``tests/golden/quant_golden.npz`` together with the
 seeded input weights, so the product packer and the oracle can be checked
 against the reference itself without the reference on the machine.
 
-Run from the repository root, in a container that has the reference at
-``--ref`` (default ``/root/reference``)::
+Run from the repository root, in a container that has a checkout of the
+reference project, giving its root directory::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --ref <path to the reference checkout>
 
 The outputs are small (a few hundred KB) and are committed.
 """
@@ -102,7 +102,7 @@ def edge_weights():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root directory of a checkout of the reference project")
     ap.add_argument("--out", default=os.path.join(HERE, "quant_golden.npz"))
     ap.add_argument("--skip-split-table", action="store_true")
     args = ap.parse_args()
