@@ -1147,6 +1147,51 @@ def run_stream(args) -> None:
     c.close()
 
 
+def measure_fused_token(c, layers, lm, steps, warmup, dtype_name="f16"):
+    """configs[1]'s weights as a decode token with the engine's element-wise work
+    fused in (g4b.decode.FusedDecodeToken: rmsnorm, normadd and gelu*up inside
+    the one chain launch, o reading q in place of attention), hidden state in,
+    logits out.  value = the token's weight + scale bytes / device time."""
+    torch = c.torch
+    from g4b import decode
+
+    dt = torch.float16 if dtype_name == "f16" else torch.float32
+    gen = c.gen(21)
+    H = layers[0].q.K
+    nw = lambda: (1.0 + 0.1 * torch.randn((H,), generator=gen, device=c.device))  # noqa: E731
+    norms = [decode.LayerNorms(inw=nw(), paw=nw(), pfw=nw(), ofw=nw(), scl=1.0) for _ in layers]
+    tok = decode.FusedDecodeToken(layers, norms, lm, nw(), dtype=dt)
+    tok.h0.copy_(torch.randn((H,), generator=gen, device=c.device))
+    token_bytes = sum(weight_bytes(w.N, w.K, False) for Ly in layers for w in vars(Ly).values()) + \
+        weight_bytes(lm.N, lm.K, False)
+    graph = capture(c, lambda: tok.run(c.stream), warmup)
+    ms = timed_graph(c, graph, steps) / steps
+    hbm, _, src = peaks()
+    value = token_bytes / (ms / 1e3) / 1e9
+    # e2e: the hidden state in from pinned host memory, the logits back, every token
+    h_h = tok.h0.cpu().pin_memory()
+    l_h = torch.empty(tok.logits.shape, dtype=tok.logits.dtype).pin_memory()
+    with torch.cuda.stream(c.stream):
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            tok.h0.copy_(h_h, non_blocking=True)
+            tok.run(c.stream)
+            l_h.copy_(tok.logits, non_blocking=True)
+            c.stream.synchronize()
+        e2e_s = time.perf_counter() - t0
+    finite = bool(torch.isfinite(tok.logits).all().item())
+    del graph
+    tok.close()
+    return {"value": round(value, 1), "unit": "GB/s", "ms_per_step": round(ms, 4), "steps_per_token": tok.nsteps,
+            "activations": dtype_name, "logits_finite": finite,
+            "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(value / hbm, 4), "traffic": None, "peak_source": src,
+                         "kernel": "gemv_i4_chain_kernel (fused rmsnorm / normadd / gelu*up)"},
+            "e2e": {"value": round(token_bytes * steps / e2e_s / 1e9, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": H * 4, "d2h_bytes_per_step": tok.logits.numel() * tok.logits.element_size()},
+            "gpu_launches": steps}
+
+
 def one_gpu_extras(c, args, model):
     """The other BASELINE.json configs on this GPU, each with its own value and roofline."""
     ex = {}
@@ -1156,6 +1201,8 @@ def one_gpu_extras(c, args, model):
     layers = [c.tp.TPLayer(**{n: ws[7 * li + i] for i, (n, _, _) in enumerate(LAYER_SHAPES)})
               for li in range(args.layers)]
     full = sum(weight_bytes(w.N, w.K, False) for w in ws)
+    ex["configs[1] as decode tokens, element-wise work fused"] = measure_fused_token(c, layers, ws[-1], args.steps,
+                                                                                      args.warmup)
     ex.update(tp_extras(c, layers, ws[-1], full, args))
     ex["configs[4] prefill M=8192"] = prefill_extra(c, args, [ws[7 * li:7 * li + 7] for li in range(args.layers)])
     # configs[1] again with e4m3 scales (GEMV_FP8)

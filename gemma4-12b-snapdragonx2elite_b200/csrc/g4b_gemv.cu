@@ -1106,7 +1106,26 @@ struct ChainStep {
     // tensor parallel: yreg >= 0: every written y value of segment 0 is also pushed, tagged with the
     // run's epoch, into slot [rank] of region yreg of every rank's exchange buffer; xreg >= 0: x is
     // the rank-order sum of the world slots of region xreg (the all-reduce of the previous step's y)
-    int xreg, yreg, pad_;
+    int xreg, yreg;
+    // completion count of the step: its tiles, plus the slices of h_out its loads write (NORMADD)
+    int done;
+    // fused element-wise work on x (g4b_chain_xform; one rank only): kind, an RMSNORM over a vector
+    // no step of the chain wrote (the activation warp sums its squares itself), and the number of
+    // column tiles of the producer step (the one before) whose sums it reads
+    int xf_kind, xf_self, xf_ptiles;
+    float xf_scale, xf_eps;
+    const void* xf_a;
+    const void* xf_b;
+    const float* xf_w;
+    const float* xf_wpost;
+    float* xf_hout;
+    const float* xf_sums;      // the producer's tile sums [xf_ptiles][4]
+    // producer side: each segment-0 tile written also stores {sum h^2, sum h*(y*w), sum (y*w)^2,
+    // sum y^2} over its columns (h = sum_res, w = sum_wpost; both null: only sum y^2) for the next
+    // step's norm
+    float* sums_out;
+    const float* sum_res;
+    const float* sum_wpost;
 };
 static_assert(sizeof(ChainStep) % 8 == 0, "ChainStep is copied as 32-bit words");
 
@@ -1120,6 +1139,42 @@ struct ChainArgs {
     int nsteps, stage_bytes, s_bytes, maxtiles, G, rank, world;
     int pf_items;             // L2 prefetch distance: items ahead of the TMA producer (0 = off)
 };
+
+// element-wise work fused into a chain step's activation load (G4B_XF_*)
+constexpr int kXfNone = 0, kXfRmsNorm = 1, kXfNormAdd = 2, kXfGeluMul = 3;
+
+// elements [r0, r0 + 8) of an f32 (F32) or f16 vector as f32, through L2 (the vector may have
+// been written by other SMs during the launch)
+template <bool F32>
+__device__ __forceinline__ void load8(const void* p, int r0, float (&v)[8]) {
+    if constexpr (F32) {
+        const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + r0);
+        const float4 a = __ldcg(q), b = __ldcg(q + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p) + r0));
+        v[0] = h_lo(u.x); v[1] = h_hi(u.x); v[2] = h_lo(u.y); v[3] = h_hi(u.y);
+        v[4] = h_lo(u.z); v[5] = h_hi(u.z); v[6] = h_lo(u.w); v[7] = h_hi(u.w);
+    }
+}
+
+// a lane's 8 activations into a stage's x slice (rows 8*lane .. +8), in the chain's x dtype
+template <bool F32>
+__device__ __forceinline__ void store8(uint8_t* dst, int lane, const float (&v)[8]) {
+    if constexpr (F32) {
+        float4* d4 = reinterpret_cast<float4*>(dst + 32 * lane);
+        d4[0] = make_float4(v[0], v[1], v[2], v[3]);
+        d4[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint4 h;
+        h.x = pack_half2(__float2half_rn(v[0]), __float2half_rn(v[1]));
+        h.y = pack_half2(__float2half_rn(v[2]), __float2half_rn(v[3]));
+        h.z = pack_half2(__float2half_rn(v[4]), __float2half_rn(v[5]));
+        h.w = pack_half2(__float2half_rn(v[6]), __float2half_rn(v[7]));
+        *reinterpret_cast<uint4*>(dst + 16 * lane) = h;
+    }
+}
 
 // exchange-buffer words: {f32 bits (low), run epoch (high)}; a 64-bit aligned
 // access is single-copy atomic, so a word that carries the epoch carries its value
@@ -1186,6 +1241,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
     __shared__ __align__(16) uint32_t s_zero[32];  // B-fragment source for lanes that feed zeros
     __shared__ __align__(8) ChainStep s_step[2];   // the consumers' current and next step
     __shared__ unsigned long long* s_peers[8];
+    __shared__ float4 s_tsum[2][kM1WarpsPerGroup];  // per-warp tile sums (double-buffered)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x;
     volatile int* abort_flag = &s_abort;
@@ -1325,9 +1381,50 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
             my_range(*dj, ibeg, iend);
             // an all-reduce input carries its own readiness (the epoch in every word): no step wait
             if (iend > ibeg && j > 0 && xreg < 0) {
-                const bool ok = chain_wait_count(&ch.sync[j - 1], (unsigned)ch.steps[j - 1].ntiles, gabort, abort_flag);
+                const bool ok = chain_wait_count(&ch.sync[j - 1], (unsigned)ch.steps[j - 1].done, gabort, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) break;
             }
+            const int xk = dj->xf_kind;
+            // the step's norm scales, once per step: from the producer's tile sums (summed in a fixed
+            // lane order) or, for a vector the chain did not write, from the vector itself
+            float inv_r = 0.f, inv_h = 0.f;
+            if (xk != kXfNone && xk != kXfGeluMul && iend > ibeg) {
+                float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (dj->xf_self) {
+                    for (int r0 = 8 * lane; r0 < K; r0 += 256) {
+                        float a8[8];
+                        load8<true>(dj->xf_a, r0, a8);
+                        #pragma unroll
+                        for (int e = 0; e < 8; e++) S.w = fmaf(a8[e], a8[e], S.w);
+                    }
+                } else {
+                    for (int t = lane; t < dj->xf_ptiles; t += 32) {
+                        const float4 v = __ldcg(reinterpret_cast<const float4*>(dj->xf_sums) + t);
+                        S.x += v.x;
+                        S.y += v.y;
+                        S.z += v.z;
+                        S.w += v.w;
+                    }
+                }
+                #pragma unroll
+                for (int m = 16; m >= 1; m >>= 1) {
+                    S.x += __shfl_xor_sync(0xffffffffu, S.x, m);
+                    S.y += __shfl_xor_sync(0xffffffffu, S.y, m);
+                    S.z += __shfl_xor_sync(0xffffffffu, S.z, m);
+                    S.w += __shfl_xor_sync(0xffffffffu, S.w, m);
+                }
+                const float invK = 1.0f / (float)K;
+                if (xk == kXfRmsNorm) {
+                    inv_h = rsqrtf(S.w * invK + dj->xf_eps);
+                } else {
+                    // h' = (h + r * inv_r * w_post) * scale, so sum h'^2 = scale^2 (sum h^2
+                    // + 2 inv_r sum h (r w_post) + inv_r^2 sum (r w_post)^2)
+                    inv_r = rsqrtf(S.w * invK + dj->xf_eps);
+                    const float sh = dj->xf_scale * dj->xf_scale * fmaf(inv_r * inv_r, S.z, fmaf(2.0f * inv_r, S.y, S.x));
+                    inv_h = rsqrtf(fmaxf(sh, 0.f) * invK + dj->xf_eps);
+                }
+            }
+            int nh = 0;  // slices of h_out this warp wrote in this step
             int o = ibeg % noct;
             for (int it = ibeg; it < iend; ++it, ++i) {
                 const int s = m1_stage(i);
@@ -1340,7 +1437,51 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                     }
                 }
                 uint8_t* dst = smem + (size_t)s * stage_bytes + kM1WBytes + s_bytes;
-                if (xreg < 0) {
+                if (xk != kXfNone) {
+                    // rows o*256 + 8*lane .. +8 through the step's element-wise work, in f32
+                    const int r0 = o * kM1Rows + 8 * lane;
+                    float v[8];
+                    if (xk == kXfGeluMul) {
+                        // vk/gelumul.comp: gelu_tanh(gate) * up
+                        float g8[8], u8[8];
+                        load8<YF32>(dj->xf_a, r0, g8);
+                        load8<YF32>(dj->xf_b, r0, u8);
+                        #pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            const float xg = g8[e];
+                            const float gl = 0.5f * xg * (1.0f + tanhf(0.7978845608028654f * (xg + 0.044715f * xg * xg * xg)));
+                            v[e] = gl * u8[e];
+                        }
+                    } else if (xk == kXfRmsNorm) {
+                        // vk/rmsnorm.comp: x * inv * w
+                        float a8[8], w8[8];
+                        if (dj->xf_self) load8<true>(dj->xf_a, r0, a8);
+                        else load8<YF32>(dj->xf_a, r0, a8);
+                        load8<true>(dj->xf_w, r0, w8);
+                        #pragma unroll
+                        for (int e = 0; e < 8; e++) v[e] = a8[e] * inv_h * w8[e];
+                    } else {
+                        // vk/normadd.comp then vk/rmsnorm.comp: h' = (h + r * inv_r * w_post) * scale,
+                        // x = h' * inv_h * w; the CTA holding tile 0's item of this slice stores h'
+                        float r8[8], h8[8], p8[8], w8[8];
+                        load8<YF32>(dj->xf_a, r0, r8);
+                        load8<true>(dj->xf_b, r0, h8);
+                        load8<true>(dj->xf_wpost, r0, p8);
+                        load8<true>(dj->xf_w, r0, w8);
+                        #pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            h8[e] = (h8[e] + r8[e] * inv_r * p8[e]) * dj->xf_scale;
+                            v[e] = h8[e] * inv_h * w8[e];
+                        }
+                        if (it < noct) {
+                            float4* ho = reinterpret_cast<float4*>(dj->xf_hout + r0);
+                            ho[0] = make_float4(h8[0], h8[1], h8[2], h8[3]);
+                            ho[1] = make_float4(h8[4], h8[5], h8[6], h8[7]);
+                            nh++;
+                        }
+                    }
+                    store8<XF32>(dst, lane, v);
+                } else if (xreg < 0) {
                     const uint8_t* src = x + (size_t)o * kM1Rows * esz;
                     #pragma unroll
                     for (int b = lane * 16; b < kM1Rows * esz; b += 512)
@@ -1388,22 +1529,18 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         stop = true;
                         break;
                     }
-                    if constexpr (XF32) {
-                        float4* d4 = reinterpret_cast<float4*>(dst + 32 * lane);
-                        d4[0] = make_float4(v[0], v[1], v[2], v[3]);
-                        d4[1] = make_float4(v[4], v[5], v[6], v[7]);
-                    } else {
-                        uint4 h;
-                        h.x = pack_half2(__float2half_rn(v[0]), __float2half_rn(v[1]));
-                        h.y = pack_half2(__float2half_rn(v[2]), __float2half_rn(v[3]));
-                        h.z = pack_half2(__float2half_rn(v[4]), __float2half_rn(v[5]));
-                        h.w = pack_half2(__float2half_rn(v[6]), __float2half_rn(v[7]));
-                        *reinterpret_cast<uint4*>(dst + 16 * lane) = h;
-                    }
+                    store8<XF32>(dst, lane, v);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(full_bar(s));
                 if (++o == noct) o = 0;
+            }
+            // the h' slices this warp stored count toward the step's completion: whoever waits for
+            // the step (or any later one) then sees them
+            if (__any_sync(0xffffffffu, nh > 0)) {
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) red_add_release_gpu(&ch.sync[j], (unsigned)nh);
             }
         }
         if (lane == 0) s_xdone = i;
@@ -1418,6 +1555,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
         constexpr int NSTEP = XF32 ? 8 : 16;  // mma steps per pass
         constexpr int RMUL = XF32 ? 4 : 2;    // rows advanced per step
         int nflush = 0;
+        int nsums = 0;       // tile-sum emissions so far (picks the s_tsum buffer)
         int ibase = 0;       // this CTA's items in earlier steps
         unsigned ndone = 0;  // ctid 0: tiles of the current step whose y this CTA wrote
 
@@ -1425,7 +1563,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
             // step j's partial slots are step j-2's: every tile of step j-2 (its reductions
             // included) is written before they are reused (normally long since)
             if (j >= 2 && ctid == 0)
-                chain_wait_count(&ch.sync[j - 2], (unsigned)ch.steps[j - 2].ntiles, gabort, abort_flag);
+                chain_wait_count(&ch.sync[j - 2], (unsigned)ch.steps[j - 2].done, gabort, abort_flag);
             // every consumer is done with step j-1, whose descriptor slot now takes step j+1's
             named_bar_sync(1, kM1Consumers);
             if (j + 1 < nsteps && ctid < kStepWords)
@@ -1455,6 +1593,50 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                     }
                 }
             };
+            // the tile sums a segment-0 tile of this step hands to the next step's norm: every thread
+            // ctid < kStTN calls this for the tile (valid = it holds a finished value v), whatever
+            // the abort state, so the named barrier below is always complete
+            auto emit_sums = [&](int t, float v, bool valid) {
+                const int n = t * kStTN + ctid;
+                float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (valid && n < d.seg0.N) {
+                    const float inv = SFMT == G4B_SCALE_E4M3 ? d.seg0.inv : 1.0f;
+                    float yv = v * inv;
+                    if (!YF32) yv = __half2float(__float2half_rn(yv));  // the value the next step reads
+                    S.w = yv * yv;
+                    if (d.sum_res) {
+                        const float hr = __ldcg(d.sum_res + n), yw = yv * __ldg(d.sum_wpost + n);
+                        S.x = hr * hr;
+                        S.y = hr * yw;
+                        S.z = yw * yw;
+                    }
+                }
+                #pragma unroll
+                for (int m = 16; m >= 1; m >>= 1) {
+                    S.x += __shfl_xor_sync(0xffffffffu, S.x, m);
+                    S.y += __shfl_xor_sync(0xffffffffu, S.y, m);
+                    S.z += __shfl_xor_sync(0xffffffffu, S.z, m);
+                    S.w += __shfl_xor_sync(0xffffffffu, S.w, m);
+                }
+                const int sb = nsums & 1;
+                if (lane == 0) s_tsum[sb][warp] = S;
+                named_bar_sync(2, kStTN);
+                if (ctid == 0) {
+                    float4 T = s_tsum[sb][0];
+                    #pragma unroll
+                    for (int w = 1; w < kStTN / 32; w++) {
+                        const float4 u = s_tsum[sb][w];
+                        T.x += u.x;
+                        T.y += u.y;
+                        T.z += u.z;
+                        T.w += u.w;
+                    }
+                    reinterpret_cast<float4*>(d.sums_out)[t] = T;
+                }
+                nsums++;
+            };
+            const bool emits = d.sums_out != nullptr;
+            const int seg0_tiles = d.nseg > 1 ? d.seg1.tile0 : d.ntiles;
             float acc[2][2];
             const int t_first = ibeg / d.noct, t_last = iend > ibeg ? (iend - 1) / d.noct : t_first - 1;
             // Sum a shared tile's partials in CTA order (deterministic) and write y.  The tile's
@@ -1510,6 +1692,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                             if (k0 + k <= c_last) v += __uint_as_float((unsigned)w[k]);
                     }
                     if (ok) write_y(t, col, v);
+                    if (emits && t < seg0_tiles) emit_sums(t, v, ok);
                 }
             };
 
@@ -1661,21 +1844,25 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                 // the tile is this CTA's alone when the CTA owns all its k-chunks
                 const bool single = ibeg <= t * d.noct && iend >= (t + 1) * d.noct;
                 const bool ok = !*abort_flag;
-                if (ctid < kStTN && ok) {
+                if (ctid < kStTN) {
                     const int col = ctid;
                     float v = red[rb][0][col];
                     #pragma unroll
                     for (int gg = 1; gg < kM1Groups; gg++) v += red[rb][gg][col];
-                    if (single) write_y(t, col, v);
-                    else
-                        st_relaxed_gpu_u64(&partial[(size_t)(2 * c + (t == t_first ? 0 : 1)) * kStTN + col],
-                                           ((unsigned long long)tag << 32) | __float_as_uint(v));
+                    if (ok) {
+                        if (single) write_y(t, col, v);
+                        else
+                            st_relaxed_gpu_u64(&partial[(size_t)(2 * c + (t == t_first ? 0 : 1)) * kStTN + col],
+                                               ((unsigned long long)tag << 32) | __float_as_uint(v));
+                    }
+                    if (single && emits && t < seg0_tiles) emit_sums(t, v, ok);
                 }
                 if (single) {
                     if (ctid == 0 && ok) ndone++;
-                } else if (__ldg(d.cspan + 2 * t + 1) == c && ok) {
+                } else if (__ldg(d.cspan + 2 * t + 1) == c) {
                     // this CTA holds the tile's last k-chunk: it reduces the tile, now if this is its final
-                    // tile, otherwise after its last item (the other consumers keep going meanwhile)
+                    // tile, otherwise after its last item (the other consumers keep going meanwhile); after
+                    // an abort the reduction gives up at once, but every thread still takes this path
                     if (t < t_last) {
                         if (ctid == 0) s_pending = t;
                     } else {
@@ -1686,7 +1873,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
             }
             // the deferred reduction of an earlier tile this CTA was the last to finish
             named_bar_sync(1, kM1Consumers);
-            if (s_pending >= 0 && !*abort_flag) {
+            if (s_pending >= 0) {
                 reduce_tile(s_pending);
                 if (ctid == 0 && !*abort_flag) ndone++;
             }
@@ -3030,10 +3217,64 @@ int g4b_gemv_chain_create(const g4b_gemv_chain_step* steps, int nsteps, int x_dt
     return g4b_gemv_chain_create_tp(steps, nsteps, x_dtype, scale_fmt, y_dtype, nullptr, 0, 1, 0, chain);
 }
 
+static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xf, int nsteps, int x_dtype,
+                             int scale_fmt, int y_dtype, void* const* peers_dev, int rank, int world,
+                             size_t exchange_bytes, g4b_gemv_chain** chain);
+
 int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x_dtype, int scale_fmt, int y_dtype,
                              void* const* peers_dev, int rank, int world, size_t exchange_bytes,
                              g4b_gemv_chain** chain) {
     G4B_ENTRY("gemv_chain_create");
+    return chain_create_impl(steps, nullptr, nsteps, x_dtype, scale_fmt, y_dtype, peers_dev, rank, world,
+                             exchange_bytes, chain);
+}
+
+int g4b_gemv_chain_create_fused(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xforms, int nsteps,
+                                int x_dtype, int scale_fmt, int y_dtype, g4b_gemv_chain** chain) {
+    G4B_ENTRY("gemv_chain_create_fused");
+    G4B_REQUIRE(xforms, G4B_E_ARG, "gemv_chain_create_fused: NULL xforms");
+    return chain_create_impl(steps, xforms, nsteps, x_dtype, scale_fmt, y_dtype, nullptr, 0, 1, 0, chain);
+}
+
+// Check step j's element-wise work (g4b_chain_xform) against the steps.
+static int chain_check_xform(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xf, int j) {
+    const g4b_chain_xform& f = xf[j];
+    const int K = steps[j].K;
+    G4B_REQUIRE(f.kind >= G4B_XF_NONE && f.kind <= G4B_XF_GELU_MUL, G4B_E_ARG,
+                "gemv_chain_create_fused: step %d has unknown xform kind %d", j, f.kind);
+    if (f.kind == G4B_XF_NONE) return G4B_OK;
+    G4B_REQUIRE(!(steps[j].flags & G4B_CHAIN_ALLREDUCE) && (j == 0 || !(steps[j - 1].flags & G4B_CHAIN_ALLREDUCE)),
+                G4B_E_ARG, "gemv_chain_create_fused: step %d: element-wise work next to an all-reduced step", j);
+    G4B_REQUIRE(f.a && aligned16(f.a), G4B_E_ARG, "gemv_chain_create_fused: step %d xform needs a 16-byte aligned a",
+                j);
+    const bool produced = j > 0 && f.a == steps[j - 1].seg[0].y;
+    G4B_REQUIRE(!produced || steps[j - 1].seg[0].N == K, G4B_E_SHAPE,
+                "gemv_chain_create_fused: step %d reads step %d's output of %d values as its %d inputs", j, j - 1,
+                steps[j - 1].seg[0].N, K);
+    if (f.kind == G4B_XF_GELU_MUL) {
+        G4B_REQUIRE(j > 0 && f.b && aligned16(f.b), G4B_E_ARG,
+                    "gemv_chain_create_fused: step %d GELU_MUL needs 16-byte aligned a and b written by earlier steps",
+                    j);
+        return G4B_OK;
+    }
+    G4B_REQUIRE(f.w && aligned16(f.w), G4B_E_ARG, "gemv_chain_create_fused: step %d needs a 16-byte aligned w", j);
+    G4B_REQUIRE(f.eps >= 0.f, G4B_E_ARG, "gemv_chain_create_fused: step %d eps must be >= 0", j);
+    if (f.kind == G4B_XF_NORMADD) {
+        G4B_REQUIRE(produced, G4B_E_ARG,
+                    "gemv_chain_create_fused: step %d NORMADD: a must be step %d's first output", j, j - 1);
+        G4B_REQUIRE(f.b && f.w_post && f.h_out && aligned16(f.b) && aligned16(f.w_post) && aligned16(f.h_out),
+                    G4B_E_ARG, "gemv_chain_create_fused: step %d NORMADD needs 16-byte aligned b, w_post and h_out", j);
+        const char* hb = reinterpret_cast<const char*>(f.h_out);
+        const char* bb = reinterpret_cast<const char*>(f.b);
+        G4B_REQUIRE(hb + (size_t)K * 4 <= bb || bb + (size_t)K * 4 <= hb, G4B_E_ARG,
+                    "gemv_chain_create_fused: step %d NORMADD h_out overlaps b", j);
+    }
+    return G4B_OK;
+}
+
+static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xf, int nsteps, int x_dtype,
+                             int scale_fmt, int y_dtype, void* const* peers_dev, int rank, int world,
+                             size_t exchange_bytes, g4b_gemv_chain** chain) {
     G4B_REQUIRE(steps && chain, G4B_E_ARG, "gemv_chain_create: NULL pointer argument");
     *chain = nullptr;
     G4B_REQUIRE(world >= 1 && world <= 8 && rank >= 0 && rank < world, G4B_E_ARG,
@@ -3059,9 +3300,14 @@ int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x
         G4B_REQUIRE((st.flags & ~(unsigned)G4B_CHAIN_ALLREDUCE) == 0, G4B_E_ARG,
                     "gemv_chain_create: step %d has unknown flags 0x%x", j, st.flags);
         const bool x_from_peers = j > 0 && (steps[j - 1].flags & G4B_CHAIN_ALLREDUCE);
-        G4B_REQUIRE(st.x || x_from_peers, G4B_E_ARG, "gemv_chain_create: step %d has a NULL x", j);
-        G4B_REQUIRE(x_from_peers || aligned16(st.x), G4B_E_ALIGN,
+        const bool x_fused = xf && xf[j].kind != G4B_XF_NONE;
+        G4B_REQUIRE(st.x || x_from_peers || x_fused, G4B_E_ARG, "gemv_chain_create: step %d has a NULL x", j);
+        G4B_REQUIRE(x_from_peers || x_fused || aligned16(st.x), G4B_E_ALIGN,
                     "gemv_chain_create: step %d x must be 16-byte aligned", j);
+        if (xf) {
+            const int xs = chain_check_xform(steps, xf, j);
+            if (xs != G4B_OK) return xs;
+        }
         G4B_REQUIRE(st.nseg >= 1 && st.nseg <= kTcMaxSeg, G4B_E_ARG, "gemv_chain_create: step %d nseg=%d (1..%d)", j,
                     st.nseg, kTcMaxSeg);
         G4B_REQUIRE(st.K > 0 && st.K % 256 == 0, G4B_E_SHAPE, "gemv_chain_create: step %d K=%d must be a multiple of 256",
@@ -3099,6 +3345,8 @@ int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x
     std::vector<CUtensorMap> hmaps((size_t)nsteps * 2 * kTcMaxSeg);
     std::vector<int> tables;           // every step's range[G + 1] and cspan[ntiles][2]
     std::vector<size_t> range_at(nsteps), cspan_at(nsteps);
+    std::vector<size_t> sums_at(nsteps, (size_t)-1);  // float offset of a producer step's tile sums
+    size_t sums_words = 0;
     int grid = 1, maxtiles = 0;
     long long region = 0;  // next free exchange word
     for (int j = 0; j < nsteps; j++) {
@@ -3137,6 +3385,32 @@ int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x
         d.K = cs.K;
         d.noct = cs.K / 256;
         d.ntiles = tile0;
+        d.done = tile0;
+        if (xf && xf[j].kind != G4B_XF_NONE) {
+            const g4b_chain_xform& f = xf[j];
+            d.xf_kind = f.kind;
+            d.xf_a = f.a;
+            d.xf_b = f.b;
+            d.xf_w = f.w;
+            d.xf_wpost = f.w_post;
+            d.xf_hout = f.h_out;
+            d.xf_scale = f.kind == G4B_XF_NORMADD ? f.scale : 1.0f;
+            d.xf_eps = f.eps;
+            const bool produced = j > 0 && f.a == steps[j - 1].seg[0].y;
+            d.xf_self = f.kind == G4B_XF_RMSNORM && !produced;
+            if (f.kind != G4B_XF_GELU_MUL && produced) {
+                // the step before hands its first output's tile sums to this step's norm
+                ChainStep& pd = hsteps[j - 1];
+                d.xf_ptiles = (steps[j - 1].seg[0].N + kStTN - 1) / kStTN;
+                sums_at[j - 1] = sums_words;
+                sums_words += (size_t)4 * d.xf_ptiles;
+                if (f.kind == G4B_XF_NORMADD) {
+                    pd.sum_res = reinterpret_cast<const float*>(f.b);
+                    pd.sum_wpost = f.w_post;
+                }
+            }
+            if (f.kind == G4B_XF_NORMADD) d.done = tile0 + d.noct;  // + the h_out slices its loads write
+        }
         const std::vector<int> range = chain_partition(d.ntiles, d.noct, sms);
         d.G = (int)range.size() - 1;
         range_at[j] = tables.size();
@@ -3180,16 +3454,24 @@ int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x
 
     const size_t maps_bytes = chain_maps_bytes(nsteps);
     const size_t steps_bytes = (size_t)nsteps * sizeof(ChainStep);
-    const size_t plan_bytes = maps_bytes + steps_bytes + tables.size() * sizeof(int);
+    const size_t tables_bytes = (tables.size() * sizeof(int) + 15) & ~(size_t)15;
+    // the tile sums (written by every run) follow the read-only plan in the same allocation
+    const size_t plan_bytes = maps_bytes + steps_bytes + tables_bytes + sums_words * sizeof(float);
     void* plan = nullptr;
     cudaError_t e = cudaMalloc(&plan, plan_bytes);
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain_create: cudaMalloc: %s", cudaGetErrorString(e));
     const int* tables_dev = reinterpret_cast<const int*>(reinterpret_cast<uint8_t*>(plan) + maps_bytes + steps_bytes);
+    float* sums_dev = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(plan) + maps_bytes + steps_bytes +
+                                               tables_bytes);
     for (int j = 0; j < nsteps; j++) {
         hsteps[j].range = tables_dev + range_at[j];
         hsteps[j].cspan = tables_dev + cspan_at[j];
+        if (sums_at[j] != (size_t)-1) {
+            hsteps[j].sums_out = sums_dev + sums_at[j];
+            hsteps[j + 1].xf_sums = sums_dev + sums_at[j];
+        }
     }
-    std::vector<uint8_t> host(plan_bytes);
+    std::vector<uint8_t> host(plan_bytes, 0);
     memcpy(host.data(), hmaps.data(), maps_bytes);
     memcpy(host.data() + maps_bytes, hsteps.data(), steps_bytes);
     memcpy(host.data() + maps_bytes + steps_bytes, tables.data(), tables.size() * sizeof(int));

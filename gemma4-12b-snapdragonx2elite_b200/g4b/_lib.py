@@ -80,6 +80,7 @@ SIGNATURES = {
     "g4b_gemv_chain_create": (_I, [_P, _I, _I, _I, _I, C.POINTER(_P)]),
     "g4b_gemv_chain_exchange_bytes": (_Z, [_P, _I, _I]),
     "g4b_gemv_chain_create_tp": (_I, [_P, _I, _I, _I, _I, _P, _I, _I, _Z, C.POINTER(_P)]),
+    "g4b_gemv_chain_create_fused": (_I, [_P, _P, _I, _I, _I, _I, C.POINTER(_P)]),
     "g4b_gemv_chain_workspace_bytes": (_Z, [_P]),
     "g4b_gemv_chain_run": (_I, [_P, _P, _Z, _P]),
     "g4b_gemv_chain_destroy": (None, [_P]),
@@ -95,6 +96,18 @@ class GemvChainStep(C.Structure):
     """struct g4b_gemv_chain_step (include/g4b.h)."""
     _fields_ = [("x", C.c_void_p), ("K", C.c_int), ("nseg", C.c_int), ("seg", GemvSegment * 3),
                 ("flags", C.c_uint)]
+
+
+XF_NONE = 0
+XF_RMSNORM = 1
+XF_NORMADD = 2
+XF_GELU_MUL = 3
+
+
+class ChainXform(C.Structure):
+    """struct g4b_chain_xform (include/g4b.h)."""
+    _fields_ = [("kind", C.c_int), ("a", C.c_void_p), ("b", C.c_void_p), ("w", C.c_void_p), ("w_post", C.c_void_p),
+                ("h_out", C.c_void_p), ("scale", C.c_float), ("eps", C.c_float)]
 
 
 class G4BError(RuntimeError):

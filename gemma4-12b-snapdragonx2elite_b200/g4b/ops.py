@@ -179,20 +179,35 @@ class GemvChain:
     L.CHAIN_ALLREDUCE (one weight) has its output summed over the ranks inside
     the launch, and the next step (x = None) reads that sum as its x.
     The tensors named in the steps must stay alive while the chain is used;
-    `run` reads their current contents on every call."""
+    `run` reads their current contents on every call.
+
+    `xforms` (one rank only): one entry per step, None or a dict with "kind"
+    ("rmsnorm", "normadd" or "gelu_mul") and the tensors "a", "b", "w",
+    "w_post", "h_out" and floats "scale", "eps" that kind uses
+    (g4b_chain_xform): the element-wise work between the GEMVs, fused into the
+    step's activation load; such a step's x may be None."""
 
     @staticmethod
     def exchange_bytes(steps: list, world: int) -> int:
         return sum(8 * world * st[1][0].N for st in steps if len(st) > 3 and st[3] & L.CHAIN_ALLREDUCE)
 
-    def __init__(self, steps: list, device: Optional[torch.device] = None, exchange=None):
+    _XF_KINDS = {"rmsnorm": L.XF_RMSNORM, "normadd": L.XF_NORMADD, "gelu_mul": L.XF_GELU_MUL}
+
+    def __init__(self, steps: list, device: Optional[torch.device] = None, exchange=None,
+                 xforms: Optional[list] = None, x_dtype: Optional[torch.dtype] = None):
         if not steps:
             raise ValueError("GemvChain: no steps")
+        if xforms is not None and (len(xforms) != len(steps) or exchange is not None):
+            raise ValueError("GemvChain: one xform (or None) per step, and none with an exchange")
         self.lib = L.load()
         x0, w0, o0 = steps[0][:3]
-        if x0 is None:
+        fused = [xforms is not None and xforms[j] is not None for j in range(len(steps))]
+        if x0 is None and not fused[0]:
             raise ValueError("GemvChain: the first step needs its x")
-        self.device = x0.device if device is None else device
+        xdt = x_dtype if x_dtype is not None else (x0.dtype if x0 is not None else None)
+        if xdt is None:
+            raise ValueError("GemvChain: give x_dtype when the first step's x is fused")
+        self.device = (x0.device if x0 is not None else o0[0].device) if device is None else device
         self._keep = []
         arr = (L.GemvChainStep * len(steps))()
         fmt = w0[0].scale_fmt
@@ -203,12 +218,12 @@ class GemvChain:
             if not 1 <= len(ws_) <= 3 or len(outs) != len(ws_):
                 raise ValueError(f"GemvChain: step {j} needs 1 to 3 weights and one output per weight")
             if x is None:
-                if not prev_flags & L.CHAIN_ALLREDUCE:
+                if not (prev_flags & L.CHAIN_ALLREDUCE or fused[j]):
                     raise ValueError(f"GemvChain: step {j} has no x and does not follow an all-reduced step")
                 K = ws_[0].K
             else:
                 _need(x, "x")
-                if x.dtype != x0.dtype:
+                if x.dtype != xdt:
                     raise ValueError("GemvChain: all steps share the x dtype")
                 K = x.numel()
             if any(o.dtype != o0[0].dtype for o in outs):
@@ -226,14 +241,31 @@ class GemvChain:
             self._keep.append((x, ws_, outs))
             prev_flags = flags
         h = ctypes.c_void_p()
-        if exchange is None:
+        if xforms is not None:
+            xa = (L.ChainXform * len(steps))()
+            for j, f in enumerate(xforms):
+                if f is None:
+                    continue
+                xa[j].kind = self._XF_KINDS[f["kind"]]
+                for key in ("a", "b", "w", "w_post", "h_out"):
+                    t = f.get(key)
+                    if t is not None:
+                        _need(t, key)
+                        setattr(xa[j], key, _ptr(t))
+                xa[j].scale = float(f.get("scale", 1.0))
+                xa[j].eps = float(f.get("eps", 1e-6))
+            self._keep.append(xforms)
+            L.check("g4b_gemv_chain_create_fused", self.lib.g4b_gemv_chain_create_fused(
+                ctypes.cast(arr, ctypes.c_void_p), ctypes.cast(xa, ctypes.c_void_p), len(steps), _DT[xdt], fmt,
+                _DT[o0[0].dtype], ctypes.byref(h)))
+        elif exchange is None:
             L.check("g4b_gemv_chain_create", self.lib.g4b_gemv_chain_create(
-                ctypes.cast(arr, ctypes.c_void_p), len(steps), _DT[x0.dtype], fmt, _DT[o0[0].dtype],
+                ctypes.cast(arr, ctypes.c_void_p), len(steps), _DT[xdt], fmt, _DT[o0[0].dtype],
                 ctypes.byref(h)))
         else:
             self._keep.append(exchange)
             L.check("g4b_gemv_chain_create_tp", self.lib.g4b_gemv_chain_create_tp(
-                ctypes.cast(arr, ctypes.c_void_p), len(steps), _DT[x0.dtype], fmt, _DT[o0[0].dtype],
+                ctypes.cast(arr, ctypes.c_void_p), len(steps), _DT[xdt], fmt, _DT[o0[0].dtype],
                 exchange.ptrs.data_ptr(), exchange.rank, exchange.world, exchange.nbytes, ctypes.byref(h)))
         self.handle = h.value
         self.nsteps = len(steps)

@@ -231,6 +231,47 @@ G4B_API size_t g4b_gemv_chain_exchange_bytes(const g4b_gemv_chain_step* steps, i
 G4B_API int g4b_gemv_chain_create_tp(const g4b_gemv_chain_step* steps, int nsteps, int x_dtype, int scale_fmt,
                                      int y_dtype, void* const* peers_dev, int rank, int world,
                                      size_t exchange_bytes, g4b_gemv_chain** chain);
+/* Element-wise work fused into a chain step's activation load: the engine's
+ * rmsnorm / normadd / gelumul dispatches between a decode layer's GEMVs
+ * (descriptor sets src/vk_engine.py:232, 243-251; dispatches :278-287).  Step j's x
+ * is then computed from the vectors below instead of read from step.x (which
+ * may be NULL); f32 arithmetic, K elements:
+ *   G4B_XF_RMSNORM   x = a * rsqrt(sum(a^2) / K + eps) * w          vk/rmsnorm.comp:8-12
+ *   G4B_XF_NORMADD   h' = (b + a * rsqrt(sum(a^2) / K + eps) * w_post) * scale
+ *                    x  = h' * rsqrt(sum(h'^2) / K + eps) * w       vk/normadd.comp:8-12,
+ *                    and h' is stored to h_out                      then vk/rmsnorm.comp
+ *   G4B_XF_GELU_MUL  x = 0.5 a (1 + tanh(0.7978845608 (a + 0.044715 a^3))) * b
+ *                                                                   vk/gelumul.comp:7-8
+ * Vectors and dtypes: a is step j-1's first output y (chain y dtype) -- for
+ * RMSNORM it may instead be a vector no step writes (f32: the token's input
+ * hidden state); b is the residual h (f32) for NORMADD, step
+ * j-1's `up` output (y dtype) for GELU_MUL; w, w_post (norm weights) and
+ * h_out are f32.  All 16-byte aligned; h_out must not overlap b.
+ * The sums come from step j-1's tile writers (per-tile partial sums, added in
+ * a fixed order, so a chain gives the same bits every run); the squares of h'
+ * are expanded as scale^2 (sum b^2 + 2 r sum b (a w_post) + r^2 sum (a w_post)^2)
+ * with r = rsqrt(sum(a^2) / K + eps).  One rank only (no G4B_CHAIN_ALLREDUCE
+ * next to a fused step). */
+#define G4B_XF_NONE      0
+#define G4B_XF_RMSNORM   1
+#define G4B_XF_NORMADD   2
+#define G4B_XF_GELU_MUL  3
+typedef struct g4b_chain_xform {
+    int kind;              /* G4B_XF_* */
+    const void* a;
+    const void* b;
+    const float* w;
+    const float* w_post;
+    float* h_out;
+    float scale;           /* NORMADD: the layer scalar (vk/normadd.comp's d.y; 1 = none) */
+    float eps;             /* 1e-6 in the reference */
+} g4b_chain_xform;
+
+/* g4b_gemv_chain_create with one g4b_chain_xform per step (kind G4B_XF_NONE:
+ * the step reads step.x as usual): a decode token's GEMVs and the element-wise
+ * work between them as one launch. */
+G4B_API int g4b_gemv_chain_create_fused(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xforms, int nsteps,
+                                        int x_dtype, int scale_fmt, int y_dtype, g4b_gemv_chain** chain);
 G4B_API size_t g4b_gemv_chain_workspace_bytes(const g4b_gemv_chain* chain);
 G4B_API int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_bytes, g4b_stream_t stream);
 G4B_API void g4b_gemv_chain_destroy(g4b_gemv_chain* chain);

@@ -23,6 +23,9 @@
  *   orc_gemm_w8a8       vk/coopgemm_w8a8.comp:18-37
  *   orc_w4a8_requant    vk/coopgemm_w4a8.comp:28-34
  *   orc_gemm_w4a8       vk/coopgemm_w4a8.comp:21-50
+ *   orc_rmsnorm         vk/rmsnorm.comp:8-12
+ *   orc_normadd         vk/normadd.comp:8-12
+ *   orc_gelumul         vk/gelumul.comp:7-8
  *
  * Choices the GLSL leaves to the implementation, fixed here and stated once:
  *   - round(): round-half-to-even (roundEven), the same as numpy's np.round used
@@ -30,6 +33,8 @@
  *   - no multiply-add contraction (built with -ffp-contract=off): every GLSL
  *     '*' and '+' is one correctly rounded f32 operation.
  *   - 1.0/s and amax/127.0 are correctly rounded f32 divisions.
+ *   - inversesqrt(v) is 1.0f / sqrtf(v), both correctly rounded (GLSL allows
+ *     2 ULP); tanh is the C library's tanhf.
  *
  * Parity pinning: the packing functions are pinned bit-for-bit against golden
  * vectors produced by running the reference's own quant() (tests/golden/).  The
@@ -406,6 +411,46 @@ void orc_gemm_w4a8(const int8_t* A8, const uint32_t* wp, const uint16_t* ratio16
     orc_w4a8_requant(wp, ratio16, N, K, w8);
     orc_gemm_w8a8(A8, w8, sa, sw16, M, N, K, C, Y16);
     free(w8);
+}
+
+/* The sum of squares as vk/rmsnorm.comp:9-10 and vk/normadd.comp:9-10 form it: 256
+ * invocations each add the squares of elements t, t + 256, ... in order, then a
+ * shared-memory tree folds the partials (sh[t] += sh[t + st] for st = 128 .. 1). */
+static float orc_sumsq_256(const float* x, int D) {
+    float sh[256];
+    for (int t = 0; t < 256; t++) {
+        float s = 0.0f;
+        for (int i = t; i < D; i += 256) {
+            const float v = x[i];
+            s += v * v;
+        }
+        sh[t] = s;
+    }
+    for (int st = 128; st > 0; st >>= 1)
+        for (int t = 0; t < st; t++) sh[t] += sh[t + st];
+    return sh[0];
+}
+
+/* vk/rmsnorm.comp:8-12: y[i] = x[i] * inv * w[i], inv = inversesqrt(sum / D + eps). */
+void orc_rmsnorm(const float* x, const float* w, float* y, int D, float eps) {
+    const float inv = 1.0f / sqrtf(orc_sumsq_256(x, D) / (float)D + eps);
+    for (int i = 0; i < D; i++) y[i] = x[i] * inv * w[i];
+}
+
+/* vk/normadd.comp:8-12: h[i] = (h[i] + x[i] * inv * w[i]) * sc (in place on h). */
+void orc_normadd(const float* x, const float* w, float* h, int D, float sc, float eps) {
+    const float inv = 1.0f / sqrtf(orc_sumsq_256(x, D) / (float)D + eps);
+    for (int i = 0; i < D; i++) h[i] = (h[i] + x[i] * inv * w[i]) * sc;
+}
+
+/* vk/gelumul.comp:7-8: out[i] = 0.5 x (1 + tanh(0.7978845608028654 (x + 0.044715 x^3))) * up[i],
+ * with the shader's left-to-right products. */
+void orc_gelumul(const float* gate, const float* up, float* out, int n) {
+    for (int i = 0; i < n; i++) {
+        const float x = gate[i];
+        const float g = 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
+        out[i] = g * up[i];
+    }
 }
 
 int orc_num_threads(void) {

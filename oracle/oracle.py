@@ -17,7 +17,7 @@ __all__ = [
     "lib", "build", "f16_to_f32", "f32_to_f16", "e4m3_decode", "e4m3_encode",
     "quant_i4", "fp8_scales", "split_for", "w8a8_weights", "w4a8_ratio", "gemv", "reduce",
     "dequant", "gemm_i4", "cast_i8", "gemm_w8a8", "w4a8_requant", "gemm_w4a8",
-    "num_threads", "set_num_threads", "pack_reference",
+    "num_threads", "set_num_threads", "pack_reference", "rmsnorm", "normadd", "gelumul", "decode_token",
 ]
 
 
@@ -55,6 +55,9 @@ def lib():
         L.orc_gemm_w8a8.argtypes = [P, P, P, P, i, i, i, P, P]
         L.orc_w4a8_requant.argtypes = [P, P, i, i, P]
         L.orc_gemm_w4a8.argtypes = [P, P, P, P, P, i, i, i, P, P]
+        L.orc_rmsnorm.argtypes = [P, P, P, i, f]
+        L.orc_normadd.argtypes = [P, P, P, i, f, f]
+        L.orc_gelumul.argtypes = [P, P, P, i]
         L.orc_num_threads.restype = i
         L.orc_set_num_threads.argtypes = [i]
         _lib = L
@@ -244,3 +247,61 @@ def pack_reference(W, fp8: bool = False, prefill_i8: bool = False):
         out["sw8"] = sw16
         out["sw_f32"] = swf
     return out
+
+
+# ---------------------------------------------------------------- decode-layer element-wise ops
+def rmsnorm(x, w, eps: float = 1e-6):
+    """vk/rmsnorm.comp:8-12 (f32)."""
+    x = _c(x, np.float32)
+    w = _c(w, np.float32)
+    y = np.empty_like(x)
+    lib().orc_rmsnorm(_p(x), _p(w), _p(y), x.size, float(eps))
+    return y
+
+
+def normadd(x, w, h, sc: float = 1.0, eps: float = 1e-6):
+    """vk/normadd.comp:8-12: returns (h + rmsnorm(x) * w) * sc (f32); h is not modified."""
+    x = _c(x, np.float32)
+    w = _c(w, np.float32)
+    out = np.array(h, dtype=np.float32, copy=True)
+    lib().orc_normadd(_p(x), _p(w), _p(out), x.size, float(sc), float(eps))
+    return out
+
+
+def gelumul(gate, up):
+    """vk/gelumul.comp:7-8 (f32)."""
+    g = _c(gate, np.float32)
+    u = _c(up, np.float32)
+    out = np.empty_like(g)
+    lib().orc_gelumul(_p(g), _p(u), _p(out), g.size)
+    return out
+
+
+def decode_token(h0, layers, lm_head, final_w, gemv_fn, round_x=None, round_y=None, eps: float = 1e-6):
+    """One decode token's weight path in the engine's dispatch order
+    (src/vk_engine.py:277-287) with attention left out: per layer rmsnorm ->
+    q|k|v -> o (on q, standing in for the attention output) -> normadd ->
+    rmsnorm -> gate|up -> gelumul -> down -> normadd; then rmsnorm -> lm_head.
+
+    layers: dicts with the packed weights "q", "k", "v", "o", "gate", "up",
+    "down" (anything gemv_fn takes) and the f32 norm weights "inw", "paw",
+    "pfw", "ofw" and layer scalar "scl".  gemv_fn(x, w) -> f32 y.  round_x /
+    round_y round a GEMV's input / output to the dtype the device chain keeps
+    them in (None: f32).  Returns (logits, final residual h, per-layer outputs)."""
+    rx = round_x or (lambda v: np.asarray(v, np.float32))
+    ry = round_y or (lambda v: np.asarray(v, np.float32))
+    h = np.asarray(h0, np.float32).copy()
+    outs = []
+    for L in layers:
+        x = rx(rmsnorm(h, L["inw"], eps))
+        q, k, v = (ry(gemv_fn(x, L[n])) for n in ("q", "k", "v"))
+        o = ry(gemv_fn(rx(q), L["o"]))
+        h = normadd(o, L["paw"], h, 1.0, eps)
+        x2 = rx(rmsnorm(h, L["pfw"], eps))
+        gate, up = ry(gemv_fn(x2, L["gate"])), ry(gemv_fn(x2, L["up"]))
+        act = rx(gelumul(gate, up))
+        down = ry(gemv_fn(act, L["down"]))
+        h = normadd(down, L["ofw"], h, L.get("scl", 1.0), eps)
+        outs.append({"q": q, "k": k, "v": v, "o": o, "gate": gate, "up": up, "down": down})
+    logits = ry(gemv_fn(rx(rmsnorm(h, final_w, eps)), lm_head))
+    return logits, h, outs
