@@ -42,29 +42,38 @@ unsigned read_status_gemm() {
 
 // ------------------------------------------------------------------ W4A16
 constexpr int kW4BN = 128;      // weight columns per tile (TMEM lanes)
-constexpr int kW4BT = 256;      // tokens per tile (MMA N)
+constexpr int kW4BT = 256;      // tokens per tile (MMA N) for prefill
+constexpr int kW4BTSmall = 64;  // tokens per tile for M <= 64 (batched decode): no MMA work on padding rows
 constexpr int kW4BK = 64;       // K rows per stage
 constexpr int kW4Stages = 6;  // even: dequant warps alternate stages
 constexpr int kW4DqWarps = 16;
 constexpr int kW4Threads = (2 + kW4DqWarps + 4) * 32;
-constexpr int kW4XBytes = kW4BT * kW4BK * 2;          // 32 KB
 constexpr int kW4WBytes = kW4BK * (kW4BN / 8) * 4;    // 4 KB
 constexpr int kW4SBytes = (kW4BK / 32) * kW4BN * 2;   // 512 B
 constexpr int kW4TmemCols = 512;
 static_assert(kW4Stages % 2 == 0 && 256 + 32 * kW4Stages <= kW4TmemCols, "TMEM budget");
-constexpr int kW4ACol = kW4BT;                         // first A column
-constexpr size_t kW4Smem = 1024 + (size_t)kW4Stages * (kW4XBytes + kW4WBytes + kW4SBytes);
+constexpr int kW4ACol = kW4BT;                         // first A column (after the widest accumulator)
+constexpr int kW4MaxSplit = 16;
+__host__ __device__ constexpr int w4_xbytes(int bt) { return bt * kW4BK * 2; }  // 32 KB / 8 KB
+__host__ __device__ constexpr size_t w4_smem(int bt) {
+    return 1024 + (size_t)kW4Stages * (w4_xbytes(bt) + kW4WBytes + kW4SBytes);
+}
 
+// Split-K: tile t of the launch is (column tile, token tile) t / S with the K range of split t % S;
+// with S > 1 each split writes its f32 partial to part[split][M][N] and a second kernel sums the
+// splits in order into y.
 struct W4Args {
     void* y;
-    int M, N, K, nkb, ntm, ntiles;
+    float* part;
+    int M, N, K, nkb, ntm, ntiles, S;
 };
 
-template <bool YF32>
+template <bool YF32, int BT, bool SPLIT>
 __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args a,
                                                                    const __grid_constant__ CUtensorMap xmap,
                                                                    const __grid_constant__ CUtensorMap wmap,
                                                                    const __grid_constant__ CUtensorMap smap) {
+    constexpr int kW4XBytes = w4_xbytes(BT);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[3 * kW4Stages + 3];
     __shared__ uint32_t s_tmem;
@@ -107,6 +116,8 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
     tc::fence_after();
     const uint32_t tmem = s_tmem;
     const int nks = a.nkb;  // K stages per tile
+    // K splits: only the SPLIT instance (small M) reads a.S; the prefill instance keeps every tile whole
+    const int S = SPLIT ? a.S : 1;
 
     if (warp == 0) {
         // ------------------------------------------------------- TMA producer
@@ -120,8 +131,10 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x) {
-                const int nt = t / a.ntm, mt = t % a.ntm;
-                for (int kb = 0; kb < nks; kb++, it++) {
+                const int tb = SPLIT ? t / S : t, ks = SPLIT ? t % S : 0;
+                const int nt = tb / a.ntm, mt = tb % a.ntm;
+                const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
+                for (int kb = kb0; kb < kb1; kb++, it++) {
                     const int s = it % kW4Stages;
                     if (it >= kW4Stages &&
                         !mbar_wait(empty_bar(s), ((it / kW4Stages) & 1) ^ 1, abort_flag, &g_gemm_status)) {
@@ -129,7 +142,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                         break;
                     }
                     mbar_arrive_expect_tx(full_bar(s), kW4XBytes + kW4WBytes + kW4SBytes);
-                    tma_load_2d(sm0 + s * kW4XBytes, &xmap, kb * kW4BK, mt * kW4BT, full_bar(s), pol_x);
+                    tma_load_2d(sm0 + s * kW4XBytes, &xmap, kb * kW4BK, mt * BT, full_bar(s), pol_x);
                     tma_load_2d(smw + s * kW4WBytes, &wmap, nt * (kW4BN / 8), kb * kW4BK, full_bar(s), pol_w);
                     tma_load_2d(sms + s * kW4SBytes, &smap, nt * kW4BN, kb * (kW4BK / 32), full_bar(s), pol_w);
                 }
@@ -141,13 +154,15 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
     } else if (warp == 1) {
         // ------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc(1, 0, 0, 0, 0, kW4BT, kW4BN);
+            constexpr uint32_t idesc = tc::idesc(1, 0, 0, 0, 0, BT, kW4BN);
             int it = 0, tc_i = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x, tc_i++) {
                 if (!mbar_wait(dempty_bar, (tc_i & 1) ^ 1, abort_flag, &g_gemm_status)) break;
                 tc::fence_after();
-                for (int kb = 0; kb < nks; kb++, it++) {
+                const int ks = SPLIT ? t % S : 0;
+                const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
+                for (int kb = kb0; kb < kb1; kb++, it++) {
                     const int s = it % kW4Stages;
                     const uint32_t ph = (it / kW4Stages) & 1;
                     if (!mbar_wait(full_bar(s), ph, abort_flag, &g_gemm_status) ||
@@ -160,7 +175,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
 #pragma unroll
                     for (int kk = 0; kk < kW4BK / 16; kk++)
                         tc::mma_f16_ts(tmem, tmem + kW4ACol + s * (kW4BK / 2) + kk * 8, bdesc + (uint64_t)(kk * 2),
-                                       idesc, (kb | kk) != 0);
+                                       idesc, SPLIT ? ((kb != kb0 || kk != 0) ? 1u : 0u) : (uint32_t)((kb | kk) != 0));
                     tc::commit(empty_bar(s));
                 }
                 if (ok) tc::commit(dfull_bar);
@@ -182,7 +197,9 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
         int it = 0;
         bool ok = true;
         for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x) {
-            for (int kb = 0; kb < nks; kb++, it++) {
+            const int ks = SPLIT ? t % S : 0;
+            const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
+            for (int kb = kb0; kb < kb1; kb++, it++) {
                 if ((it & 1) != par) continue;
                 const int s = it % kW4Stages;
                 if (!mbar_wait(full_bar(s), (it / kW4Stages) & 1, abort_flag, &g_gemm_status)) {
@@ -221,24 +238,34 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
         for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, tc_i++) {
             if (!mbar_wait(dfull_bar, tc_i & 1, abort_flag, &g_gemm_status)) break;
             tc::fence_after();
-            const int nt = t / a.ntm, mt = t % a.ntm;
+            const int tb = SPLIT ? t / S : t, ks = SPLIT ? t % S : 0;
+            const int nt = tb / a.ntm, mt = tb % a.ntm;
             const int n = nt * kW4BN + nl;
-            const int m0 = mt * kW4BT;
+            const int m0 = mt * BT;
+            float* const part = SPLIT && S > 1 ? a.part + (size_t)ks * a.M * a.N : nullptr;
 #pragma unroll 1
-            for (int c = 0; c < kW4BT / 32; c++) {
+            for (int c = 0; c < BT / 32; c++) {
                 uint32_t r[32];
                 tc::ld_32x32b_x32(tmem + lane_addr + c * 32, r);
                 tc::wait_ld();
                 const int mb = m0 + c * 32;
+                // the f32 partials of a K split, or y; the row index is checked per element (M may end mid-tile)
+                if (SPLIT && part) {
+                    float* pp = part + (size_t)mb * a.N + n;  // one running address: no extra registers
 #pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const int m = mb + i;
-                    if (m < a.M) {
-                        const float f = __uint_as_float(r[i]);
-                        if (YF32)
-                            reinterpret_cast<float*>(a.y)[(size_t)m * a.N + n] = f;
-                        else
-                            reinterpret_cast<__half*>(a.y)[(size_t)m * a.N + n] = __float2half_rn(f);
+                    for (int i = 0; i < 32; i++, pp += a.N)
+                        if (mb + i < a.M) *pp = __uint_as_float(r[i]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const int m = mb + i;
+                        if (m < a.M) {
+                            const float f = __uint_as_float(r[i]);
+                            if (YF32)
+                                reinterpret_cast<float*>(a.y)[(size_t)m * a.N + n] = f;
+                            else
+                                reinterpret_cast<__half*>(a.y)[(size_t)m * a.N + n] = __float2half_rn(f);
+                        }
                     }
                 }
             }
@@ -299,6 +326,9 @@ struct S8Cfg {
 };
 static_assert(256 + 32 * kS8Stages <= 512, "TMEM budget");
 
+// Tile t is (token tile t / ntn, column tile t % ntn): the CTAs resident at once share a few
+// activation panels and sweep every column tile, so the whole int8 weight (59 MB at config 4)
+// stays in L2 across waves and each activation panel is read from DRAM about once.
 struct S8Args {
     void* y;
     int32_t* c;           // nullable raw accumulators
@@ -361,12 +391,15 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
             prefetch_tensor_map(&amap);
             prefetch_tensor_map(&wmap);
             if (W4) prefetch_tensor_map(&rmap);
+            // the weights are swept again by every wave of tiles: keep them in L2; an activation panel
+            // is read by the CTAs of one wave only (token-tile-major order), so it may go first
             uint64_t pol_keep;
             asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_keep));
+            const uint64_t pol_once = l2_evict_first_policy();
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x) {
-                const int nt = t / a.ntm, mt = t % a.ntm;
+                const int ntn = a.ntiles / a.ntm, mt = t / ntn, nt = t % ntn;  // token-tile major: see S8Args
                 for (int kb = 0; kb < nks; kb++, it++) {
                     const int s = it % kS8Stages;
                     if (it >= kS8Stages &&
@@ -375,7 +408,7 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(full_bar(s), Cfg::kStageBytes);
-                    tma_load_2d(sm0 + s * kS8ABytes, &amap, kb * kS8BK, mt * kS8BT, full_bar(s), pol_keep);
+                    tma_load_2d(sm0 + s * kS8ABytes, &amap, kb * kS8BK, mt * kS8BT, full_bar(s), pol_once);
                     if (W4) {
                         const uint32_t dst = smw + s * Cfg::kWBytes;
                         tma_load_2d(dst, &wmap, nt * (kS8BN / 8), kb * kS8BK, full_bar(s), pol_keep);
@@ -506,7 +539,7 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
             const uint32_t use = (uint32_t)(tc_i / Cfg::kAccBufs);
             if (!mbar_wait(dfull_bar(buf), use & 1, abort_flag, &g_gemm_status)) break;
             tc::fence_after();
-            const int nt = t / a.ntm, mt = t % a.ntm;
+            const int ntn = a.ntiles / a.ntm, mt = t / ntn, nt = t % ntn;  // token-tile major: see S8Args
             const int n = nt * kS8BN + nl;
             const bool nok = n < a.N;
             const float swf = nok ? __half2float(__ushort_as_half(a.sw[n])) : 0.0f;
@@ -547,9 +580,53 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
     if (warp == 1) tc::tmem_dealloc(tmem, 512);
 }
 
-static size_t w4a16_ws(int M, int K, int x_dtype) {
-    return x_dtype == G4B_DT_F32 ? (((size_t)M * K * 2 + 255) & ~(size_t)255) : 0;
+// y[i] = sum over the splits s = 0 .. S-1 of part[s][i], in split order (deterministic)
+template <bool YF32>
+__global__ void w4a16_splitk_reduce(const float* __restrict__ part, void* __restrict__ y, size_t n4, size_t stride,
+                                    int S) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        float4 v = __ldg(reinterpret_cast<const float4*>(part) + i);
+        for (int s = 1; s < S; s++) {
+            const float4 u = __ldg(reinterpret_cast<const float4*>(part + (size_t)s * stride) + i);
+            v.x += u.x;
+            v.y += u.y;
+            v.z += u.z;
+            v.w += u.w;
+        }
+        if (YF32) {
+            reinterpret_cast<float4*>(y)[i] = v;
+        } else {
+            uint2 h;
+            h.x = pack_half2(__float2half_rn(v.x), __float2half_rn(v.y));
+            h.y = pack_half2(__float2half_rn(v.z), __float2half_rn(v.w));
+            reinterpret_cast<uint2*>(y)[i] = h;
+        }
+    }
 }
+
+// How a W4A16 GEMM is tiled: the token-tile width and the number of K splits.  Small-M GEMMs
+// (batched decode) use 64-token tiles, and when their column tiles cannot fill the SMs they split
+// K so that about one tile per SM runs, keeping at least 4 K stages (256 rows) per split.
+struct W4Plan {
+    int bt, ntm, base, S;
+    size_t xconv_bytes, part_bytes;
+};
+
+static W4Plan w4a16_plan(int M, int N, int K, int x_dtype, int sms) {
+    W4Plan p{};
+    p.bt = M <= kW4BTSmall ? kW4BTSmall : kW4BT;
+    p.ntm = (M + p.bt - 1) / p.bt;
+    p.base = (N / kW4BN) * p.ntm;
+    const int nkb = K / kW4BK;
+    p.S = 1;
+    if (p.bt == kW4BTSmall && p.base * 2 <= sms && nkb >= 8)
+        p.S = std::max(1, std::min({sms / std::max(p.base, 1), nkb / 4, kW4MaxSplit}));
+    p.xconv_bytes = x_dtype == G4B_DT_F32 ? (((size_t)M * K * 2 + 255) & ~(size_t)255) : 0;
+    p.part_bytes = p.S > 1 ? (size_t)p.S * M * N * sizeof(float) : 0;
+    return p;
+}
+
+static size_t w4a16_ws(const W4Plan& p) { return p.xconv_bytes + p.part_bytes; }
 
 }  // namespace g4b
 
@@ -558,9 +635,11 @@ using namespace g4b;
 extern "C" {
 
 size_t g4b_gemm_i4_workspace_bytes(int M, int N, int K, int x_dtype) {
-    (void)N;
-    if (M <= 0 || K <= 0) return 0;
-    return w4a16_ws(M, K, x_dtype);
+    if (M <= 0 || K <= 0 || N <= 0 || N % kW4BN || K % kW4BK) return 0;
+    int sms = 148;
+    if (check_device(&sms) != G4B_OK) sms = 148;
+    clear_error();
+    return w4a16_ws(w4a16_plan(M, N, K, x_dtype, sms));
 }
 
 int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* scales_f16, void* Y, int y_dtype,
@@ -578,20 +657,21 @@ int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* 
     int st = check_device(&sms);
     if (st != G4B_OK) return st;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    const size_t need = w4a16_ws(M, K, x_dtype);
+    W4Plan p = w4a16_plan(M, N, K, x_dtype, sms);
+    if (p.S > 1 && (!workspace || ws_bytes < w4a16_ws(p))) {
+        // the split-K partials do not fit the caller's workspace: one split (always correct)
+        p.S = 1;
+        p.part_bytes = 0;
+    }
+    const size_t need = w4a16_ws(p);
     G4B_REQUIRE(ws_bytes >= need && (need == 0 || workspace), G4B_E_WORKSPACE,
                 "gemm_i4: f32 X needs a %zu-byte workspace (got %zu)", need, ws_bytes);
-    const void* X16 = X;
-    if (x_dtype == G4B_DT_F32) {
-        G4B_REQUIRE(aligned16(workspace), G4B_E_ALIGN, "gemm_i4: workspace must be 16-byte aligned");
-        st = cast_f32_to_f16_async(reinterpret_cast<const float*>(X), reinterpret_cast<__half*>(workspace),
-                                   (size_t)M * K, s);
-        if (st != G4B_OK) return st;
-        X16 = workspace;
-    }
+    G4B_REQUIRE(need == 0 || aligned16(workspace), G4B_E_ALIGN, "gemm_i4: workspace must be 16-byte aligned");
+    // encode the tensor maps first: nothing is queued until every check has passed
+    const void* X16 = x_dtype == G4B_DT_F32 ? workspace : X;
     CUtensorMap xmap, wmap, smap;
     st = tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kW4BK,
-                       kW4BT, CU_TENSOR_MAP_SWIZZLE_128B);
+                       p.bt, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st == G4B_OK)
         st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, wp, (uint64_t)N / 8, (uint64_t)K, (uint64_t)N / 2,
                            kW4BN / 8, kW4BK, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -601,17 +681,35 @@ int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* 
     if (st != G4B_OK) return st;
     W4Args a;
     a.y = Y;
+    a.part = p.part_bytes ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + p.xconv_bytes) : nullptr;
     a.M = M;
     a.N = N;
     a.K = K;
     a.nkb = K / kW4BK;
-    a.ntm = (M + kW4BT - 1) / kW4BT;
-    a.ntiles = (N / kW4BN) * a.ntm;
-    auto kern = y_dtype == G4B_DT_F32 ? gemm_w4a16_kernel<true> : gemm_w4a16_kernel<false>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kW4Smem);
+    a.ntm = p.ntm;
+    a.S = p.S;
+    a.ntiles = p.base * p.S;
+    const bool yf32 = y_dtype == G4B_DT_F32;
+    auto kern = p.bt == kW4BT ? (yf32 ? gemm_w4a16_kernel<true, kW4BT, false> : gemm_w4a16_kernel<false, kW4BT, false>)
+                              : (yf32 ? gemm_w4a16_kernel<true, kW4BTSmall, true>
+                                      : gemm_w4a16_kernel<false, kW4BTSmall, true>);
+    const size_t smem = w4_smem(p.bt);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemm_i4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    if (x_dtype == G4B_DT_F32) {
+        st = cast_f32_to_f16_async(reinterpret_cast<const float*>(X), reinterpret_cast<__half*>(workspace),
+                                   (size_t)M * K, s);
+        if (st != G4B_OK) return st;
+    }
     const int grid = std::min(a.ntiles, sms);
-    kern<<<grid, kW4Threads, kW4Smem, s>>>(a, xmap, wmap, smap);
+    kern<<<grid, kW4Threads, smem, s>>>(a, xmap, wmap, smap);
+    count_launch();
+    st = launch_status("gemm_i4");
+    if (st != G4B_OK || p.S == 1) return st;
+    const size_t n4 = (size_t)M * N / 4;
+    const int threads = 256, blocks = (int)std::min<size_t>((n4 + threads - 1) / threads, (size_t)sms * 8);
+    if (yf32) w4a16_splitk_reduce<true><<<blocks, threads, 0, s>>>(a.part, Y, n4, (size_t)M * N, p.S);
+    else w4a16_splitk_reduce<false><<<blocks, threads, 0, s>>>(a.part, Y, n4, (size_t)M * N, p.S);
     count_launch();
     return launch_status("gemm_i4");
 }

@@ -291,6 +291,12 @@ class GemvChain:
             pass
 
 
+def gemm_i4_workspace_bytes(M: int, N: int, K: int, x_dtype: torch.dtype = torch.float16) -> int:
+    """Workspace g4b_gemm_i4 can use: the f16 copy of an f32 X, plus the split-K
+    partials of a small-M GEMM (batched decode)."""
+    return int(L.load().g4b_gemm_i4_workspace_bytes(M, N, K, _DT[x_dtype]))
+
+
 def gemm_i4(X: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None,
             out_dtype: torch.dtype = torch.float16, stream: Optional[torch.cuda.Stream] = None,
             workspace: Optional[torch.Tensor] = None) -> torch.Tensor:

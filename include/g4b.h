@@ -333,8 +333,12 @@ G4B_API int g4b_cast_i8(const void* X, int x_dtype, int8_t* A8, float* sa, int M
 
 /* ---------------------------------------------------------------- prefill GEMMs */
 
-/* Bytes of workspace g4b_gemm_i4 needs: non-zero only for f32 X, which is
- * first converted to f16 in the workspace (the cast_dn step). */
+/* Bytes of workspace g4b_gemm_i4 can use for these sizes: the f16 copy of an
+ * f32 X (the cast_dn step; required for f32 X), plus, for small M whose
+ * column tiles cannot fill the SMs (batched decode), the f32 partials of a
+ * K split across the SMs.  With a smaller workspace -- or none, for f16 X --
+ * the GEMM runs without the split; the result is the same up to f32
+ * summation order. */
 G4B_API size_t g4b_gemm_i4_workspace_bytes(int M, int N, int K, int x_dtype);
 
 /* W4A16 prefill GEMM with in-kernel dequantisation: vk/coopgemm_i4h.comp:13-35
@@ -346,7 +350,9 @@ G4B_API size_t g4b_gemm_i4_workspace_bytes(int M, int N, int K, int x_dtype);
  * dequantised weights are bit-identical to the shader's; the accumulator is
  * f32 (the i4h shader accumulates in f16).  X [M, K] f16 or f32 (f32 is
  * converted to f16 in `workspace`, RNE, as cast_dn does); Y [M, N] f16 or f32.
- * M >= 1 (any), N % 128 == 0, K % 64 == 0; pointers 16-byte aligned. */
+ * M >= 1 (any), N % 128 == 0, K % 64 == 0; pointers 16-byte aligned.  M <= 64
+ * runs 64-token tiles; a K split (see g4b_gemm_i4_workspace_bytes) adds a
+ * second launch that sums the splits' partials in split order. */
 G4B_API int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* scales_f16,
                         void* Y, int y_dtype, int M, int N, int K,
                         void* workspace, size_t ws_bytes, g4b_stream_t stream);

@@ -117,3 +117,30 @@ def test_gemm_f32_staging_does_not_disturb_gemv():
     assert L.query(L.Q_KERNEL_STATUS) == 0
     ref = O.gemv(x, pw.wp, pw.scales.view(np.uint16), 0, 1.0, Ng, Kg, pw.split)
     assert_close(y.cpu().numpy(), ref, "gemv after an f32 gemm_i4")
+
+
+# Batched-decode shapes: M <= 64 runs 64-token tiles, and when the column tiles
+# cannot fill the SMs K is split across them (f32 partials in the workspace,
+# summed in split order by a second kernel).  Reference: the fp64 product of
+# the same f16 operands (bit-exact dequant), with the long-K guard.
+@pytest.mark.parametrize("M", [1, 8, 64])
+@pytest.mark.parametrize("N,K", [(2048, 3840), (4096, 3840), (3840, 15360)])
+def test_gemm_i4_small_m_split_k(M, N, K):
+    pw, dw = _dw(N, K, seed=M + N)
+    assert ops.gemm_i4_workspace_bytes(M, N, K, torch.float16) > 0        # the split-K plan is taken
+    X16 = torch.from_numpy(activations(M, K, seed=7).astype(np.float16)).to(DEV)
+    Y = ops.gemm_i4(X16, dw, out_dtype=torch.float32)
+    Y2 = ops.gemm_i4(X16, dw, out_dtype=torch.float32)
+    Wd = ops.dequant_i4(dw, out_dtype=torch.float16)
+    ref = (X16.double() @ Wd.double()).cpu().numpy()
+    # no workspace: one split, the same product up to f32 summation order
+    lib = L.load()
+    Y1 = torch.empty_like(Y)
+    st = lib.g4b_gemm_i4(X16.data_ptr(), L.DT_F16, dw.wp.data_ptr(), dw.scales16.data_ptr(), Y1.data_ptr(), L.DT_F32,
+                         M, N, K, None, 0, torch.cuda.current_stream().cuda_stream)
+    assert st == L.G4B_OK, L.last_error()
+    torch.cuda.synchronize()
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+    assert torch.equal(Y, Y2)                                                 # deterministic
+    assert_close(Y.cpu().numpy(), ref, f"split-K M={M} N={N} K={K}", guard=LONG_K_GUARD)
+    assert_close(Y1.cpu().numpy(), ref, f"one split M={M} N={N} K={K}", guard=LONG_K_GUARD)
