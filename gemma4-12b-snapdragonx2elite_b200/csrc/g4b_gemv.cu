@@ -1386,10 +1386,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
             }
             const int xk = dj->xf_kind;
             // the step's norm scales, once per step: from the producer's tile sums (summed in a fixed
-            // lane order) or, for a vector the chain did not write, from the vector itself
+            // lane order) or, for a vector the chain did not write, from the vector itself.  The sums'
+            // loads are issued here and only reduced after the first slice's loads are in flight, so
+            // they cost no round trip of their own.
             float inv_r = 0.f, inv_h = 0.f;
-            if (xk != kXfNone && xk != kXfGeluMul && iend > ibeg) {
-                float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
+            bool scales_ready = xk == kXfNone || xk == kXfGeluMul || iend <= ibeg;
+            float4 S = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (!scales_ready) {
                 if (dj->xf_self) {
                     for (int r0 = 8 * lane; r0 < K; r0 += 256) {
                         float a8[8];
@@ -1406,6 +1409,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         S.w += v.w;
                     }
                 }
+            }
+            auto norm_scales = [&]() {
                 #pragma unroll
                 for (int m = 16; m >= 1; m >>= 1) {
                     S.x += __shfl_xor_sync(0xffffffffu, S.x, m);
@@ -1423,7 +1428,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                     const float sh = dj->xf_scale * dj->xf_scale * fmaf(inv_r * inv_r, S.z, fmaf(2.0f * inv_r, S.y, S.x));
                     inv_h = rsqrtf(fmaxf(sh, 0.f) * invK + dj->xf_eps);
                 }
-            }
+                scales_ready = true;
+            };
             int nh = 0;  // slices of h_out this warp wrote in this step
             int o = ibeg % noct;
             for (int it = ibeg; it < iend; ++it, ++i) {
@@ -1458,6 +1464,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         if (dj->xf_self) load8<true>(dj->xf_a, r0, a8);
                         else load8<YF32>(dj->xf_a, r0, a8);
                         load8<true>(dj->xf_w, r0, w8);
+                        if (!scales_ready) norm_scales();
                         #pragma unroll
                         for (int e = 0; e < 8; e++) v[e] = a8[e] * inv_h * w8[e];
                     } else {
@@ -1468,6 +1475,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         load8<true>(dj->xf_b, r0, h8);
                         load8<true>(dj->xf_wpost, r0, p8);
                         load8<true>(dj->xf_w, r0, w8);
+                        if (!scales_ready) norm_scales();
                         #pragma unroll
                         for (int e = 0; e < 8; e++) {
                             h8[e] = (h8[e] + r8[e] * inv_r * p8[e]) * dj->xf_scale;
@@ -1653,10 +1661,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                     float v = 0.f;
                     bool ok = true;
                     uint64_t t0 = 0;
-                    for (int k0 = c_first; k0 <= c_last && ok; k0 += 8) {
-                        unsigned long long w[8];
+                    // up to 16 sharers' words in flight at once (one round trip for the decode shapes)
+                    constexpr int kPoll = 16;
+                    for (int k0 = c_first; k0 <= c_last && ok; k0 += kPoll) {
+                        unsigned long long w[kPoll];
                         #pragma unroll
-                        for (int k = 0; k < 8; k++) {
+                        for (int k = 0; k < kPoll; k++) {
                             const int cc = k0 + k;
                             const int sl = 2 * cc + (cc == c_first ? (int)(f >> 31) : 0);
                             w[k] = cc <= c_last ? ld_relaxed_gpu_u64(&partial[(size_t)sl * kStTN + col])
@@ -1665,7 +1675,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         for (;;) {
                             bool all = true;
                             #pragma unroll
-                            for (int k = 0; k < 8; k++) all = all && (unsigned)(w[k] >> 32) == tag;
+                            for (int k = 0; k < kPoll; k++) all = all && (unsigned)(w[k] >> 32) == tag;
                             if (all) break;
                             if (t0 == 0) t0 = global_ns();
                             if (*abort_flag || *(volatile unsigned*)gabort) {
@@ -1680,7 +1690,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                                 break;
                             }
                             #pragma unroll
-                            for (int k = 0; k < 8; k++) {
+                            for (int k = 0; k < kPoll; k++) {
                                 const int cc = k0 + k;
                                 const int sl = 2 * cc + (cc == c_first ? (int)(f >> 31) : 0);
                                 if ((unsigned)(w[k] >> 32) != tag)
@@ -1688,7 +1698,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                             }
                         }
                         #pragma unroll
-                        for (int k = 0; k < 8; k++)
+                        for (int k = 0; k < kPoll; k++)
                             if (k0 + k <= c_last) v += __uint_as_float((unsigned)w[k]);
                     }
                     if (ok) write_y(t, col, v);
