@@ -254,6 +254,12 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x
                  : "memory");
 }
 
+// Bring `bytes` (a multiple of 16, 16-byte aligned address) of global memory into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)), "r"(bytes)
+                 : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -1361,6 +1361,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         const int lt = t - tc_seg(d, sg).tile0;
                         tma_prefetch_l2_2d(&wm[sg], lt * (kStTN / 8), o * kM1Rows);
                         tma_prefetch_l2_2d(&sm[sg], lt * (kStTN * ssz / 8), o * 8);
+                        // the item's x slice too, so that its load after the step boundary hits L2 (the
+                        // lines stay coherent with whatever an earlier step writes to them later)
+                        if (d.x && d.xreg < 0 && d.xf_kind == kXfNone)
+                            bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(d.x) + (size_t)o * kM1Rows * esz,
+                                             kM1Rows * esz);
                     }
                     if (++o == d.noct) {
                         o = 0;
