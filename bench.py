@@ -254,6 +254,11 @@ def describe(args, world: int) -> dict:
                 "scaling": "weak",
                 "config": {"workload": text, "M": M, "N": N, "K": K, "parallelism": f"replicas{world}",
                            "l2": "256 MB buffer written between timed iterations (L2 flush, outside the events)"}}
+    if wl == "engine":
+        return {"metric": "decode tok/s at context 16 (engine harness, attention stand-in)", "unit": "tok/s",
+                "scaling": "weak",
+                "config": {"workload": "benchmarks/bench_engine.py's measurements on the configs[1] stack",
+                           "layers": args.layers, "parallelism": f"replicas{world}"}}
     if wl == "prefill":
         return {"metric": f"W4A16 prefill GEMM TFLOP/s (48-layer stack, M={PREFILL_M} split over GPUs)",
                 "unit": "TFLOP/s", "scaling": "strong",
@@ -340,6 +345,11 @@ def reference_sampler(args) -> dict:
         work = sum(2 * rows * N * K for N, K, *_ in mats)
         return {"step": step, "work": work, "unit": unit, "div": 1e12, "sample": what, "cores": O.num_threads()}
     # GEMV workloads: the reference's split (quant()'s heuristic) and reduce
+    if wl == "engine":
+        # decode tokens/s: one layer's seven GEMVs per step is 1/LAYERS of a token's matmuls
+        st = reference_sampler(argparse.Namespace(**{**vars(args), "workload": "stream"}))
+        return {"step": st["step"], "work": 1.0 / LAYERS, "unit": "tok/s", "div": 1.0, "cores": st["cores"],
+                "sample": st["sample"] + f"; reported as tokens/s of a {LAYERS}-layer token's GEMVs"}
     if wl == "gemv":
         shapes = [("lm_head", VOCAB, HIDDEN)] if args.shape == "lm_head" else [("gate", FFN, HIDDEN)]
         what = f"one GEMV W[{shapes[0][1]}, {shapes[0][2]}] per step"
@@ -1188,6 +1198,125 @@ def measure_fused_token(c, layers, lm, steps, warmup, dtype_name="f16"):
             "gpu_launches": steps}
 
 
+ENGINE_CTX = (16, 1024, 4096)
+PROMPT_LEN = 2048
+NH, NKV_HEADS, HEAD_DIM = 16, 8, 256
+
+
+def measure_engine(c, args):
+    """benchmarks/bench_engine.py:14-41 on this stack: decode tok/s at a context
+    of 16, 1024 and 4096 tokens, and prefill prompt-tok/s on a 2048-token prompt.
+
+    The 48 layers' matmuls and the decode layer's element-wise work are g4b's:
+    a decode token is one fused chain launch per layer, split at attention
+    (g4b.decode.SegmentedDecodeToken); prefill runs the W4A16 GEMMs (and, as
+    PREFILL_I8 does, cast_i8 + the W8A8 GEMMs).  Attention and, in prefill, the
+    norms and gelu*up over [T, H] rows are stand-ins outside this path: torch's
+    scaled_dot_product_attention over a synthetic f16 KV cache (GQA, 16 query
+    and 8 KV heads of 256) and torch element-wise ops.  Decode is timed as K
+    graph replays at a fixed context (the reference grows it by 64 tokens);
+    prefill is one pass over the prompt in one batch, the logits for its last
+    token."""
+    torch = c.torch
+    F = torch.nn.functional
+    from g4b import decode
+
+    gen = c.gen(31)
+    H = HIDDEN
+    layers_w, layers_d = [], []
+    for _ in range(args.layers):
+        dd = {}
+        for name, N, K in LAYER_SHAPES:
+            W = torch.randn((N, K), generator=gen, device=c.device).mul_(0.02)
+            dd[name] = c.qz.quant_device(W, pf=True, fp8=False, prefill_i8=True)
+            del W
+        layers_w.append(dd)
+        layers_d.append(c.tp.TPLayer(**dd))
+    W = torch.randn((VOCAB, H), generator=gen, device=c.device).mul_(0.02)
+    lm = c.qz.quant_device(W, pf=False, fp8=False, prefill_i8=False)
+    del W
+    torch.cuda.empty_cache()
+    nw = lambda: (1.0 + 0.1 * torch.randn((H,), generator=gen, device=c.device))  # noqa: E731
+    norms = [decode.LayerNorms(inw=nw(), paw=nw(), pfw=nw(), ofw=nw(), scl=1.0) for _ in range(args.layers)]
+    finw = nw()
+    out = {"attention": "stand-in: torch scaled_dot_product_attention (GQA 16/8 heads of 256) over an f16 KV cache",
+           "steps": args.steps}
+    # ---- decode
+    tok = decode.SegmentedDecodeToken(layers_d, norms, lm, finw, dtype=torch.float16)
+    tok.h0.copy_(torch.randn((H,), generator=gen, device=c.device))
+    for ctx in ENGINE_CTX:
+        kc = torch.randn((args.layers, 1, NKV_HEADS, ctx, HEAD_DIM), generator=gen, device=c.device).half()
+        vc = torch.randn((args.layers, 1, NKV_HEADS, ctx, HEAD_DIM), generator=gen, device=c.device).half()
+
+        def attention(li, stream, kc=kc, vc=vc, ctx=ctx):
+            b = tok.bufs
+            kc[li, 0, :, ctx - 1].copy_(b["k"].view(NKV_HEADS, HEAD_DIM))   # this token's k, v in the cache
+            vc[li, 0, :, ctx - 1].copy_(b["v"].view(NKV_HEADS, HEAD_DIM))
+            o = F.scaled_dot_product_attention(b["q"].view(1, NH, 1, HEAD_DIM), kc[li], vc[li], enable_gqa=True)
+            b["attn"].copy_(o.view(-1))
+
+        graph = capture(c, lambda: tok.run(c.stream, attention), args.warmup)
+        ms = timed_graph(c, graph, args.steps) / args.steps
+        out[f"decode tok/s @ctx {ctx}"] = round(1000.0 / ms, 1)
+        out[f"decode ms/token @ctx {ctx}"] = round(ms, 4)
+        del graph, kc, vc
+        torch.cuda.empty_cache()
+    out["decode launches/token"] = f"{len(tok.chains)} chain launches + the attention stand-in's kernels"
+    tok.close()
+    # ---- prefill: one 2048-token prompt
+    T = PROMPT_LEN
+    X0 = torch.randn((T, H), generator=gen, device=c.device)
+    logits = torch.empty((VOCAB,), device=c.device, dtype=torch.float16)
+    A8 = torch.empty((T, FFN), dtype=torch.int8, device=c.device)
+    sa = torch.empty((T,), dtype=torch.float32, device=c.device)
+    lib = c.L.load()
+
+    def rms(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + decode.EPS) * w
+
+    def mm(x16, w, i8):
+        if not i8:
+            return c.ops.gemm_i4(x16, w, out_dtype=torch.float16, stream=c.stream)
+        M_, K_ = x16.shape
+        c.L.check("g4b_cast_i8", lib.g4b_cast_i8(x16.data_ptr(), c.L.DT_F16, A8.data_ptr(), sa.data_ptr(), M_, K_,
+                                                 c.sh))
+        return c.ops.gemm_w8a8(A8.view(-1)[:M_ * K_].view(M_, K_), sa[:M_], w, stream=c.stream)
+
+    def prefill(i8):
+        h = X0
+        for dd, nm in zip(layers_w, norms):
+            x = rms(h, nm.inw).half()
+            q, k, v = mm(x, dd["q"], i8), mm(x, dd["k"], i8), mm(x, dd["v"], i8)
+            a = F.scaled_dot_product_attention(q.view(T, NH, HEAD_DIM).transpose(0, 1)[None],
+                                               k.view(T, NKV_HEADS, HEAD_DIM).transpose(0, 1)[None],
+                                               v.view(T, NKV_HEADS, HEAD_DIM).transpose(0, 1)[None],
+                                               is_causal=True, enable_gqa=True)
+            o = mm(a[0].transpose(0, 1).reshape(T, NQ).contiguous(), dd["o"], i8)
+            h = h + rms(o.float(), nm.paw)
+            x2 = rms(h, nm.pfw).half()
+            g, u = mm(x2, dd["gate"], i8), mm(x2, dd["up"], i8)
+            act = (F.gelu(g.float(), approximate="tanh") * u.float()).half()
+            h = (h + rms(mm(act, dd["down"], i8).float(), nm.ofw)) * nm.scl
+        c.ops.gemv_i4(rms(h[-1], finw).half(), lm, out=logits, stream=c.stream)
+
+    for i8 in (False, True):
+        with torch.cuda.stream(c.stream):
+            prefill(i8)                                       # warm-up
+            c.stream.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(c.stream)
+            prefill(i8)
+            e1.record(c.stream)
+        c.stream.synchronize()
+        ms = c.max(e0.elapsed_time(e1))
+        key = "prefill prompt-tok/s (PREFILL_I8: cast_i8 + W8A8)" if i8 else "prefill prompt-tok/s (W4A16)"
+        out[key] = round(T / (ms / 1e3), 1)
+    del layers_w, layers_d, X0, A8
+    torch.cuda.empty_cache()
+    return out
+
+
 def one_gpu_extras(c, args, model):
     """The other BASELINE.json configs on this GPU, each with its own value and roofline."""
     ex = {}
@@ -1215,6 +1344,7 @@ def one_gpu_extras(c, args, model):
         r = measure_gemm(c, key, args.steps, args.warmup)
         r["workload"] = text
         ex[f"{'configs[2]' if kind == 'w4a16' else 'configs[3]'} {key}"] = r
+    ex["engine harness (benchmarks/bench_engine.py shape)"] = measure_engine(c, args)
     return ex
 
 
@@ -1312,6 +1442,20 @@ def run_prefill(args) -> None:
     c.close()
 
 
+def run_engine(args) -> None:
+    """The engine harness alone (benchmarks/bench_engine.py's measurements)."""
+    c = Ctx()
+    d = describe(args, c.world)
+    r = measure_engine(c, args)
+    if c.rank == 0:
+        v = r["decode tok/s @ctx 16"]
+        out = header(args, c, d, v, r["decode ms/token @ctx 16"], "int4 x f16 -> f32 acc",
+                     "synthetic (seeded N(0,0.02) weights, N(0,1) hidden state and KV cache)")
+        out.update({"engine": r, "cpu_baseline": None, "e2e": None, "gpu_launches": None})
+        print(json.dumps(out), flush=True)
+    c.close()
+
+
 def select_runner(args, world: int):
     """The function that produces this run's line.  ``--impl reference`` is
     resolved first, whatever the workload and world size, so that the
@@ -1324,6 +1468,8 @@ def select_runner(args, world: int):
         return run_prefill
     if args.workload == "gemv":
         return run_gemv
+    if args.workload == "engine":
+        return run_engine
     if stream_is_tp(args, world):
         return run_tp
     return run_stream
@@ -1341,7 +1487,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the extra keys (the other configs measured after the line's own workload)")
-    ap.add_argument("--workload", default="stream", choices=["stream", "gemv", "prefill"] + list(GEMM_WORKLOADS),
+    ap.add_argument("--workload", default="stream", choices=["stream", "gemv", "prefill", "engine"] + list(GEMM_WORKLOADS),
                     help="stream: configs[1] decode weight stream (default); gemv: configs[0] single GEMV; "
                          "gemm_i4 / gemm_i4_down: configs[2] W4A16 prefill GEMM; w8a8 / w4a8: configs[3]; "
                          "prefill: configs[4]'s M=8192 prefill split over the GPUs")

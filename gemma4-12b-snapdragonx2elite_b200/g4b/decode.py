@@ -122,3 +122,83 @@ class FusedDecodeToken:
 
     def close(self) -> None:
         self.chain.close()
+
+
+def layer_segments(layers, norms: List[LayerNorms], lm_head, final_w, bufs: dict, eps: float = EPS):
+    """The same token split at every layer's attention, for an engine that runs
+    attention itself: segment 0 is layer 0's q|k|v; segment l + 1 starts with
+    layer l's o on bufs["attn"] (the attention output, written between the
+    segments) and runs gate|up, down and then layer l + 1's q|k|v -- or, after
+    the last layer, lm_head.  Returns ([(steps, xforms)], final residual name)."""
+    segs = []
+    cur = "h0"
+
+    def nxt(name):
+        return "hB" if name == "hA" else "hA"
+
+    L0, n0 = layers[0], norms[0]
+    segs.append(([(None, [L0.q, L0.k, L0.v], [bufs["q"], bufs["k"], bufs["v"]])],
+                 [{"kind": "rmsnorm", "a": bufs["h0"], "w": n0.inw, "eps": eps}]))
+    for li, (Ly, nm) in enumerate(zip(layers, norms)):
+        steps, xf = [(bufs["attn"], [Ly.o], [bufs["o"]])], [None]
+        out = nxt(cur)
+        steps.append((None, [Ly.gate, Ly.up], [bufs["gate"], bufs["up"]]))
+        xf.append({"kind": "normadd", "a": bufs["o"], "b": bufs[cur], "w_post": nm.paw, "w": nm.pfw,
+                   "h_out": bufs[out], "scale": 1.0, "eps": eps})
+        cur = out
+        steps.append((None, [Ly.down], [bufs["down"]]))
+        xf.append({"kind": "gelu_mul", "a": bufs["gate"], "b": bufs["up"]})
+        out = nxt(cur)
+        if li + 1 < len(layers):
+            Ln, nn = layers[li + 1], norms[li + 1]
+            steps.append((None, [Ln.q, Ln.k, Ln.v], [bufs["q"], bufs["k"], bufs["v"]]))
+            xf.append({"kind": "normadd", "a": bufs["down"], "b": bufs[cur], "w_post": nm.ofw, "w": nn.inw,
+                       "h_out": bufs[out], "scale": nm.scl, "eps": eps})
+        else:
+            steps.append((None, [lm_head], [bufs["logits"]]))
+            xf.append({"kind": "normadd", "a": bufs["down"], "b": bufs[cur], "w_post": nm.ofw, "w": final_w,
+                       "h_out": bufs[out], "scale": nm.scl, "eps": eps})
+        cur = out
+        segs.append((steps, xf))
+    return segs, cur
+
+
+class SegmentedDecodeToken:
+    """A token as one fused chain launch per layer, split at attention.
+
+    run(stream, attention) launches segment 0, then for every layer calls
+    attention(layer, stream) -- which must read bufs "q", "k", "v" and write
+    bufs["attn"] ([q width], the chain's dtype) on that stream -- and launches
+    the next segment.  Buffers as FusedDecodeToken's, plus "attn"."""
+
+    def __init__(self, layers, norms: List[LayerNorms], lm_head, final_w: torch.Tensor,
+                 dtype: torch.dtype = torch.float16, eps: float = EPS, device: Optional[torch.device] = None):
+        dev = device or lm_head.wp.device
+        H = layers[0].q.K
+        L0 = layers[0]
+        z = lambda n, dt: torch.zeros(n, dtype=dt, device=dev)  # noqa: E731
+        self.bufs = {"h0": z(H, torch.float32), "hA": z(H, torch.float32), "hB": z(H, torch.float32),
+                     "q": z(L0.q.N, dtype), "k": z(L0.k.N, dtype), "v": z(L0.v.N, dtype),
+                     "attn": z(L0.o.K, dtype), "o": z(L0.o.N, dtype), "gate": z(L0.gate.N, dtype),
+                     "up": z(L0.up.N, dtype), "down": z(L0.down.N, dtype), "logits": z(lm_head.N, dtype)}
+        segs, self._hname = layer_segments(layers, norms, lm_head, final_w, self.bufs, eps)
+        self._keep = (layers, norms, lm_head, final_w)
+        self.chains = [ops.GemvChain(st, xforms=xf, x_dtype=dtype, device=dev) for st, xf in segs]
+
+    @property
+    def h0(self) -> torch.Tensor:
+        return self.bufs["h0"]
+
+    @property
+    def logits(self) -> torch.Tensor:
+        return self.bufs["logits"]
+
+    def run(self, stream: Optional[torch.cuda.Stream], attention) -> None:
+        self.chains[0].run(stream)
+        for li, ch in enumerate(self.chains[1:]):
+            attention(li, stream)
+            ch.run(stream)
+
+    def close(self) -> None:
+        for ch in self.chains:
+            ch.close()

@@ -43,3 +43,27 @@ def test_token_plan_layout():
     for p, n in zip(adds, adds[1:]):
         assert n["b"] == p["h_out"] and n["h_out"] != n["b"]
     assert all(f["h_out"] in ("hA", "hB") for f in adds) and final == adds[-1]["h_out"]
+
+
+def test_layer_segments_split_at_attention():
+    """layer_segments: segment 0 = layer 0's q|k|v; segment l+1 = o on the
+    attention buffer, gate|up, down, then the next layer's q|k|v (lm_head after
+    the last layer); the element-wise work matches token_plan's."""
+    layers = [_layer(i) for i in range(3)]
+    norms = [decode.LayerNorms(inw=f"inw{i}", paw=f"paw{i}", pfw=f"pfw{i}", ofw=f"ofw{i}", scl=0.5 + i)
+             for i in range(3)]
+    bufs = {k: k for k in ("h0", "hA", "hB", "q", "k", "v", "attn", "o", "gate", "up", "down", "logits")}
+    segs, final = decode.layer_segments(layers, norms, W("lm", 8, 8), "finw", bufs)
+    assert len(segs) == 4
+    assert [w.name for w in segs[0][0][0][1]] == ["q0", "k0", "v0"] and segs[0][1][0]["a"] == "h0"
+    for li in range(3):
+        steps, xf = segs[li + 1]
+        assert steps[0][0] == "attn" and steps[0][1][0].name == f"o{li}" and xf[0] is None
+        assert [st[1][0].name for st in steps[1:]] == [f"gate{li}", f"down{li}", f"q{li + 1}" if li < 2 else "lm"]
+        assert [f["kind"] for f in xf[1:]] == ["normadd", "gelu_mul", "normadd"]
+    # the flat plan and the split plan do the same element-wise work in the same order
+    tsteps, txf, tfinal = decode.token_plan(layers, norms, W("lm", 8, 8), "finw", bufs)
+    flat = [f for _, xf in segs for f in xf]
+    assert [None if f is None else (f["kind"], f.get("w"), f.get("w_post"), f.get("b"), f.get("h_out")) for f in flat] == \
+        [None if f is None else (f["kind"], f.get("w"), f.get("w_post"), f.get("b"), f.get("h_out")) for f in txf]
+    assert final == tfinal
