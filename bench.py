@@ -255,7 +255,7 @@ def describe(args, world: int) -> dict:
                 "config": {"workload": text, "M": M, "N": N, "K": K, "parallelism": f"replicas{world}",
                            "l2": "256 MB buffer written between timed iterations (L2 flush, outside the events)"}}
     if wl == "engine":
-        return {"metric": "decode tok/s at context 16 (engine harness, attention stand-in)", "unit": "tok/s",
+        return {"metric": "decode tok/s at context 16 (engine harness)", "unit": "tok/s",
                 "scaling": "weak",
                 "config": {"workload": "benchmarks/bench_engine.py's measurements on the configs[1] stack",
                            "layers": args.layers, "parallelism": f"replicas{world}"}}
@@ -1207,16 +1207,15 @@ def measure_engine(c, args):
     """benchmarks/bench_engine.py:14-41 on this stack: decode tok/s at a context
     of 16, 1024 and 4096 tokens, and prefill prompt-tok/s on a 2048-token prompt.
 
-    The 48 layers' matmuls and the decode layer's element-wise work are g4b's:
-    a decode token is one fused chain launch per layer, split at attention
-    (g4b.decode.SegmentedDecodeToken); prefill runs the W4A16 GEMMs (and, as
-    PREFILL_I8 does, cast_i8 + the W8A8 GEMMs).  Attention and, in prefill, the
-    norms and gelu*up over [T, H] rows are stand-ins outside this path: torch's
-    scaled_dot_product_attention over a synthetic f16 KV cache (GQA, 16 query
-    and 8 KV heads of 256) and torch element-wise ops.  Decode is timed as K
-    graph replays at a fixed context (the reference grows it by 64 tokens);
-    prefill is one pass over the prompt in one batch, the logits for its last
-    token."""
+    Decode is all g4b: per layer one fused chain launch (the GEMVs with the
+    norms and gelu*up, g4b.decode.SegmentedDecodeToken) and the KV-cache write
+    and flash-decode attention (g4b_attn_prepkv, g4b_attn_decode) over a
+    synthetic f16 cache (GQA, 16 query and 8 KV heads of 256), timed as K
+    graph replays at a fixed context (the reference grows it by 64 tokens).
+    Prefill runs the W4A16 GEMMs (and, as PREFILL_I8 does, cast_i8 + the W8A8
+    GEMMs) over the 2048-token prompt in one batch; its attention and its norms
+    and gelu*up over [T, H] rows are torch stand-ins (prefill attention,
+    vk/pre_attn.comp, is not built here).  The logits are for the last token."""
     torch = c.torch
     F = torch.nn.functional
     from g4b import decode
@@ -1239,29 +1238,38 @@ def measure_engine(c, args):
     nw = lambda: (1.0 + 0.1 * torch.randn((H,), generator=gen, device=c.device))  # noqa: E731
     norms = [decode.LayerNorms(inw=nw(), paw=nw(), pfw=nw(), ofw=nw(), scl=1.0) for _ in range(args.layers)]
     finw = nw()
-    out = {"attention": "stand-in: torch scaled_dot_product_attention (GQA 16/8 heads of 256) over an f16 KV cache",
+    out = {"attention": "decode: g4b_attn_prepkv + g4b_attn_decode (GQA 16/8 heads of 256, f16 KV cache); "
+                        "prefill: torch scaled_dot_product_attention stand-in",
            "steps": args.steps}
     # ---- decode
     tok = decode.SegmentedDecodeToken(layers_d, norms, lm, finw, dtype=torch.float16)
     tok.h0.copy_(torch.randn((H,), generator=gen, device=c.device))
+    hn = lambda: (1.0 + 0.1 * torch.randn((HEAD_DIM,), generator=gen, device=c.device))  # noqa: E731
+    qnw, knw = [hn() for _ in range(args.layers)], [hn() for _ in range(args.layers)]
     for ctx in ENGINE_CTX:
-        kc = torch.randn((args.layers, 1, NKV_HEADS, ctx, HEAD_DIM), generator=gen, device=c.device).half()
-        vc = torch.randn((args.layers, 1, NKV_HEADS, ctx, HEAD_DIM), generator=gen, device=c.device).half()
+        kc = torch.randn((args.layers, NKV_HEADS, ctx, HEAD_DIM), generator=gen, device=c.device).half()
+        vc = torch.randn((args.layers, NKV_HEADS, ctx, HEAD_DIM), generator=gen, device=c.device).half()
+        pos = torch.tensor([ctx - 1], dtype=torch.int32, device=c.device)
+        ang = (ctx - 1) / 10000.0 ** (torch.arange(0, HEAD_DIM, 2, device=c.device, dtype=torch.float64) / HEAD_DIM)
+        cos_t, sin_t = torch.cat([ang, ang]).cos().float(), torch.cat([ang, ang]).sin().float()
+        aws = torch.zeros(c.ops.attn_workspace_bytes(NH, NKV_HEADS, HEAD_DIM, ctx) + 256, dtype=torch.uint8,
+                          device=c.device)
 
-        def attention(li, stream, kc=kc, vc=vc, ctx=ctx):
+        def attention(li, stream, kc=kc, vc=vc, pos=pos, cos_t=cos_t, sin_t=sin_t, aws=aws):
             b = tok.bufs
-            kc[li, 0, :, ctx - 1].copy_(b["k"].view(NKV_HEADS, HEAD_DIM))   # this token's k, v in the cache
-            vc[li, 0, :, ctx - 1].copy_(b["v"].view(NKV_HEADS, HEAD_DIM))
-            o = F.scaled_dot_product_attention(b["q"].view(1, NH, 1, HEAD_DIM), kc[li], vc[li], enable_gqa=True)
-            b["attn"].copy_(o.view(-1))
+            c.ops.attn_prepkv(b["qkv"], knw[li], cos_t, sin_t, kc[li], vc[li], pos, NKV_HEADS, HEAD_DIM, NQ,
+                              NQ + NKV_HEADS * HEAD_DIM, stream=stream)
+            c.ops.attn_decode(b["qkv"], qnw[li], cos_t, sin_t, kc[li], vc[li], pos, NH, NKV_HEADS, HEAD_DIM,
+                              out=b["attn"], stream=stream, workspace=aws)
 
         graph = capture(c, lambda: tok.run(c.stream, attention), args.warmup)
         ms = timed_graph(c, graph, args.steps) / args.steps
         out[f"decode tok/s @ctx {ctx}"] = round(1000.0 / ms, 1)
         out[f"decode ms/token @ctx {ctx}"] = round(ms, 4)
-        del graph, kc, vc
+        del graph, kc, vc, aws
         torch.cuda.empty_cache()
-    out["decode launches/token"] = f"{len(tok.chains)} chain launches + the attention stand-in's kernels"
+    out["decode launches/token"] = (f"{len(tok.chains)} chain launches + {args.layers} x (prepkv, attention, "
+                                    "split combine)")
     tok.close()
     # ---- prefill: one 2048-token prompt
     T = PROMPT_LEN

@@ -167,9 +167,10 @@ class SegmentedDecodeToken:
     """A token as one fused chain launch per layer, split at attention.
 
     run(stream, attention) launches segment 0, then for every layer calls
-    attention(layer, stream) -- which must read bufs "q", "k", "v" and write
-    bufs["attn"] ([q width], the chain's dtype) on that stream -- and launches
-    the next segment.  Buffers as FusedDecodeToken's, plus "attn"."""
+    attention(layer, stream) -- which must read bufs "qkv" (q, k and v one
+    after another) and write bufs["attn"] ([q width], the chain's dtype) on
+    that stream, e.g. g4b.ops.attn_prepkv + attn_decode -- and launches the
+    next segment.  Buffers as FusedDecodeToken's, plus "qkv" and "attn"."""
 
     def __init__(self, layers, norms: List[LayerNorms], lm_head, final_w: torch.Tensor,
                  dtype: torch.dtype = torch.float16, eps: float = EPS, device: Optional[torch.device] = None):
@@ -177,8 +178,11 @@ class SegmentedDecodeToken:
         H = layers[0].q.K
         L0 = layers[0]
         z = lambda n, dt: torch.zeros(n, dtype=dt, device=dev)  # noqa: E731
+        # q, k and v are views of one q|k|v buffer, as the engine's B["qkv"] (src/vk_engine.py:180): the
+        # KV-cache write and the attention read k and v at offsets into it
+        qkv = z(L0.q.N + L0.k.N + L0.v.N, dtype)
         self.bufs = {"h0": z(H, torch.float32), "hA": z(H, torch.float32), "hB": z(H, torch.float32),
-                     "q": z(L0.q.N, dtype), "k": z(L0.k.N, dtype), "v": z(L0.v.N, dtype),
+                     "qkv": qkv, "q": qkv[:L0.q.N], "k": qkv[L0.q.N:L0.q.N + L0.k.N], "v": qkv[L0.q.N + L0.k.N:],
                      "attn": z(L0.o.K, dtype), "o": z(L0.o.N, dtype), "gate": z(L0.gate.N, dtype),
                      "up": z(L0.up.N, dtype), "down": z(L0.down.N, dtype), "logits": z(lm_head.N, dtype)}
         segs, self._hname = layer_segments(layers, norms, lm_head, final_w, self.bufs, eps)

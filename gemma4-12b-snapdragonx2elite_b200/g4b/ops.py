@@ -415,3 +415,45 @@ def stream_wait(stream: Optional[torch.cuda.Stream] = None, timeout_ms: int = 0)
     """Bounded wait for a stream (the engine's fence wait with a timeout)."""
     dev = torch.device("cuda", torch.cuda.current_device())
     L.check("g4b_stream_wait", L.load().g4b_stream_wait(_stream_handle(stream, dev), int(timeout_ms)))
+
+
+# ----------------------------------------------------------------- decode attention
+def attn_workspace_bytes(nH: int, nkv: int, hd: int, max_T: int) -> int:
+    return int(L.load().g4b_attn_workspace_bytes(nH, nkv, hd, max_T))
+
+
+def attn_prepkv(qkv: torch.Tensor, knw: torch.Tensor, cos_t: torch.Tensor, sin_t: torch.Tensor, kc: torch.Tensor,
+                vc: torch.Tensor, pos: torch.Tensor, nkv: int, hd: int, koff: int, voff: int, keqv: bool = False,
+                window: int = 0, stream: Optional[torch.cuda.Stream] = None) -> None:
+    """vk/prepkv.comp: this token's normed, rotated k and normed v into the f16 caches
+    kc / vc [nkv, stride, hd] at slot pos (pos % window for a sliding ring).
+    pos is a one-element int32 device tensor."""
+    for t, n in ((qkv, "qkv"), (knw, "knw"), (cos_t, "cos"), (sin_t, "sin"), (kc, "kc"), (vc, "vc"), (pos, "pos")):
+        _need(t, n)
+    stride = kc.shape[1]
+    sh = _stream_handle(stream, qkv.device)
+    L.check("g4b_attn_prepkv", L.load().g4b_attn_prepkv(
+        _ptr(qkv), _DT[qkv.dtype], _ptr(knw), _ptr(cos_t), _ptr(sin_t), _ptr(kc), _ptr(vc), nkv, hd, koff, voff,
+        1 if keqv else 0, stride, window, _ptr(pos), sh))
+
+
+def attn_decode(qkv: torch.Tensor, qnw: torch.Tensor, cos_t: torch.Tensor, sin_t: torch.Tensor, kc: torch.Tensor,
+                vc: torch.Tensor, pos: torch.Tensor, nH: int, nkv: int, hd: int, qoff: int = 0, window: int = 0,
+                out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float32,
+                stream: Optional[torch.cuda.Stream] = None, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """vk/attn.comp: one token's attention over the cached keys (flash decoding)."""
+    for t, n in ((qkv, "qkv"), (qnw, "qnw"), (cos_t, "cos"), (sin_t, "sin"), (kc, "kc"), (vc, "vc"), (pos, "pos")):
+        _need(t, n)
+    stride = kc.shape[1]
+    if out is None:
+        out = torch.empty((nH * hd,), dtype=out_dtype, device=qkv.device)
+    sh = _stream_handle(stream, qkv.device)
+    need = attn_workspace_bytes(nH, nkv, hd, window if window > 0 else stride)
+    ws = workspace
+    if need and ws is None:
+        ws = WORKSPACES.get(qkv.device, sh, need, use="attn")
+    L.check("g4b_attn_decode", L.load().g4b_attn_decode(
+        _ptr(qkv), _DT[qkv.dtype], _ptr(qnw), _ptr(cos_t), _ptr(sin_t), _ptr(kc), _ptr(vc), _ptr(out),
+        _DT[out.dtype], nH, nkv, hd, qoff, stride, window, _ptr(pos), _ptr(ws), ws.numel() if ws is not None else 0,
+        sh))
+    return out

@@ -380,6 +380,36 @@ G4B_API int g4b_gemm_w4a8(const int8_t* A8, const uint32_t* wp, const uint16_t* 
                           const uint16_t* sw_f16, void* Y, int y_dtype, int32_t* C_debug,
                           int M, int N, int K, g4b_stream_t stream);
 
+/* ------------------------------------------------------------ decode attention */
+/* KV-cache write for one decode token, vk/prepkv.comp:14-31 (the prepkv dispatch
+ * forward() records per layer, src/vk_engine.py:281): for every KV head h,
+ *   k = RoPE(rmsnorm(qkv[koff + h*hd ..], knw))   with the token's rotation (cos_t, sin_t: [hd] f32),
+ *   v = qkv[voff + h*hd ..] * rsqrt(mean(v^2) + 1e-6)          (keqv: v is read at koff instead)
+ *   kc / vc [(h*stride + slot)*hd + i] = f16(k[i] / v[i]),  slot = window ? pos % window : pos
+ * (sliding layers keep a ring of `window` slots).  qkv is the q|k|v output (f32 or f16); knw is f32;
+ * pos is read from device memory (*pos_dev), so one captured graph serves every token.
+ * hd 128, 256 or 512; window <= stride. */
+G4B_API int g4b_attn_prepkv(const void* qkv, int dtype, const float* knw, const float* cos_t, const float* sin_t,
+                            uint16_t* kc, uint16_t* vc, int nkv, int hd, int koff, int voff, int keqv, int stride,
+                            int window, const int* pos_dev, g4b_stream_t stream);
+
+/* Workspace bytes g4b_attn_decode needs for a cache of max_T keys (window, or stride for
+ * full-attention layers); 0 when the keys are not split. */
+G4B_API size_t g4b_attn_workspace_bytes(int nH, int nkv, int hd, int max_T);
+
+/* Decode attention for one token, vk/attn.comp:15-55 (the attn dispatch, src/vk_engine.py:282):
+ * for every query head h (KV head h / (nH / nkv)),
+ *   q = RoPE(rmsnorm(qkv[qoff + h*hd ..], qnw)),  T = window ? min(pos + 1, window) : pos + 1,
+ *   out[h*hd + i] = sum_{j < T} softmax_j(q . k_j) v_j[i]            (no 1/sqrt(hd) scale, as the shader)
+ * over the cached keys (slots 0 .. T-1).  The keys are split over the SMs (flash decoding): a
+ * split's softmax partial goes to `workspace` and a second kernel combines the splits.
+ * Shapes: hd 128 (up to 8 query heads per KV head), 256 (up to 4) or 512 (up to 2).
+ * out [nH, hd] f32 or f16. */
+G4B_API int g4b_attn_decode(const void* qkv, int dtype, const float* qnw, const float* cos_t, const float* sin_t,
+                            const uint16_t* kc, const uint16_t* vc, void* out, int out_dtype, int nH, int nkv,
+                            int hd, int qoff, int stride, int window, const int* pos_dev, void* workspace,
+                            size_t ws_bytes, g4b_stream_t stream);
+
 /* ------------------------------------------------------------ tensor parallel */
 /* The all-reduce after the row-parallel o and down GEMVs of a tensor-parallel
  * decode -- the cross-GPU counterpart of vk/reduce.comp:8-12 (the reference

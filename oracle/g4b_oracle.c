@@ -26,6 +26,8 @@
  *   orc_rmsnorm         vk/rmsnorm.comp:8-12
  *   orc_normadd         vk/normadd.comp:8-12
  *   orc_gelumul         vk/gelumul.comp:7-8
+ *   orc_attn_prepkv     vk/prepkv.comp:14-31
+ *   orc_attn_decode     vk/attn.comp:15-55
  *
  * Choices the GLSL leaves to the implementation, fixed here and stated once:
  *   - round(): round-half-to-even (roundEven), the same as numpy's np.round used
@@ -450,6 +452,86 @@ void orc_gelumul(const float* gate, const float* up, float* out, int n) {
         const float x = gate[i];
         const float g = 0.5f * x * (1.0f + tanhf(0.7978845608028654f * (x + 0.044715f * x * x * x)));
         out[i] = g * up[i];
+    }
+}
+
+/* vk/prepkv.comp:14-31: every KV head's k (rmsnorm with knw, then RoPE) and v (rmsnorm without a weight)
+ * into the f16 caches [nkv][stride][hd] at slot pos (pos % window for a sliding ring); keqv reads v at koff. */
+void orc_attn_prepkv(const float* qkv, const float* knw, const float* cosb, const float* sinb, uint16_t* kc,
+                     uint16_t* vc, int nkv, int hd, int koff, int voff, int keqv, int stride, int window, int pos) {
+    const int hf = hd / 2, slot = window > 0 ? pos % window : pos;
+    float hv[512];
+    for (int h = 0; h < nkv; h++) {
+        for (int i = 0; i < hd; i++) hv[i] = qkv[koff + h * hd + i];
+        const float ik = 1.0f / sqrtf(orc_sumsq_256(hv, hd) / (float)hd + 1e-6f);
+        for (int i = 0; i < hd; i++) hv[i] = hv[i] * ik * knw[i];
+        for (int i = 0; i < hd; i++) {
+            const float rh = i < hf ? -hv[i + hf] : hv[i - hf];
+            kc[((size_t)h * stride + slot) * hd + i] = orc_f32_to_f16(hv[i] * cosb[i] + rh * sinb[i]);
+        }
+        const int vo = keqv ? koff : voff;
+        for (int i = 0; i < hd; i++) hv[i] = qkv[vo + h * hd + i];
+        const float iv = 1.0f / sqrtf(orc_sumsq_256(hv, hd) / (float)hd + 1e-6f);
+        for (int i = 0; i < hd; i++) vc[((size_t)h * stride + slot) * hd + i] = orc_f32_to_f16(hv[i] * iv);
+    }
+}
+
+/* vk/attn.comp:15-55: per query head, q = RoPE(rmsnorm(q, qnw)), then the online softmax over the keys
+ * in tiles of 256 (tile max and sum by the shader's 256-lane tree), acc = acc * corr + sum_j p_j v_j in
+ * key order, out = acc / l.  No 1/sqrt(hd) scale. */
+void orc_attn_decode(const float* qkv, const float* qnw, const float* cosb, const float* sinb, const uint16_t* kc,
+                     const uint16_t* vc, float* out, int nH, int nkv, int hd, int qoff, int stride, int window,
+                     int pos) {
+    const int grp = nH / nkv, hf = hd / 2;
+    const int T = window > 0 ? (pos + 1 < window ? pos + 1 : window) : pos + 1;
+#pragma omp parallel for schedule(static)
+    for (int h = 0; h < nH; h++) {
+        const int kvh = h / grp;
+        float qr[512], acc[512], sc[256], red[256];
+        for (int i = 0; i < hd; i++) qr[i] = qkv[qoff + h * hd + i];
+        const float iq = 1.0f / sqrtf(orc_sumsq_256(qr, hd) / (float)hd + 1e-6f);
+        for (int i = 0; i < hd; i++) qr[i] = qr[i] * iq * qnw[i];
+        for (int i = 0; i < hd; i++) {
+            const float rh = i < hf ? -qr[i + hf] : qr[i - hf];
+            acc[i] = qr[i] * cosb[i] + rh * sinb[i];
+        }
+        for (int i = 0; i < hd; i++) {
+            qr[i] = acc[i];
+            acc[i] = 0.0f;
+        }
+        float msh = -1e30f, lsh = 0.0f;
+        for (int tile = 0; tile < T; tile += 256) {
+            const int tlen = T - tile < 256 ? T - tile : 256;
+            for (int j = 0; j < tlen; j++) {
+                const uint16_t* k = kc + ((size_t)kvh * stride + tile + j) * hd;
+                float d2 = 0.0f;
+                for (int i = 0; i < hd; i += 4)
+                    d2 += qr[i] * orc_f16_to_f32(k[i]) + qr[i + 1] * orc_f16_to_f32(k[i + 1]) +
+                          qr[i + 2] * orc_f16_to_f32(k[i + 2]) + qr[i + 3] * orc_f16_to_f32(k[i + 3]);
+                sc[j] = d2;
+            }
+            float mx = -1e30f;
+            for (int j = 0; j < tlen; j++) mx = sc[j] > mx ? sc[j] : mx;
+            const float mn = msh > mx ? msh : mx;
+            const float corr = expf(msh - mn);
+            msh = mn;
+            for (int t = 0; t < 256; t++) {
+                red[t] = 0.0f;
+                if (t < tlen) {
+                    sc[t] = expf(sc[t] - mn);
+                    red[t] = sc[t];
+                }
+            }
+            for (int st = 128; st > 0; st >>= 1)
+                for (int t = 0; t < st; t++) red[t] += red[t + st];
+            lsh = lsh * corr + red[0];
+            for (int i = 0; i < hd; i++) {
+                float a = acc[i] * corr;
+                for (int j = 0; j < tlen; j++) a += sc[j] * orc_f16_to_f32(vc[((size_t)kvh * stride + tile + j) * hd + i]);
+                acc[i] = a;
+            }
+        }
+        for (int i = 0; i < hd; i++) out[h * hd + i] = acc[i] / lsh;
     }
 }
 

@@ -18,6 +18,7 @@ __all__ = [
     "quant_i4", "fp8_scales", "split_for", "w8a8_weights", "w4a8_ratio", "gemv", "reduce",
     "dequant", "gemm_i4", "cast_i8", "gemm_w8a8", "w4a8_requant", "gemm_w4a8",
     "num_threads", "set_num_threads", "pack_reference", "rmsnorm", "normadd", "gelumul", "decode_token",
+    "attn_prepkv", "attn_decode",
 ]
 
 
@@ -58,6 +59,8 @@ def lib():
         L.orc_rmsnorm.argtypes = [P, P, P, i, f]
         L.orc_normadd.argtypes = [P, P, P, i, f, f]
         L.orc_gelumul.argtypes = [P, P, P, i]
+        L.orc_attn_prepkv.argtypes = [P, P, P, P, P, P, i, i, i, i, i, i, i, i]
+        L.orc_attn_decode.argtypes = [P, P, P, P, P, P, P, i, i, i, i, i, i, i]
         L.orc_num_threads.restype = i
         L.orc_set_num_threads.argtypes = [i]
         _lib = L
@@ -305,3 +308,23 @@ def decode_token(h0, layers, lm_head, final_w, gemv_fn, round_x=None, round_y=No
         outs.append({"q": q, "k": k, "v": v, "o": o, "gate": gate, "up": up, "down": down})
     logits = ry(gemv_fn(rx(rmsnorm(h, final_w, eps)), lm_head))
     return logits, h, outs
+
+
+# ---------------------------------------------------------------- decode attention
+def attn_prepkv(qkv, knw, cos_t, sin_t, kc, vc, nkv: int, hd: int, koff: int, voff: int, keqv: bool,
+                window: int, pos: int):
+    """vk/prepkv.comp:14-31 on host arrays: writes slot pos (pos % window) of kc / vc
+    ([nkv, stride, hd] uint16 f16 bits) in place."""
+    qkv = _c(qkv, np.float32)
+    assert kc.dtype == np.uint16 and vc.dtype == np.uint16 and kc.flags.c_contiguous and vc.flags.c_contiguous
+    lib().orc_attn_prepkv(_p(qkv), _p(_c(knw, np.float32)), _p(_c(cos_t, np.float32)), _p(_c(sin_t, np.float32)),
+                          _p(kc), _p(vc), nkv, hd, koff, voff, 1 if keqv else 0, kc.shape[1], window, pos)
+
+
+def attn_decode(qkv, qnw, cos_t, sin_t, kc, vc, nH: int, nkv: int, hd: int, qoff: int, window: int, pos: int):
+    """vk/attn.comp:15-55 on host arrays: the [nH * hd] f32 attention output."""
+    out = np.empty((nH * hd,), np.float32)
+    lib().orc_attn_decode(_p(_c(qkv, np.float32)), _p(_c(qnw, np.float32)), _p(_c(cos_t, np.float32)),
+                          _p(_c(sin_t, np.float32)), _p(_c(kc, np.uint16)), _p(_c(vc, np.uint16)), _p(out), nH, nkv,
+                          hd, qoff, kc.shape[1], window, pos)
+    return out
