@@ -64,10 +64,10 @@ LAYER_SHAPES = [("q", NQ, HIDDEN), ("k", NKV, HIDDEN), ("v", NKV, HIDDEN), ("o",
                 ("gate", FFN, HIDDEN), ("up", FFN, HIDDEN), ("down", HIDDEN, FFN)]
 LM_HEAD = ("lm_head", VOCAB, HIDDEN)
 STREAM_METRIC = "int4 GEMV HBM GB/s (decode weight stream, 48 layers + lm_head, batch 1)"
-# tensor-parallel stream defaults: one chain launch per token with the all-reduces inside it where that has been
-# run on a B200 box; other worlds default to per-GEMV launches with NCCL's all-reduce (--schedule chain selects
-# the chain there too)
-TP_CHAIN_CONFIRMED_WORLDS = (2,)
+# tensor-parallel stream defaults: one chain launch per token with the all-reduces inside it on the worlds whose
+# in-chain all-reduce has passed its parity test on B200s (tests/test_gpu_tp.py at 2, 4 and 8 ranks); any other
+# world defaults to per-GEMV launches with NCCL's all-reduce (--schedule chain selects the chain there too)
+TP_CHAIN_CONFIRMED_WORLDS = (2, 4, 8)
 TP_DEFAULT_ALLREDUCE = "nccl"
 # prefill GEMMs: name -> (M, N, K, kind, the BASELINE.json config it is quoted on)
 GEMM_WORKLOADS = {
