@@ -457,3 +457,41 @@ def attn_decode(qkv: torch.Tensor, qnw: torch.Tensor, cos_t: torch.Tensor, sin_t
         _DT[out.dtype], nH, nkv, hd, qoff, stride, window, _ptr(pos), _ptr(ws), ws.numel() if ws is not None else 0,
         sh))
     return out
+
+
+def attn_prefill_prepkv(k: torch.Tensor, v: torch.Tensor, knw: torch.Tensor, cosM: torch.Tensor, sinM: torch.Tensor,
+                        kc: torch.Tensor, vc: torch.Tensor, p0: torch.Tensor, nkv: int, hd: int, window: int = 0,
+                        stream: Optional[torch.cuda.Stream] = None) -> None:
+    """vk/pre_prepkv.comp: a chunk's k / v rows ([M, row] views, head h at h * hd; v may be k) into the
+    f16 caches at slots p0 .. p0 + M - 1 (% window); cosM / sinM [M, hd] are the tokens' rotations.
+    p0 is a one-element int32 device tensor."""
+    for t, n in ((knw, "knw"), (cosM, "cosM"), (sinM, "sinM"), (kc, "kc"), (vc, "vc"), (p0, "p0")):
+        _need(t, n)
+    if k.dim() != 2 or k.shape != v.shape or k.stride(1) != 1 or v.stride(0) != k.stride(0) or k.dtype != v.dtype:
+        raise ValueError("attn_prefill_prepkv: k and v must be [M, row] views with the same row stride and dtype")
+    sh = _stream_handle(stream, k.device)
+    L.check("g4b_attn_prefill_prepkv", L.load().g4b_attn_prefill_prepkv(
+        _ptr(k), _ptr(v), _DT[k.dtype], k.stride(0), k.shape[0], _ptr(knw), _ptr(cosM), _ptr(sinM), _ptr(kc),
+        _ptr(vc), nkv, hd, kc.shape[1], window, _ptr(p0), sh))
+
+
+def attn_prefill(q: torch.Tensor, qnw: torch.Tensor, cosM: torch.Tensor, sinM: torch.Tensor, kc: torch.Tensor,
+                 vc: torch.Tensor, p0: torch.Tensor, nH: int, nkv: int, hd: int, window: int = 0,
+                 out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float32,
+                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """vk/pre_attn.comp: causal attention of a chunk's queries q [M, row] (head h at h * hd) over the
+    cache; returns out [M, nH * hd] (or writes the given [M, row] view)."""
+    for t, n in ((qnw, "qnw"), (cosM, "cosM"), (sinM, "sinM"), (kc, "kc"), (vc, "vc"), (p0, "p0")):
+        _need(t, n)
+    if q.dim() != 2 or q.stride(1) != 1:
+        raise ValueError("attn_prefill: q must be an [M, row] view")
+    M = q.shape[0]
+    if out is None:
+        out = torch.empty((M, nH * hd), dtype=out_dtype, device=q.device)
+    if out.dim() != 2 or out.stride(1) != 1 or out.shape[0] != M:
+        raise ValueError("attn_prefill: out must be an [M, row] view")
+    sh = _stream_handle(stream, q.device)
+    L.check("g4b_attn_prefill", L.load().g4b_attn_prefill(
+        _ptr(q), _DT[q.dtype], q.stride(0), M, _ptr(qnw), _ptr(cosM), _ptr(sinM), _ptr(kc), _ptr(vc), _ptr(out),
+        _DT[out.dtype], out.stride(0), nH, nkv, hd, kc.shape[1], window, _ptr(p0), sh))
+    return out

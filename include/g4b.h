@@ -380,7 +380,7 @@ G4B_API int g4b_gemm_w4a8(const int8_t* A8, const uint32_t* wp, const uint16_t* 
                           const uint16_t* sw_f16, void* Y, int y_dtype, int32_t* C_debug,
                           int M, int N, int K, g4b_stream_t stream);
 
-/* ------------------------------------------------------------ decode attention */
+/* ------------------------------------------------------------ attention */
 /* KV-cache write for one decode token, vk/prepkv.comp:14-31 (the prepkv dispatch
  * forward() records per layer, src/vk_engine.py:281): for every KV head h,
  *   k = RoPE(rmsnorm(qkv[koff + h*hd ..], knw))   with the token's rotation (cos_t, sin_t: [hd] f32),
@@ -409,6 +409,32 @@ G4B_API int g4b_attn_decode(const void* qkv, int dtype, const float* qnw, const 
                             const uint16_t* kc, const uint16_t* vc, void* out, int out_dtype, int nH, int nkv,
                             int hd, int qoff, int stride, int window, const int* pos_dev, void* workspace,
                             size_t ws_bytes, g4b_stream_t stream);
+
+/* KV-cache write for a prefill chunk, vk/pre_prepkv.comp:15-30 (src/vk_engine.py:416): token m of
+ * M (position *p0_dev + m) writes what g4b_attn_prepkv writes for one token, from its own rows
+ * k + m*row_stride, v + m*row_stride (element offsets; head h at h*hd; k == v for attention_k_eq_v)
+ * and its own rotation rows cosM / sinM [M, hd] f32.  On a sliding ring a chunk longer than the
+ * window writes a slot more than once: the latest token's k / v stay.  Slots past the cache
+ * (pos >= stride on a full-attention layer) are not written.  hd 128, 256 or 512. */
+G4B_API int g4b_attn_prefill_prepkv(const void* k, const void* v, int dtype, int row_stride, int M,
+                                    const float* knw, const float* cosM, const float* sinM, uint16_t* kc,
+                                    uint16_t* vc, int nkv, int hd, int stride, int window, const int* p0_dev,
+                                    g4b_stream_t stream);
+
+/* Causal attention for a prefill chunk, vk/pre_attn.comp:16-53 (src/vk_engine.py:417): for token m
+ * (position pos = *p0_dev + m) and query head h,
+ *   q = RoPE(rmsnorm(q[m*q_stride + h*hd ..], qnw), cosM[m], sinM[m]),
+ *   T = window ? min(pos + 1, window) : pos + 1,
+ *   out[m*out_stride + h*hd + i] = sum_j softmax_j(q . k_j) v_j[i]  over the slots j < T, leaving out,
+ *   on a sliding ring, the slots whose position (base - ((base + window - j) % window), base =
+ *   *p0_dev + M - 1: the chunk's keys are all written first) is after pos.
+ * Tensor cores (mma.sync, f32 accumulate) with q and the softmax weights as f16 hi + lo pairs.
+ * q f32 or f16; out f32 or f16; q_stride, out_stride multiples of 8 (>= nH*hd); hd 128, 256 or 512;
+ * nH a multiple of nkv; q, kc, vc, out 16-byte aligned. */
+G4B_API int g4b_attn_prefill(const void* q, int dtype, int q_stride, int M, const float* qnw, const float* cosM,
+                             const float* sinM, const uint16_t* kc, const uint16_t* vc, void* out, int out_dtype,
+                             int out_stride, int nH, int nkv, int hd, int stride, int window, const int* p0_dev,
+                             g4b_stream_t stream);
 
 /* ------------------------------------------------------------ tensor parallel */
 /* The all-reduce after the row-parallel o and down GEMVs of a tensor-parallel

@@ -28,6 +28,8 @@
  *   orc_gelumul         vk/gelumul.comp:7-8
  *   orc_attn_prepkv     vk/prepkv.comp:14-31
  *   orc_attn_decode     vk/attn.comp:15-55
+ *   orc_attn_prefill_prepkv  vk/pre_prepkv.comp:15-30
+ *   orc_attn_prefill    vk/pre_attn.comp:16-53
  *
  * Choices the GLSL leaves to the implementation, fixed here and stated once:
  *   - round(): round-half-to-even (roundEven), the same as numpy's np.round used
@@ -533,6 +535,109 @@ void orc_attn_decode(const float* qkv, const float* qnw, const float* cosb, cons
         }
         for (int i = 0; i < hd; i++) out[h * hd + i] = acc[i] / lsh;
     }
+}
+
+/* vk/pre_prepkv.comp:15-30: token m of a chunk of M at absolute position p0 + m writes its normed,
+ * rotated k (row m of kin, at kvh * hd) and normed v into slot (p0 + m) (% window); cosM / sinM rows are
+ * the tokens' own angles ([M, hd]).  kin / vin rows are nk = row_stride floats apart. */
+void orc_attn_prefill_prepkv(const float* kin, const float* vin, const float* knw, const float* cosM,
+                             const float* sinM, uint16_t* kc, uint16_t* vc, int M, int nkv, int hd, int row_stride,
+                             int stride, int window, int p0) {
+    const int hf = hd / 2;
+    float hv[512];
+    for (int m = 0; m < M; m++) {
+        const int pos = p0 + m, slot = window > 0 ? pos % window : pos;
+        const float* cb = cosM + (size_t)m * hd;
+        const float* sb = sinM + (size_t)m * hd;
+        for (int h = 0; h < nkv; h++) {
+            const size_t kb = (size_t)m * row_stride + (size_t)h * hd;
+            for (int i = 0; i < hd; i++) hv[i] = kin[kb + i];
+            const float ik = 1.0f / sqrtf(orc_sumsq_256(hv, hd) / (float)hd + 1e-6f);
+            for (int i = 0; i < hd; i++) hv[i] = hv[i] * ik * knw[i];
+            for (int i = 0; i < hd; i++) {
+                const float rh = i < hf ? -hv[i + hf] : hv[i - hf];
+                kc[((size_t)h * stride + slot) * hd + i] = orc_f32_to_f16(hv[i] * cb[i] + rh * sb[i]);
+            }
+            for (int i = 0; i < hd; i++) hv[i] = vin[kb + i];
+            const float iv = 1.0f / sqrtf(orc_sumsq_256(hv, hd) / (float)hd + 1e-6f);
+            for (int i = 0; i < hd; i++) vc[((size_t)h * stride + slot) * hd + i] = orc_f32_to_f16(hv[i] * iv);
+        }
+    }
+}
+
+/* vk/pre_attn.comp:16-53: causal attention of token m (position pos = p0 + m) of a chunk of M, per
+ * query head: q = RoPE(rmsnorm(q[m], qnw), cosM[m], sinM[m]); T = pos + 1 (or min(pos + 1, window)); the
+ * keys are slots 0..T-1 in tiles of 256; on a sliding ring a slot's absolute position is
+ * base - ((base + window - slot) % window) with base = p0 + M - 1 (the chunk's keys are all written
+ * first), and keys after pos score -1e30.  The tile's max and sum follow the shader (strided lane sums,
+ * 256-lane tree); acc = acc * corr + sum_j p_j v_j in key order; out = acc / l.  q / out rows are
+ * row_stride floats apart; head h starts at h * hd. */
+void orc_attn_prefill(const float* q, const float* qnw, const float* cosM, const float* sinM, const uint16_t* kc,
+                      const uint16_t* vc, float* out, int M, int nH, int nkv, int hd, int row_stride, int stride,
+                      int window, int p0) {
+    const int grp = nH / nkv, hf = hd / 2;
+#pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int m = 0; m < M; m++)
+        for (int h = 0; h < nH; h++) {
+            const int kvh = h / grp;
+            const int pos = p0 + m;
+            const int T = window > 0 ? (pos + 1 < window ? pos + 1 : window) : pos + 1;
+            const float* cb = cosM + (size_t)m * hd;
+            const float* sb = sinM + (size_t)m * hd;
+            float qr[512], acc[512], sc[256], red[256];
+            const size_t qb = (size_t)m * row_stride + (size_t)h * hd;
+            for (int i = 0; i < hd; i++) qr[i] = q[qb + i];
+            const float iq = 1.0f / sqrtf(orc_sumsq_256(qr, hd) / (float)hd + 1e-6f);
+            for (int i = 0; i < hd; i++) qr[i] = qr[i] * iq * qnw[i];
+            for (int i = 0; i < hd; i++) {
+                const float rh = i < hf ? -qr[i + hf] : qr[i - hf];
+                acc[i] = qr[i] * cb[i] + rh * sb[i];
+            }
+            for (int i = 0; i < hd; i++) {
+                qr[i] = acc[i];
+                acc[i] = 0.0f;
+            }
+            float msh = -1e30f, lsh = 0.0f;
+            for (int tile = 0; tile < T; tile += 256) {
+                const int tlen = T - tile < 256 ? T - tile : 256;
+                for (int j = 0; j < tlen; j++) {
+                    const int slot = tile + j;
+                    const uint16_t* k = kc + ((size_t)kvh * stride + slot) * hd;
+                    float d2 = 0.0f;
+                    for (int i = 0; i < hd; i += 4)
+                        d2 += qr[i] * orc_f16_to_f32(k[i]) + qr[i + 1] * orc_f16_to_f32(k[i + 1]) +
+                              qr[i + 2] * orc_f16_to_f32(k[i + 2]) + qr[i + 3] * orc_f16_to_f32(k[i + 3]);
+                    if (window > 0) {
+                        const long long base = (long long)p0 + M - 1;
+                        const long long posn = base - ((base + window - slot) % window);
+                        if (posn > pos) d2 = -1e30f;
+                    }
+                    sc[j] = d2;
+                }
+                float mx = -1e30f;
+                for (int j = 0; j < tlen; j++) mx = sc[j] > mx ? sc[j] : mx;
+                const float mn = msh > mx ? msh : mx;
+                const float corr = expf(msh - mn);
+                msh = mn;
+                for (int t = 0; t < 256; t++) {
+                    red[t] = 0.0f;
+                    if (t < tlen) {
+                        sc[t] = expf(sc[t] - mn);
+                        red[t] = sc[t];
+                    }
+                }
+                for (int st = 128; st > 0; st >>= 1)
+                    for (int t = 0; t < st; t++) red[t] += red[t + st];
+                lsh = lsh * corr + red[0];
+                for (int i = 0; i < hd; i++) {
+                    float a = acc[i] * corr;
+                    for (int j = 0; j < tlen; j++)
+                        a += sc[j] * orc_f16_to_f32(vc[((size_t)kvh * stride + tile + j) * hd + i]);
+                    acc[i] = a;
+                }
+            }
+            for (int i = 0; i < hd; i++) out[qb + i] = acc[i] / lsh;
+        }
 }
 
 int orc_num_threads(void) {

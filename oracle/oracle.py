@@ -18,7 +18,7 @@ __all__ = [
     "quant_i4", "fp8_scales", "split_for", "w8a8_weights", "w4a8_ratio", "gemv", "reduce",
     "dequant", "gemm_i4", "cast_i8", "gemm_w8a8", "w4a8_requant", "gemm_w4a8",
     "num_threads", "set_num_threads", "pack_reference", "rmsnorm", "normadd", "gelumul", "decode_token",
-    "attn_prepkv", "attn_decode",
+    "attn_prepkv", "attn_decode", "attn_prefill_prepkv", "attn_prefill",
 ]
 
 
@@ -61,6 +61,8 @@ def lib():
         L.orc_gelumul.argtypes = [P, P, P, i]
         L.orc_attn_prepkv.argtypes = [P, P, P, P, P, P, i, i, i, i, i, i, i, i]
         L.orc_attn_decode.argtypes = [P, P, P, P, P, P, P, i, i, i, i, i, i, i]
+        L.orc_attn_prefill_prepkv.argtypes = [P, P, P, P, P, P, P, i, i, i, i, i, i, i]
+        L.orc_attn_prefill.argtypes = [P, P, P, P, P, P, P, i, i, i, i, i, i, i, i]
         L.orc_num_threads.restype = i
         L.orc_set_num_threads.argtypes = [i]
         _lib = L
@@ -327,4 +329,28 @@ def attn_decode(qkv, qnw, cos_t, sin_t, kc, vc, nH: int, nkv: int, hd: int, qoff
     lib().orc_attn_decode(_p(_c(qkv, np.float32)), _p(_c(qnw, np.float32)), _p(_c(cos_t, np.float32)),
                           _p(_c(sin_t, np.float32)), _p(_c(kc, np.uint16)), _p(_c(vc, np.uint16)), _p(out), nH, nkv,
                           hd, qoff, kc.shape[1], window, pos)
+    return out
+
+
+def attn_prefill_prepkv(k, v, knw, cosM, sinM, kc, vc, nkv: int, hd: int, window: int, p0: int):
+    """vk/pre_prepkv.comp:15-30 on host arrays: k, v [M, row] f32 (v may be k), cosM / sinM [M, hd];
+    writes slots p0 .. p0 + M - 1 (% window) of kc / vc ([nkv, stride, hd] uint16 f16 bits) in place."""
+    k = _c(k, np.float32)
+    v = _c(v, np.float32)
+    assert k.shape == v.shape and k.ndim == 2
+    assert kc.dtype == np.uint16 and vc.dtype == np.uint16 and kc.flags.c_contiguous and vc.flags.c_contiguous
+    lib().orc_attn_prefill_prepkv(_p(k), _p(v), _p(_c(knw, np.float32)), _p(_c(cosM, np.float32)),
+                                  _p(_c(sinM, np.float32)), _p(kc), _p(vc), k.shape[0], nkv, hd, k.shape[1],
+                                  kc.shape[1], window, p0)
+
+
+def attn_prefill(q, qnw, cosM, sinM, kc, vc, nH: int, nkv: int, hd: int, window: int, p0: int):
+    """vk/pre_attn.comp:16-53 on host arrays: q [M, row] f32 -> the [M, row] f32 attention output
+    (columns beyond nH * hd are zero)."""
+    q = _c(q, np.float32)
+    assert q.ndim == 2 and q.shape[1] >= nH * hd
+    out = np.zeros_like(q)
+    lib().orc_attn_prefill(_p(q), _p(_c(qnw, np.float32)), _p(_c(cosM, np.float32)), _p(_c(sinM, np.float32)),
+                           _p(_c(kc, np.uint16)), _p(_c(vc, np.uint16)), _p(out), q.shape[0], nH, nkv, hd, q.shape[1],
+                           kc.shape[1], window, p0)
     return out

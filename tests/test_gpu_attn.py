@@ -6,8 +6,9 @@ this token's k and v with prepkv (and checks that slot against the oracle's
 and that no other slot moved), then runs attention and compares it with the
 oracle run on the very cache contents the device holds.  Floating-point bar:
 tests/util.py (max relative error 1e-2 with a 1e-3 x rms guard, cosine >=
-0.9999); the k / v slot is compared the same way (its rsqrt differs in the
-last bits, which can move an f16 rounding)."""
+0.9999; the prefill outputs, 1.2M values per case, with util.ATTN_GUARD's 1e-2 x
+rms floor); the k / v slots are compared the same way (their rsqrt differs in
+the last bits, which can move an f16 rounding)."""
 import numpy as np
 import pytest
 import torch
@@ -15,7 +16,7 @@ import torch
 import oracle as O
 from g4b import _lib as L
 from g4b import ops
-from util import assert_close
+from util import ATTN_GUARD, assert_close
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -126,3 +127,74 @@ def test_attention_rejects_unsupported_shapes():
                              z.data_ptr(), z.data_ptr(), L.DT_F32, 8, 1, 512, 0, 4, 0, p.data_ptr(), None, 0,
                              torch.cuda.current_stream().cuda_stream)
     assert st == L.G4B_E_SHAPE and "query heads" in L.last_error()
+
+
+# ---------------------------------------------------------------- prefill (vk/pre_prepkv.comp, vk/pre_attn.comp)
+def _rope_rows(hd, p0, M):
+    rows = [_rope(hd, p0 + m) for m in range(M)]
+    return np.stack([r[0] for r in rows]), np.stack([r[1] for r in rows])
+
+
+@pytest.mark.parametrize("nH,nkv,hd,stride,window,p0,M,keqv,dtype", [
+    (16, 8, 256, 4096, 0, 0, 300, False, torch.float32),      # a prompt's first chunk
+    (16, 8, 256, 2048, 0, 1000, 128, False, torch.float16),   # a chunk after a cached prefix
+    (16, 8, 256, 512, 512, 700, 200, False, torch.float32),   # sliding ring: wraps, future slots masked
+    (4, 2, 128, 64, 64, 30, 100, True, torch.float32),        # chunk longer than the ring; k = v
+    (4, 2, 512, 1024, 0, 100, 70, False, torch.float32),      # head_dim 512
+    (8, 1, 128, 512, 0, 5, 77, False, torch.float16),         # 8 query heads per KV head
+    (2, 2, 256, 256, 0, 40, 1, False, torch.float32),         # one token
+])
+def test_prefill_attention_matches_oracle(nH, nkv, hd, stride, window, p0, M, keqv, dtype):
+    rng = np.random.default_rng(M + hd + p0)
+    nq, nk = nH * hd, nkv * hd
+    q = rng.standard_normal((M, nq)).astype(np.float32)
+    k = rng.standard_normal((M, nk)).astype(np.float32)
+    v = k if keqv else rng.standard_normal((M, nk)).astype(np.float32)
+    if dtype == torch.float16:
+        q, k, v = (a.astype(np.float16).astype(np.float32) for a in (q, k, v))
+    knw = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    qnw = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kc = rng.standard_normal((nkv, stride, hd)).astype(np.float16).view(np.uint16)   # the cached prefix
+    vc = rng.standard_normal((nkv, stride, hd)).astype(np.float16).view(np.uint16)
+    cosM, sinM = _rope_rows(hd, p0, M)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)  # noqa: E731
+    qd, kd_in, vd_in = t(q).to(dtype), t(k).to(dtype), t(v).to(dtype)
+    if keqv:
+        vd_in = kd_in
+    kcd, vcd = t(kc.view(np.int16)), t(vc.view(np.int16))
+    p0d = torch.tensor([p0], dtype=torch.int32, device=DEV)
+    ops.attn_prefill_prepkv(kd_in, vd_in, t(knw), t(cosM), t(sinM), kcd, vcd, p0d, nkv, hd, window=window)
+    O.attn_prefill_prepkv(k, v, knw, cosM, sinM, kc, vc, nkv, hd, window, p0)
+    torch.cuda.synchronize()
+    kd = kcd.cpu().numpy().view(np.uint16)
+    vd = vcd.cpu().numpy().view(np.uint16)
+    f = lambda u: u.view(np.float16).astype(np.float32)  # noqa: E731
+    assert_close(f(kd), f(kc), "prefill prepkv k")
+    assert_close(f(vd), f(vc), "prefill prepkv v")
+    ref = O.attn_prefill(q, qnw, cosM, sinM, kd, vd, nH, nkv, hd, window, p0)
+    for out_dtype in (torch.float32, torch.float16):
+        out = ops.attn_prefill(qd, t(qnw), t(cosM), t(sinM), kcd, vcd, p0d, nH, nkv, hd, window=window,
+                               out_dtype=out_dtype)
+        torch.cuda.synchronize()
+        assert_close(out.float().cpu().numpy(), ref, f"prefill attn nH={nH} hd={hd} p0={p0} M={M} window={window}",
+                     guard=ATTN_GUARD)
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+
+
+def test_prefill_attention_writes_into_row_views():
+    """q and out as column slices of wider rows (the engine's q|k|v and attention buffers)."""
+    nH, nkv, hd, stride, M, p0 = 4, 2, 256, 512, 50, 60
+    rng = np.random.default_rng(3)
+    row = nH * hd + 2 * nkv * hd
+    qkv = torch.from_numpy(rng.standard_normal((M, row)).astype(np.float32)).to(DEV)
+    kc = torch.from_numpy(rng.standard_normal((nkv, stride, hd)).astype(np.float16).view(np.int16)).to(DEV)
+    vc = kc.clone()
+    qnw = torch.ones(hd, device=DEV)
+    cosM, sinM = (torch.from_numpy(a).to(DEV) for a in _rope_rows(hd, p0, M))
+    p0d = torch.tensor([p0], dtype=torch.int32, device=DEV)
+    wide = torch.full((M, nH * hd + 64), 7.0, device=DEV)
+    ops.attn_prefill(qkv[:, :nH * hd], qnw, cosM, sinM, kc, vc, p0d, nH, nkv, hd, out=wide[:, :nH * hd])
+    ref = ops.attn_prefill(qkv[:, :nH * hd].contiguous(), qnw, cosM, sinM, kc, vc, p0d, nH, nkv, hd)
+    torch.cuda.synchronize()
+    assert torch.equal(wide[:, :nH * hd], ref)
+    assert bool((wide[:, nH * hd:] == 7.0).all())

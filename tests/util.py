@@ -9,6 +9,11 @@ import numpy as np
 MAX_REL = 1e-2
 GUARD = 1e-3
 MIN_COS = 0.9999
+# Attention outputs: the softmax turns a score's rounding (about 1e-5 of a score whose magnitude is
+# ~|q||k| = tens, differing between any two summation orders of the same f32 products) into a relative
+# change of the weights, so an output that cancels to near zero carries an absolute error of ~1e-5 x
+# rms(v) whatever the implementation.  Their denominator floor is 1e-2 x rms (as the long-K GEMMs').
+ATTN_GUARD = 1e-2
 
 
 def rel_err(out, ref, guard: float = GUARD) -> float:
