@@ -1209,7 +1209,7 @@ def measure_engine(c, args):
 
     Decode is all g4b: per layer one fused chain launch (the GEMVs with the
     norms and gelu*up, g4b.decode.SegmentedDecodeToken) and the KV-cache write
-    and flash-decode attention (g4b_attn_prepkv, g4b_attn_decode) over a
+    and flash-decode attention in one launch (g4b_attn_decode_prepkv) over a
     synthetic f16 cache (GQA, 16 query and 8 KV heads of 256), timed as K
     graph replays at a fixed context (the reference grows it by 64 tokens).
     Prefill runs the W4A16 GEMMs (and, as PREFILL_I8 does, cast_i8 + the W8A8
@@ -1238,7 +1238,7 @@ def measure_engine(c, args):
     nw = lambda: (1.0 + 0.1 * torch.randn((H,), generator=gen, device=c.device))  # noqa: E731
     norms = [decode.LayerNorms(inw=nw(), paw=nw(), pfw=nw(), ofw=nw(), scl=1.0) for _ in range(args.layers)]
     finw = nw()
-    out = {"attention": "decode: g4b_attn_prepkv + g4b_attn_decode (GQA 16/8 heads of 256, f16 KV cache); "
+    out = {"attention": "decode: g4b_attn_decode_prepkv (GQA 16/8 heads of 256, f16 KV cache); "
                         "prefill: torch scaled_dot_product_attention stand-in",
            "steps": args.steps}
     # ---- decode
@@ -1257,10 +1257,9 @@ def measure_engine(c, args):
 
         def attention(li, stream, kc=kc, vc=vc, pos=pos, cos_t=cos_t, sin_t=sin_t, aws=aws):
             b = tok.bufs
-            c.ops.attn_prepkv(b["qkv"], knw[li], cos_t, sin_t, kc[li], vc[li], pos, NKV_HEADS, HEAD_DIM, NQ,
-                              NQ + NKV_HEADS * HEAD_DIM, stream=stream)
-            c.ops.attn_decode(b["qkv"], qnw[li], cos_t, sin_t, kc[li], vc[li], pos, NH, NKV_HEADS, HEAD_DIM,
-                              out=b["attn"], stream=stream, workspace=aws)
+            c.ops.attn_decode_prepkv(b["qkv"], qnw[li], knw[li], cos_t, sin_t, kc[li], vc[li], pos, NH, NKV_HEADS,
+                                     HEAD_DIM, NQ, NQ + NKV_HEADS * HEAD_DIM, out=b["attn"], stream=stream,
+                                     workspace=aws)
 
         graph = capture(c, lambda: tok.run(c.stream, attention), args.warmup)
         ms = timed_graph(c, graph, args.steps) / args.steps
@@ -1268,8 +1267,7 @@ def measure_engine(c, args):
         out[f"decode ms/token @ctx {ctx}"] = round(ms, 4)
         del graph, kc, vc, aws
         torch.cuda.empty_cache()
-    out["decode launches/token"] = (f"{len(tok.chains)} chain launches + {args.layers} x (prepkv, attention, "
-                                    "split combine)")
+    out["decode launches/token"] = f"{len(tok.chains)} chain launches + {args.layers} attention launches"
     tok.close()
     # ---- prefill: one 2048-token prompt
     T = PROMPT_LEN

@@ -9,10 +9,11 @@
 //   decode  flash decoding: grid (splits, KV heads).  A CTA normalises and rotates the
 //           query heads that share its KV head (GQA), then its 8 warps stream their
 //           share of the split's keys -- each K and V row is read once for all those
-//           heads, 16-byte loads per lane -- with an online softmax per warp; the warps'
-//           partials merge in shared memory, and a split's (max, sum, weighted V) goes
-//           to the workspace for a second kernel to combine.  HBM-bound on the cache:
-//           T * hd * 2 bytes of K and of V per KV head.
+//           heads, 16-byte loads per lane, 4 keys in flight per warp -- with an online
+//           softmax per warp; the warps' partials merge in shared memory, a split's (max,
+//           sum, weighted V) goes to the workspace, and the last split of a KV head to
+//           finish combines them.  HBM-bound on the cache: T * hd * 2 bytes of K and of V
+//           per KV head.
 //
 //   prefill causal attention of a chunk of M tokens, flash-attention style on the tensor
 //           cores (mma.sync m16n8k16, f32 accumulate): a CTA takes 64-128 (token, query
@@ -34,6 +35,7 @@ constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr float kAttnEps = 1e-6f;     // vk/attn.comp:25, vk/prepkv.comp:21
 constexpr float kNegInit = -1e30f;    // the shaders' running-max start (vk/attn.comp:29)
+constexpr int kAttnMaxSplits = 64;    // key splits per KV head (the last split combines them from shared memory)
 
 // n consecutive values (n = 4, 8, 16) of an f32 or f16 vector as f32
 template <int N, bool F32>
@@ -77,28 +79,14 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 // ------------------------------------------------------------------ prepkv
-// One CTA per (KV head, token m); thread t owns elements t and t + 256 (hd <= 512).  Token m's k and
-// v rows are row_stride elements after token m-1's; its cos / sin row is cs_stride floats after (0:
-// one shared row, the decode token); its position is pos_dev[0] + m.
+// One KV head of one token, by a CTA of kAttnThreads threads (thread t owns elements t and t + 256;
+// hd <= 512): k = RoPE(rmsnorm(k, knw)) and v = rmsnorm(v) as f16 into slot `slot` of kc / vc
+// (vk/prepkv.comp:18-29, vk/pre_prepkv.comp:20-30).  rb is the head's offset into the kin / vin rows.
 template <bool XF32>
-__global__ void __launch_bounds__(kAttnThreads) attn_prepkv_kernel(const void* __restrict__ kin,
-                                                                  const void* __restrict__ vin, int row_stride,
-                                                                  const float* __restrict__ knw,
-                                                                  const float* __restrict__ cos_t,
-                                                                  const float* __restrict__ sin_t, int cs_stride,
-                                                                  uint16_t* kc, uint16_t* vc, int hd, int stride,
-                                                                  int window, const int* __restrict__ pos_dev) {
-    __shared__ float hv[512];
-    __shared__ float wsum[kAttnWarps];
-    const int h = blockIdx.x, m = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5, hf = hd / 2;
-    const int pos = __ldg(pos_dev) + m;
-    const int slot = window > 0 ? pos % window : pos;
-    if (slot >= stride) return;   // past the cache (the host checks what it can; the position is on the device)
-    // a chunk longer than the ring writes some slots twice: the later token's write is the one that stays
-    if (window > 0 && m + window < (int)gridDim.y) return;
-    const size_t rb = (size_t)m * row_stride + (size_t)h * hd;
-    const float* cb = cos_t + (size_t)m * cs_stride;
-    const float* sb = sin_t + (size_t)m * cs_stride;
+__device__ __forceinline__ void prep_head(const void* kin, const void* vin, size_t rb, const float* __restrict__ knw,
+                                          const float* __restrict__ cb, const float* __restrict__ sb, uint16_t* kc,
+                                          uint16_t* vc, int h, int hd, int stride, int slot, float* hv, float* wsum) {
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, hf = hd / 2;
     auto elem = [&](const void* base, int i) -> float {
         return XF32 ? __ldg(reinterpret_cast<const float*>(base) + rb + i)
                     : __half2float(__ldg(reinterpret_cast<const __half*>(base) + rb + i));
@@ -113,7 +101,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prepkv_kernel(const void* _
         __syncthreads();
         return rsqrtf(tot / (float)hd + kAttnEps);
     };
-    // k: rmsnorm with knw, then RoPE (vk/prepkv.comp:18-24, vk/pre_prepkv.comp:20-24)
     float s = 0.f;
     for (int i = t; i < hd; i += kAttnThreads) {
         const float v = elem(kin, i);
@@ -128,7 +115,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prepkv_kernel(const void* _
         const float rh = i < hf ? -hv[i + hf] : hv[i - hf];
         krow[i] = __half_as_ushort(__float2half_rn(hv[i] * __ldg(cb + i) + rh * __ldg(sb + i)));
     }
-    // v: rmsnorm without a weight (vk/prepkv.comp:25-29, vk/pre_prepkv.comp:26-30); k = v passes vin = kin
     s = 0.f;
     float vv[2] = {0.f, 0.f};
     for (int i = t, n = 0; i < hd; i += kAttnThreads, n++) {
@@ -140,10 +126,35 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prepkv_kernel(const void* _
     for (int i = t, n = 0; i < hd; i += kAttnThreads, n++) vrow[i] = __half_as_ushort(__float2half_rn(vv[n] * iv));
 }
 
+// One CTA per (KV head, token m).  Token m's k and v rows are row_stride elements after token m-1's;
+// its cos / sin row is cs_stride floats after (0: one shared row, the decode token); its position is
+// pos_dev[0] + m.  k = v passes vin = kin.
+template <bool XF32>
+__global__ void __launch_bounds__(kAttnThreads) attn_prepkv_kernel(const void* __restrict__ kin,
+                                                                  const void* __restrict__ vin, int row_stride,
+                                                                  const float* __restrict__ knw,
+                                                                  const float* __restrict__ cos_t,
+                                                                  const float* __restrict__ sin_t, int cs_stride,
+                                                                  uint16_t* kc, uint16_t* vc, int hd, int stride,
+                                                                  int window, const int* __restrict__ pos_dev) {
+    __shared__ float hv[512];
+    __shared__ float wsum[kAttnWarps];
+    const int h = blockIdx.x, m = blockIdx.y;
+    const int pos = __ldg(pos_dev) + m;
+    const int slot = window > 0 ? pos % window : pos;
+    if (slot >= stride) return;   // past the cache (the host checks what it can; the position is on the device)
+    // a chunk longer than the ring writes some slots twice: the later token's write is the one that stays
+    if (window > 0 && m + window < (int)gridDim.y) return;
+    prep_head<XF32>(kin, vin, (size_t)m * row_stride + (size_t)h * hd, knw, cos_t + (size_t)m * cs_stride,
+                    sin_t + (size_t)m * cs_stride, kc, vc, h, hd, stride, slot, hv, wsum);
+}
+
 // ------------------------------------------------------------------ decode
 struct AttnArgs {
     const void* qkv;
     const float* qnw;
+    const float* knw;    // PREP: the k norm weight
+    int koff, voff;      // PREP: k and v in qkv (voff = koff for k = v)
     const float* cos_t;
     const float* sin_t;
     const uint16_t* kc;
@@ -151,45 +162,75 @@ struct AttnArgs {
     void* out;           // S == 1: [nH, hd] output
     float* part;         // S > 1: [nH][S][hd] weighted V sums
     float* pml;          // S > 1: [nH][S][2] (running max, sum)
+    unsigned* arrive;    // S > 1: [nkv] split arrival counters, zero between calls
     const int* pos_dev;
     int nH, nkv, hd, qoff, stride, window, S, out_f32;
 };
 
-// D = hd / 32 values per lane, G = query heads per KV head
-template <int D, int G, bool XF32>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArgs a) {
+// n f16 values of a cache row as n / 2 packed pairs (streamed: the cache is read once per token)
+template <int N>
+__device__ __forceinline__ void load_pairs(const uint16_t* p, uint32_t (&w)[N / 2]) {
+    if constexpr (N == 4) {
+        const uint2 u = __ldcs(reinterpret_cast<const uint2*>(p));
+        w[0] = u.x; w[1] = u.y;
+    } else {
+        #pragma unroll
+        for (int j = 0; j < N / 8; j++) {
+            const uint4 u = __ldcs(reinterpret_cast<const uint4*>(p) + j);
+            w[4 * j] = u.x; w[4 * j + 1] = u.y; w[4 * j + 2] = u.z; w[4 * j + 3] = u.w;
+        }
+    }
+}
+
+// D = hd / 32 values per lane, G = query heads per KV head; PREP: the CTA whose split holds this
+// token's slot first writes the token's k / v there (prepkv fused in: the engine's two dispatches in
+// one launch)
+template <int D, int G, bool XF32, bool PREP>
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const AttnArgs a) {
     constexpr int HD = 32 * D;
+    constexpr int KB = D >= 16 ? 2 : 4;   // keys a warp loads at once (4 KB in flight per warp at hd 256)
+    constexpr int DW = D / 2;
     static_assert(G * D <= 32, "query heads x values per lane held in registers");
-    __shared__ float qs[G][HD];                       // the normed query heads
-    __shared__ float xacc[kAttnWarps / 2][G][HD];     // partials handed down the warp merge tree
-    __shared__ float xm[kAttnWarps / 2][G], xl[kAttnWarps / 2][G];
+    __shared__ float xacc[kAttnWarps][G][HD];   // every warp's partial, merged by all threads
+    __shared__ float xm[kAttnWarps][G], xl[kAttnWarps][G];
     const int s = blockIdx.x, kvh = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int pos = __ldg(a.pos_dev);
     const int T = min(a.window > 0 ? min(pos + 1, a.window) : pos + 1, a.stride);   // never past the cache
     const int k0 = (int)((long long)s * T / a.S), k1 = (int)((long long)(s + 1) * T / a.S);
-    // the query heads of this KV head: rmsnorm with qnw, then RoPE (vk/attn.comp:22-28)
-    if (warp < G) {
-        const int h = kvh * G + warp;
-        float q[D];
-        loadn<D, XF32>(a.qkv, (size_t)a.qoff + (size_t)h * HD + lane * D, q);
+    const size_t row0 = (size_t)kvh * a.stride;
+    if constexpr (PREP) {
+        __shared__ float hv[512];
+        __shared__ float wsum[kAttnWarps];
+        const int slot = a.window > 0 ? pos % a.window : pos;
+        if (slot >= k0 && slot < k1) {   // the same for every thread of the CTA
+            const size_t esz = XF32 ? 4 : 2;
+            prep_head<XF32>(reinterpret_cast<const char*>(a.qkv) + (size_t)a.koff * esz,
+                            reinterpret_cast<const char*>(a.qkv) + (size_t)a.voff * esz, (size_t)kvh * HD, a.knw,
+                            a.cos_t, a.sin_t, const_cast<uint16_t*>(a.kc), const_cast<uint16_t*>(a.vc), kvh, HD,
+                            a.stride, slot, hv, wsum);
+            __syncthreads();   // the new row is read below by other warps of this CTA
+        }
+    }
+    // the query heads of this KV head: rmsnorm with qnw, then RoPE (vk/attn.comp:22-28); every warp
+    // makes its own copy (element i's rotation partner i +- hd/2 is in lane ^ 16)
+    float q[G][D];
+    #pragma unroll
+    for (int g = 0; g < G; g++) {
+        float v[D];
+        loadn<D, XF32>(a.qkv, (size_t)a.qoff + (size_t)(kvh * G + g) * HD + lane * D, v);
         float ss = 0.f;
         #pragma unroll
-        for (int d = 0; d < D; d++) ss += q[d] * q[d];
+        for (int d = 0; d < D; d++) ss += v[d] * v[d];
         const float iq = rsqrtf(warp_sum(ss) / (float)HD + kAttnEps);
         #pragma unroll
-        for (int d = 0; d < D; d++) qs[warp][lane * D + d] = q[d] * iq * __ldg(a.qnw + lane * D + d);
-    }
-    __syncthreads();
-    float qr[G][D];
-    #pragma unroll
-    for (int g = 0; g < G; g++)
-        #pragma unroll
         for (int d = 0; d < D; d++) {
-            const int i = lane * D + d, hf = HD / 2;
-            const float rh = i < hf ? -qs[g][i + hf] : qs[g][i - hf];
-            qr[g][d] = qs[g][i] * __ldg(a.cos_t + i) + rh * __ldg(a.sin_t + i);
+            const int i = lane * D + d;
+            const float nv = v[d] * iq * __ldg(a.qnw + i);
+            const float pv = __shfl_xor_sync(0xffffffffu, nv, 16);
+            q[g][d] = nv * __ldg(a.cos_t + i) + (lane < 16 ? -pv : pv) * __ldg(a.sin_t + i);
         }
-    // this warp's keys: an online softmax per query head
+    }
+    // this warp's keys, KB at a time: an online softmax per query head
     float m[G], l[G], acc[G][D];
     #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -198,132 +239,179 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const AttnArg
         #pragma unroll
         for (int d = 0; d < D; d++) acc[g][d] = 0.f;
     }
-    const size_t row0 = (size_t)kvh * a.stride;
-    for (int j = k0 + warp; j < k1; j += kAttnWarps) {
-        float kv[D], vv[D];
-        load_f16n<D>(a.kc + (row0 + j) * HD + lane * D, kv);
-        load_f16n<D>(a.vc + (row0 + j) * HD + lane * D, vv);
+    const uint16_t* kbase = a.kc + row0 * HD + lane * D;
+    const uint16_t* vbase = a.vc + row0 * HD + lane * D;
+    for (int j0 = k0 + warp * KB; j0 < k1; j0 += kAttnWarps * KB) {
+        uint32_t kr[KB][DW], vr[KB][DW];
+        #pragma unroll
+        for (int u = 0; u < KB; u++) {
+            const size_t j = (size_t)min(j0 + u, k1 - 1);   // past the split: a repeat, weighted 0 below
+            load_pairs<D>(kbase + j * HD, kr[u]);
+            load_pairs<D>(vbase + j * HD, vr[u]);
+        }
+        float dot[G][KB];
+        #pragma unroll
+        for (int g = 0; g < G; g++)
+            #pragma unroll
+            for (int u = 0; u < KB; u++) {
+                float x = 0.f;
+                #pragma unroll
+                for (int w = 0; w < DW; w++) {
+                    x = fmaf(q[g][2 * w], h_lo(kr[u][w]), x);
+                    x = fmaf(q[g][2 * w + 1], h_hi(kr[u][w]), x);
+                }
+                dot[g][u] = x;
+            }
+        #pragma unroll
+        for (int mk = 16; mk >= 1; mk >>= 1)
+            #pragma unroll
+            for (int g = 0; g < G; g++)
+                #pragma unroll
+                for (int u = 0; u < KB; u++) dot[g][u] += __shfl_xor_sync(0xffffffffu, dot[g][u], mk);
         #pragma unroll
         for (int g = 0; g < G; g++) {
-            float dot = 0.f;
+            float mx = m[g];
             #pragma unroll
-            for (int d = 0; d < D; d++) dot = fmaf(qr[g][d], kv[d], dot);
-            dot = warp_sum(dot);
-            const float mn = fmaxf(m[g], dot);
-            const float corr = __expf(m[g] - mn), p = __expf(dot - mn);
-            l[g] = l[g] * corr + p;
-            m[g] = mn;
+            for (int u = 0; u < KB; u++)
+                if (j0 + u < k1) mx = fmaxf(mx, dot[g][u]);
+            const float corr = __expf(m[g] - mx);
+            float p[KB], ps = 0.f;
             #pragma unroll
-            for (int d = 0; d < D; d++) acc[g][d] = fmaf(p, vv[d], acc[g][d] * corr);
+            for (int u = 0; u < KB; u++) {
+                p[u] = j0 + u < k1 ? __expf(dot[g][u] - mx) : 0.f;
+                ps += p[u];
+            }
+            l[g] = l[g] * corr + ps;
+            m[g] = mx;
+            #pragma unroll
+            for (int w = 0; w < DW; w++) {
+                float a0 = acc[g][2 * w] * corr, a1 = acc[g][2 * w + 1] * corr;
+                #pragma unroll
+                for (int u = 0; u < KB; u++) {
+                    a0 = fmaf(p[u], h_lo(vr[u][w]), a0);
+                    a1 = fmaf(p[u], h_hi(vr[u][w]), a1);
+                }
+                acc[g][2 * w] = a0;
+                acc[g][2 * w + 1] = a1;
+            }
         }
     }
-    // merge the warps' partials down a tree (8 -> 4 -> 2 -> 1): the upper half hands its (max, sum,
-    // weighted V) to the lower half through shared memory, which rescales and adds in registers
+    // merge the 8 warps' partials: each thread rescales and sums a few (head, element) values
     #pragma unroll
-    for (int half = kAttnWarps / 2; half >= 1; half >>= 1) {
-        if (warp >= half && warp < 2 * half) {
-            #pragma unroll
-            for (int g = 0; g < G; g++) {
-                if (lane == 0) {
-                    xm[warp - half][g] = m[g];
-                    xl[warp - half][g] = l[g];
-                }
-                #pragma unroll
-                for (int d = 0; d < D; d++) xacc[warp - half][g][lane * D + d] = acc[g][d];
-            }
+    for (int g = 0; g < G; g++) {
+        if (lane == 0) {
+            xm[warp][g] = m[g];
+            xl[warp][g] = l[g];
         }
-        __syncthreads();
-        if (warp < half) {
-            #pragma unroll
-            for (int g = 0; g < G; g++) {
-                const float m2 = xm[warp][g], l2 = xl[warp][g], M = fmaxf(m[g], m2);
-                const float e1 = __expf(m[g] - M), e2 = __expf(m2 - M);
-                l[g] = l[g] * e1 + l2 * e2;
-                m[g] = M;
-                #pragma unroll
-                for (int d = 0; d < D; d++) acc[g][d] = acc[g][d] * e1 + xacc[warp][g][lane * D + d] * e2;
-            }
-        }
-        __syncthreads();
-    }
-    if (warp == 0) {
         #pragma unroll
-        for (int g = 0; g < G; g++) {
-            const int h = kvh * G + g;
-            if (a.S == 1) {
-                const float invl = 1.0f / l[g];
-                #pragma unroll
-                for (int d = 0; d < D; d++) {
-                    const float o = acc[g][d] * invl;
-                    const size_t at = (size_t)h * HD + lane * D + d;
-                    if (a.out_f32) reinterpret_cast<float*>(a.out)[at] = o;
-                    else reinterpret_cast<__half*>(a.out)[at] = __float2half_rn(o);
-                }
-            } else {
-                #pragma unroll
-                for (int d = 0; d < D; d++) a.part[((size_t)h * a.S + s) * HD + lane * D + d] = acc[g][d];
-                if (lane == 0) {
-                    a.pml[((size_t)h * a.S + s) * 2] = m[g];
-                    a.pml[((size_t)h * a.S + s) * 2 + 1] = l[g];
-                }
+        for (int d = 0; d < D; d++) xacc[warp][g][lane * D + d] = acc[g][d];
+    }
+    __syncthreads();
+    for (int e = t; e < G * HD; e += kAttnThreads) {
+        const int g = e / HD, i = e % HD, h = kvh * G + g;
+        float M = kNegInit;
+        #pragma unroll
+        for (int w = 0; w < kAttnWarps; w++) M = fmaxf(M, xm[w][g]);
+        float L = 0.f, V = 0.f;
+        #pragma unroll
+        for (int w = 0; w < kAttnWarps; w++) {
+            const float ew = __expf(xm[w][g] - M);
+            L = fmaf(xl[w][g], ew, L);
+            V = fmaf(xacc[w][g][i], ew, V);
+        }
+        if (a.S == 1) {
+            const float o = V / L;
+            if (a.out_f32) reinterpret_cast<float*>(a.out)[(size_t)h * HD + i] = o;
+            else reinterpret_cast<__half*>(a.out)[(size_t)h * HD + i] = __float2half_rn(o);
+        } else {
+            a.part[((size_t)h * a.S + s) * HD + i] = V;
+            if (i == 0) {
+                a.pml[((size_t)h * a.S + s) * 2] = M;
+                a.pml[((size_t)h * a.S + s) * 2 + 1] = L;
             }
         }
+    }
+    if (a.S == 1) return;
+    // the last split of this KV head to arrive combines all of them:
+    //   out = sum_s v_s e^(m_s - M) / sum_s l_s e^(m_s - M)
+    // (atomicInc wraps the counter back to zero for the next call)
+    __shared__ unsigned s_last;
+    __threadfence();
+    __syncthreads();
+    if (t == 0) s_last = atomicInc(a.arrive + kvh, (unsigned)(a.S - 1)) == (unsigned)(a.S - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // warp g: head g's split weights e^(m_s - M) / L into shared memory (one round trip for the (m, l)s)
+    __shared__ float s_w[G][kAttnMaxSplits];
+    if (warp < G) {
+        const float2* pm = reinterpret_cast<const float2*>(a.pml) + (size_t)(kvh * G + warp) * a.S;
+        float2 v[kAttnMaxSplits / 32];
+        float M = kNegInit;
+        #pragma unroll
+        for (int r = 0; r < kAttnMaxSplits / 32; r++) {
+            const int k = lane + 32 * r;
+            v[r] = k < a.S ? __ldcg(pm + k) : make_float2(kNegInit, 0.f);
+            M = fmaxf(M, v[r].x);
+        }
+        #pragma unroll
+        for (int mk = 16; mk >= 1; mk >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, mk));
+        float L = 0.f;
+        #pragma unroll
+        for (int r = 0; r < kAttnMaxSplits / 32; r++) {
+            v[r].x = __expf(v[r].x - M);
+            L = fmaf(v[r].y, v[r].x, L);
+        }
+        const float invL = 1.0f / warp_sum(L);
+        #pragma unroll
+        for (int r = 0; r < kAttnMaxSplits / 32; r++)
+            if (lane + 32 * r < a.S) s_w[warp][lane + 32 * r] = v[r].x * invL;
+    }
+    __syncthreads();
+    for (int e = t; e < G * HD; e += kAttnThreads) {
+        const int g = e / HD, i = e % HD, h = kvh * G + g;
+        const float* pp = a.part + (size_t)h * a.S * HD + i;
+        float V = 0.f;
+        #pragma unroll 8
+        for (int k = 0; k < a.S; k++) V = fmaf(__ldcg(pp + (size_t)k * HD), s_w[g][k], V);
+        if (a.out_f32) reinterpret_cast<float*>(a.out)[(size_t)h * HD + i] = V;
+        else reinterpret_cast<__half*>(a.out)[(size_t)h * HD + i] = __float2half_rn(V);
     }
 }
 
-// the splits' partials -> the output, per query head: out = sum_s v_s e^(m_s - M) / sum_s l_s e^(m_s - M)
-__global__ void __launch_bounds__(kAttnThreads) attn_combine_kernel(const AttnArgs a) {
-    const int h = blockIdx.x, S = a.S;
-    extern __shared__ float sh_e[];                   // [S] weights e^(m_s - M)
-    __shared__ float s_L;
-    if (threadIdx.x < 32) {
-        float M = kNegInit;
-        for (int s = threadIdx.x; s < S; s += 32) M = fmaxf(M, a.pml[((size_t)h * S + s) * 2]);
-        #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float L = 0.f;
-        for (int s = threadIdx.x; s < S; s += 32) {
-            const float e = __expf(a.pml[((size_t)h * S + s) * 2] - M);
-            sh_e[s] = e;
-            L = fmaf(a.pml[((size_t)h * S + s) * 2 + 1], e, L);
-        }
-        L = warp_sum(L);
-        if (threadIdx.x == 0) s_L = L;
-    }
-    __syncthreads();
-    const float invL = 1.0f / s_L;
-    for (int i = threadIdx.x; i < a.hd; i += kAttnThreads) {
-        float v = 0.f;
-        for (int s = 0; s < S; s++) v = fmaf(a.part[((size_t)h * S + s) * a.hd + i], sh_e[s], v);
-        const float o = v * invL;
-        if (a.out_f32) reinterpret_cast<float*>(a.out)[(size_t)h * a.hd + i] = o;
-        else reinterpret_cast<__half*>(a.out)[(size_t)h * a.hd + i] = __float2half_rn(o);
-    }
-}
+// the workspace's arrival counters (one per KV head), ahead of the partials
+static size_t attn_ws_counters(int nkv) { return ((size_t)nkv * sizeof(unsigned) + 255) / 256 * 256; }
 
 // splits of the keys: about two CTAs per SM over the KV heads, at least 32 keys per split
 static int attn_splits(int nkv, int max_T, int sms) {
     const int by_keys = (max_T + 31) / 32;
     const int by_sms = std::max(1, 2 * sms / std::max(nkv, 1));
-    return std::max(1, std::min(by_keys, by_sms));
+    return std::max(1, std::min(std::min(by_keys, by_sms), kAttnMaxSplits));
 }
 
-template <int D, int G>
+template <int D, int G, bool PREP>
 static cudaError_t launch_decode(const AttnArgs& a, bool xf32, cudaStream_t s) {
     const dim3 grid(a.S, a.nkv);
-    if (xf32) attn_decode_kernel<D, G, true><<<grid, kAttnThreads, 0, s>>>(a);
-    else attn_decode_kernel<D, G, false><<<grid, kAttnThreads, 0, s>>>(a);
+    if (xf32) attn_decode_kernel<D, G, true, PREP><<<grid, kAttnThreads, 0, s>>>(a);
+    else attn_decode_kernel<D, G, false, PREP><<<grid, kAttnThreads, 0, s>>>(a);
     return cudaGetLastError();
 }
 
-template <int D>
+template <int D, bool PREP>
 static cudaError_t launch_decode_g(const AttnArgs& a, int G, bool xf32, cudaStream_t s) {
     switch (G) {
-        case 1: return launch_decode<D, 1>(a, xf32, s);
-        case 2: return launch_decode<D, 2>(a, xf32, s);
-        case 4: return launch_decode<D, (D <= 8 ? 4 : 2)>(a, xf32, s);    // G * D <= 32 (checked by the caller)
-        default: return launch_decode<D, (D <= 4 ? 8 : 2)>(a, xf32, s);
+        case 1: return launch_decode<D, 1, PREP>(a, xf32, s);
+        case 2: return launch_decode<D, 2, PREP>(a, xf32, s);
+        case 4: return launch_decode<D, (D <= 8 ? 4 : 2), PREP>(a, xf32, s);   // G * D <= 32 (checked by the caller)
+        default: return launch_decode<D, (D <= 4 ? 8 : 2), PREP>(a, xf32, s);
     }
+}
+
+template <bool PREP>
+static cudaError_t launch_decode_hd(const AttnArgs& a, int G, bool xf32, cudaStream_t s) {
+    return a.hd == 128 ? launch_decode_g<4, PREP>(a, G, xf32, s)
+         : a.hd == 256 ? launch_decode_g<8, PREP>(a, G, xf32, s)
+                       : launch_decode_g<16, PREP>(a, G, xf32, s);
 }
 
 // the (hd, query heads per KV head) pairs with an instance: G * hd / 32 <= 32 values per lane
@@ -679,46 +767,54 @@ size_t g4b_attn_workspace_bytes(int nH, int nkv, int hd, int max_T) {
     clear_error();
     const int S = attn_splits(nkv, max_T, sms);
     if (S == 1) return 0;
-    return (size_t)nH * S * (hd + 2) * sizeof(float);
+    return attn_ws_counters(nkv) + (size_t)nH * S * (hd + 2) * sizeof(float);
 }
 
-int g4b_attn_decode(const void* qkv, int dtype, const float* qnw, const float* cos_t, const float* sin_t,
-                    const uint16_t* kc, const uint16_t* vc, void* out, int out_dtype, int nH, int nkv, int hd,
-                    int qoff, int stride, int window, const int* pos_dev, void* workspace, size_t ws_bytes,
-                    g4b_stream_t stream) {
-    G4B_ENTRY("attn_decode");
-    G4B_REQUIRE(qkv && qnw && cos_t && sin_t && kc && vc && out && pos_dev, G4B_E_ARG, "attn_decode: NULL pointer");
-    G4B_REQUIRE(dtype == G4B_DT_F32 || dtype == G4B_DT_F16, G4B_E_ARG, "attn_decode: bad dtype %d", dtype);
-    G4B_REQUIRE(out_dtype == G4B_DT_F32 || out_dtype == G4B_DT_F16, G4B_E_ARG, "attn_decode: bad out_dtype %d",
+}  // extern "C"
+
+// g4b_attn_decode and g4b_attn_decode_prepkv: the checks and the launches; knw != nullptr fuses prepkv
+static int attn_decode_impl(const char* op, const void* qkv, int dtype, const float* qnw, const float* knw,
+                            const float* cos_t, const float* sin_t, const uint16_t* kc, const uint16_t* vc, void* out,
+                            int out_dtype, int nH, int nkv, int hd, int qoff, int koff, int voff, int keqv, int stride,
+                            int window, const int* pos_dev, void* workspace, size_t ws_bytes, g4b_stream_t stream) {
+    G4B_REQUIRE(qkv && qnw && cos_t && sin_t && kc && vc && out && pos_dev, G4B_E_ARG, "%s: NULL pointer", op);
+    G4B_REQUIRE(dtype == G4B_DT_F32 || dtype == G4B_DT_F16, G4B_E_ARG, "%s: bad dtype %d", op, dtype);
+    G4B_REQUIRE(out_dtype == G4B_DT_F32 || out_dtype == G4B_DT_F16, G4B_E_ARG, "%s: bad out_dtype %d", op,
                 out_dtype);
-    G4B_REQUIRE(nkv >= 1 && nH >= nkv && nH % nkv == 0 && stride >= 1 && window >= 0 && window <= stride && qoff >= 0,
-                G4B_E_SHAPE, "attn_decode: nH=%d nkv=%d stride=%d window=%d", nH, nkv, stride, window);
+    G4B_REQUIRE(nkv >= 1 && nH >= nkv && nH % nkv == 0 && stride >= 1 && window >= 0 && window <= stride && qoff >= 0 &&
+                    koff >= 0 && voff >= 0,
+                G4B_E_SHAPE, "%s: nH=%d nkv=%d stride=%d window=%d", op, nH, nkv, stride, window);
     const int G = nH / nkv;
     G4B_REQUIRE(attn_shape_ok(hd, G), G4B_E_SHAPE,
-                "attn_decode: hd=%d with %d query heads per KV head (hd 128: 1-8, hd 256: 1-4, hd 512: 1-2)", hd,
-                G);
+                "%s: hd=%d with %d query heads per KV head (hd 128: 1-8, hd 256: 1-4, hd 512: 1-2)", op, hd, G);
     const bool xf32 = dtype == G4B_DT_F32;
     const size_t esz = xf32 ? 4 : 2;
     G4B_REQUIRE(aligned16(kc) && aligned16(vc) && aligned16((const char*)qkv + (size_t)qoff * esz) && aligned16(out),
-                G4B_E_ALIGN, "attn_decode: qkv + qoff, the caches and out must be 16-byte aligned");
+                G4B_E_ALIGN, "%s: qkv + qoff, the caches and out must be 16-byte aligned", op);
     int sms = 148;
     int st = check_device(&sms);
     if (st != G4B_OK) return st;
     const int max_T = window > 0 ? window : stride;
     const int S = attn_splits(nkv, max_T, sms);
-    const size_t need = S == 1 ? 0 : (size_t)nH * S * (hd + 2) * sizeof(float);
+    const size_t cbytes = attn_ws_counters(nkv);
+    const size_t need = S == 1 ? 0 : cbytes + (size_t)nH * S * (hd + 2) * sizeof(float);
     G4B_REQUIRE(ws_bytes >= need && (need == 0 || (workspace && aligned16(workspace))), G4B_E_WORKSPACE,
-                "attn_decode: needs a 16-byte aligned workspace of %zu bytes, got %zu", need, ws_bytes);
+                "%s: needs a 16-byte aligned, zero-initialised workspace of %zu bytes, got %zu", op, need, ws_bytes);
     AttnArgs a{};
     a.qkv = qkv;
     a.qnw = qnw;
+    a.knw = knw;
+    a.koff = koff;
+    a.voff = keqv ? koff : voff;
     a.cos_t = cos_t;
     a.sin_t = sin_t;
     a.kc = kc;
     a.vc = vc;
     a.out = out;
-    a.part = S > 1 ? reinterpret_cast<float*>(workspace) : nullptr;
-    a.pml = S > 1 ? reinterpret_cast<float*>(workspace) + (size_t)nH * S * hd : nullptr;
+    char* wsb = reinterpret_cast<char*>(workspace);
+    a.arrive = S > 1 ? reinterpret_cast<unsigned*>(wsb) : nullptr;
+    a.part = S > 1 ? reinterpret_cast<float*>(wsb + cbytes) : nullptr;
+    a.pml = S > 1 ? reinterpret_cast<float*>(wsb + cbytes) + (size_t)nH * S * hd : nullptr;
     a.pos_dev = pos_dev;
     a.nH = nH;
     a.nkv = nkv;
@@ -729,16 +825,31 @@ int g4b_attn_decode(const void* qkv, int dtype, const float* qnw, const float* c
     a.S = S;
     a.out_f32 = out_dtype == G4B_DT_F32;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = hd == 128 ? launch_decode_g<4>(a, G, xf32, s)
-                  : hd == 256 ? launch_decode_g<8>(a, G, xf32, s)
-                              : launch_decode_g<16>(a, G, xf32, s);
-    if (e != cudaSuccess) return fail(G4B_E_CUDA, "attn_decode: launch: %s", cudaGetErrorString(e));
+    cudaError_t e = knw ? launch_decode_hd<true>(a, G, xf32, s) : launch_decode_hd<false>(a, G, xf32, s);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "%s: launch: %s", op, cudaGetErrorString(e));
     count_launch();
-    if (S > 1) {
-        attn_combine_kernel<<<nH, kAttnThreads, (size_t)S * sizeof(float), s>>>(a);
-        count_launch();
-    }
-    return launch_status("attn_decode");
+    return launch_status(op);
+}
+
+extern "C" {
+
+int g4b_attn_decode(const void* qkv, int dtype, const float* qnw, const float* cos_t, const float* sin_t,
+                    const uint16_t* kc, const uint16_t* vc, void* out, int out_dtype, int nH, int nkv, int hd,
+                    int qoff, int stride, int window, const int* pos_dev, void* workspace, size_t ws_bytes,
+                    g4b_stream_t stream) {
+    G4B_ENTRY("attn_decode");
+    return attn_decode_impl("attn_decode", qkv, dtype, qnw, nullptr, cos_t, sin_t, kc, vc, out, out_dtype, nH, nkv, hd,
+                            qoff, 0, 0, 0, stride, window, pos_dev, workspace, ws_bytes, stream);
+}
+
+int g4b_attn_decode_prepkv(const void* qkv, int dtype, const float* qnw, const float* knw, const float* cos_t,
+                           const float* sin_t, uint16_t* kc, uint16_t* vc, void* out, int out_dtype, int nH, int nkv,
+                           int hd, int qoff, int koff, int voff, int keqv, int stride, int window, const int* pos_dev,
+                           void* workspace, size_t ws_bytes, g4b_stream_t stream) {
+    G4B_ENTRY("attn_decode_prepkv");
+    G4B_REQUIRE(knw, G4B_E_ARG, "attn_decode_prepkv: NULL knw");
+    return attn_decode_impl("attn_decode_prepkv", qkv, dtype, qnw, knw, cos_t, sin_t, kc, vc, out, out_dtype, nH, nkv,
+                            hd, qoff, koff, voff, keqv, stride, window, pos_dev, workspace, ws_bytes, stream);
 }
 
 int g4b_attn_prefill_prepkv(const void* k, const void* v, int dtype, int row_stride, int M, const float* knw,

@@ -1159,6 +1159,10 @@ __device__ __forceinline__ void load8(const void* p, int r0, float (&v)[8]) {
     }
 }
 
+// A chain stage's f16 x slice: 32-row block b at bytes [128 b, 128 b + 64), repeated at +64, so the
+// consumers read a block's words from any rotation without wrapping.  Lane l holds rows 8l .. 8l+7.
+__device__ __forceinline__ int chain_xoff16(int lane) { return (lane >> 2) * 128 + (lane & 3) * 16; }
+
 // a lane's 8 activations into a stage's x slice (rows 8*lane .. +8), in the chain's x dtype
 template <bool F32>
 __device__ __forceinline__ void store8(uint8_t* dst, int lane, const float (&v)[8]) {
@@ -1172,7 +1176,8 @@ __device__ __forceinline__ void store8(uint8_t* dst, int lane, const float (&v)[
         h.y = pack_half2(__float2half_rn(v[2]), __float2half_rn(v[3]));
         h.z = pack_half2(__float2half_rn(v[4]), __float2half_rn(v[5]));
         h.w = pack_half2(__float2half_rn(v[6]), __float2half_rn(v[7]));
-        *reinterpret_cast<uint4*>(dst + 16 * lane) = h;
+        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane)) = h;
+        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane) + 64) = h;
     }
 }
 
@@ -1496,9 +1501,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                     store8<XF32>(dst, lane, v);
                 } else if (xreg < 0) {
                     const uint8_t* src = x + (size_t)o * kM1Rows * esz;
-                    #pragma unroll
-                    for (int b = lane * 16; b < kM1Rows * esz; b += 512)
-                        *reinterpret_cast<uint4*>(dst + b) = __ldcg(reinterpret_cast<const uint4*>(src + b));
+                    if constexpr (XF32) {
+                        #pragma unroll
+                        for (int b = lane * 16; b < kM1Rows * esz; b += 512)
+                            *reinterpret_cast<uint4*>(dst + b) = __ldcg(reinterpret_cast<const uint4*>(src + b));
+                    } else {
+                        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src + lane * 16));
+                        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane)) = v;
+                        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane) + 64) = v;
+                    }
                 } else {
                     // rows o*256 + 8*lane .. +8: the world ranks' words, polled until they carry this
                     // run's epoch (bounded), summed in rank order.  A rank's 8 words are loaded at once
@@ -1734,7 +1745,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         const float4 v1 = *reinterpret_cast<const float4*>(xs + lane * 32 + 16);
                         xsum = ((((((v0.x + v0.y) + v0.z) + v0.w) + v1.x) + v1.y) + v1.z) + v1.w;
                     } else {
-                        const uint4 v = *reinterpret_cast<const uint4*>(xs + lane * 16);
+                        const uint4 v = *reinterpret_cast<const uint4*>(xs + chain_xoff16(lane));
                         xsum = ((((((h_lo(v.x) + h_hi(v.x)) + h_lo(v.y)) + h_hi(v.y)) + h_lo(v.z)) + h_hi(v.z)) + h_lo(v.w)) +
                                h_hi(v.w);
                     }
@@ -1746,13 +1757,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         const int lblk = XF32 ? 4 * pass + lq : lq + 4 * lh;
                         const int lrot = RMUL * lds + 2 * lq + le + ((XF32 && lh) ? 2 : 0);
                         const uint32_t lbase = st_u + (uint32_t)(lblk * 32 * 128);
-                        // row offsets for the 4 step phases (steps p = 4m + d advance the row by 8m (f16) / 16m (f32))
-                        uint32_t roff[4], swz[4];
+                        // the ldmatrix offset of each step pair p (p = 4m + d advances the row by 8m (f16) / 16m
+                        // (f32)), rotated and swizzled once here so the loop adds only the stage base
+                        uint32_t aoff[NSTEP / 2];
                         #pragma unroll
-                        for (int d = 0; d < 4; d++) {
+                        for (int p = 0; p < NSTEP; p += 2) {
+                            const int d = p & 3, mrow = (p >> 2) * (RMUL == 2 ? 1024 : 2048);
                             const int r = (RMUL * d + lrot) & 31;
-                            roff[d] = (uint32_t)(r * 128);
-                            swz[d] = (uint32_t)((seg ^ (r & 7)) << 4);
+                            aoff[p / 2] = ((uint32_t)(r * 128 + mrow) & 4095u) | (uint32_t)((seg ^ (r & 7)) << 4);
                         }
                         // B-fragment sources: lanes that feed zeros read a zeroed area instead
                         uint32_t xb0, xb1, xoff;
@@ -1762,17 +1774,19 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                             xb1 = xb0;
                             xoff = (uint32_t)(8 * q);
                         } else {
-                            xb0 = g == q ? smem_u32(xs) + (uint32_t)(q * 64) : smem_u32(s_zero);
-                            xb1 = g == q + 4 ? smem_u32(xs) + (uint32_t)((q + 4) * 64) : smem_u32(s_zero);
-                            xoff = (uint32_t)(4 * q);
+                            // each 32-row block of x sits twice in a row (128 bytes), so the rotated
+                            // word (q + pp) is read at a constant offset from here: no wrap to compute
+                            xb0 = (g == q ? smem_u32(xs) + (uint32_t)(q * 128) : smem_u32(s_zero)) + (uint32_t)(4 * q);
+                            xb1 = (g == q + 4 ? smem_u32(xs) + (uint32_t)((q + 4) * 128) : smem_u32(s_zero)) +
+                                  (uint32_t)(4 * q);
+                            xoff = 0u;
                         }
                         float C[2][4];
                         #pragma unroll
                         for (int k = 0; k < 2; k++) C[k][0] = C[k][1] = C[k][2] = C[k][3] = 0.f;
                         #pragma unroll
                         for (int p = 0; p < NSTEP; p += 2) {
-                            const int d = p & 3, mrow = (p >> 2) * (RMUL == 2 ? 1024 : 2048);
-                            const uint32_t addr = lbase + (((roff[d] + (uint32_t)mrow) & 4095u) | swz[d]);
+                            const uint32_t addr = lbase + aoff[p / 2];
                             uint32_t ra0, rb0, ra1, rb1;
                             ldsm_x4_trans(addr, ra0, rb0, ra1, rb1);
                             #pragma unroll
@@ -1789,9 +1803,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                                     b0 = split_pair(xa.x, xa.y, lo);
                                     b1 = split_pair(xb.x, xb.y, lo);
                                 } else {
-                                    const uint32_t o = (xoff + 4u * pp) & 63u;
-                                    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(xb0 + o));
-                                    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(xb1 + o));
+                                    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(xb0 + 4u * pp));
+                                    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(xb1 + 4u * pp));
                                 }
                                 const uint32_t RA8 = RA >> 8, RB8 = RB >> 8;
                                 mma_16816(C[0], RA & 0x000F000Fu, RA8 & 0x000F000Fu, RB & 0x000F000Fu, RB8 & 0x000F000Fu, b0, b1);
@@ -3459,7 +3472,8 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
             if (st != G4B_OK) return st;
         }
     }
-    const int stage_bytes = (kM1WBytes + 8 * kStTN * ssz + kM1Rows * (xf32 ? 4 : 2) + 1023) & ~1023;
+    // x slice: f32, or f16 stored twice over (each block repeated, see chain_xoff16): 1 KB either way
+    const int stage_bytes = (kM1WBytes + 8 * kStTN * ssz + kM1Rows * 4 + 1023) & ~1023;
     const size_t smem = (size_t)kM1Stages * stage_bytes + 1024;
     int resident = 0;
     st = chain_prepare(xf32, scale_fmt, y_dtype == G4B_DT_F32, smem, &resident);

@@ -84,6 +84,8 @@ SIGNATURES = {
     "g4b_attn_prepkv": (_I, [_P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "g4b_attn_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g4b_attn_decode": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P]),
+    "g4b_attn_decode_prepkv": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I,
+                                    _P, _P, _Z, _P]),
     "g4b_attn_prefill_prepkv": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "g4b_attn_prefill": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "g4b_gemv_chain_workspace_bytes": (_Z, [_P]),

@@ -459,6 +459,32 @@ def attn_decode(qkv: torch.Tensor, qnw: torch.Tensor, cos_t: torch.Tensor, sin_t
     return out
 
 
+def attn_decode_prepkv(qkv: torch.Tensor, qnw: torch.Tensor, knw: torch.Tensor, cos_t: torch.Tensor,
+                       sin_t: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, pos: torch.Tensor, nH: int, nkv: int,
+                       hd: int, koff: int, voff: int, keqv: bool = False, qoff: int = 0, window: int = 0,
+                       out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float32,
+                       stream: Optional[torch.cuda.Stream] = None,
+                       workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """vk/prepkv.comp then vk/attn.comp in one launch: this token's k / v into the caches, then its
+    attention over them."""
+    for t, n in ((qkv, "qkv"), (qnw, "qnw"), (knw, "knw"), (cos_t, "cos"), (sin_t, "sin"), (kc, "kc"), (vc, "vc"),
+                 (pos, "pos")):
+        _need(t, n)
+    stride = kc.shape[1]
+    if out is None:
+        out = torch.empty((nH * hd,), dtype=out_dtype, device=qkv.device)
+    sh = _stream_handle(stream, qkv.device)
+    need = attn_workspace_bytes(nH, nkv, hd, window if window > 0 else stride)
+    ws = workspace
+    if need and ws is None:
+        ws = WORKSPACES.get(qkv.device, sh, need, use="attn")
+    L.check("g4b_attn_decode_prepkv", L.load().g4b_attn_decode_prepkv(
+        _ptr(qkv), _DT[qkv.dtype], _ptr(qnw), _ptr(knw), _ptr(cos_t), _ptr(sin_t), _ptr(kc), _ptr(vc), _ptr(out),
+        _DT[out.dtype], nH, nkv, hd, qoff, koff, voff, 1 if keqv else 0, stride, window, _ptr(pos), _ptr(ws),
+        ws.numel() if ws is not None else 0, sh))
+    return out
+
+
 def attn_prefill_prepkv(k: torch.Tensor, v: torch.Tensor, knw: torch.Tensor, cosM: torch.Tensor, sinM: torch.Tensor,
                         kc: torch.Tensor, vc: torch.Tensor, p0: torch.Tensor, nkv: int, hd: int, window: int = 0,
                         stream: Optional[torch.cuda.Stream] = None) -> None:

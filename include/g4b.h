@@ -394,7 +394,9 @@ G4B_API int g4b_attn_prepkv(const void* qkv, int dtype, const float* knw, const 
                             int window, const int* pos_dev, g4b_stream_t stream);
 
 /* Workspace bytes g4b_attn_decode needs for a cache of max_T keys (window, or stride for
- * full-attention layers); 0 when the keys are not split. */
+ * full-attention layers); 0 when the keys are not split.  The workspace starts with one arrival
+ * counter per KV head: zero-initialise it once; every call leaves the counters at zero, and calls
+ * that share a workspace must be ordered (one stream). */
 G4B_API size_t g4b_attn_workspace_bytes(int nH, int nkv, int hd, int max_T);
 
 /* Decode attention for one token, vk/attn.comp:15-55 (the attn dispatch, src/vk_engine.py:282):
@@ -402,13 +404,23 @@ G4B_API size_t g4b_attn_workspace_bytes(int nH, int nkv, int hd, int max_T);
  *   q = RoPE(rmsnorm(qkv[qoff + h*hd ..], qnw)),  T = window ? min(pos + 1, window) : pos + 1,
  *   out[h*hd + i] = sum_{j < T} softmax_j(q . k_j) v_j[i]            (no 1/sqrt(hd) scale, as the shader)
  * over the cached keys (slots 0 .. T-1).  The keys are split over the SMs (flash decoding): a
- * split's softmax partial goes to `workspace` and a second kernel combines the splits.
+ * split's softmax partial goes to `workspace` and the last split of each KV head to finish
+ * combines them (one launch).
  * Shapes: hd 128 (up to 8 query heads per KV head), 256 (up to 4) or 512 (up to 2).
  * out [nH, hd] f32 or f16. */
 G4B_API int g4b_attn_decode(const void* qkv, int dtype, const float* qnw, const float* cos_t, const float* sin_t,
                             const uint16_t* kc, const uint16_t* vc, void* out, int out_dtype, int nH, int nkv,
                             int hd, int qoff, int stride, int window, const int* pos_dev, void* workspace,
                             size_t ws_bytes, g4b_stream_t stream);
+
+/* The engine's prepkv and attn dispatches for one decode token in one launch: what
+ * g4b_attn_prepkv then g4b_attn_decode compute, with the token's k / v written by the
+ * CTA whose key split holds its slot before that CTA reads it.  Arguments as those two calls'. */
+G4B_API int g4b_attn_decode_prepkv(const void* qkv, int dtype, const float* qnw, const float* knw,
+                                   const float* cos_t, const float* sin_t, uint16_t* kc, uint16_t* vc, void* out,
+                                   int out_dtype, int nH, int nkv, int hd, int qoff, int koff, int voff, int keqv,
+                                   int stride, int window, const int* pos_dev, void* workspace, size_t ws_bytes,
+                                   g4b_stream_t stream);
 
 /* KV-cache write for a prefill chunk, vk/pre_prepkv.comp:15-30 (src/vk_engine.py:416): token m of
  * M (position *p0_dev + m) writes what g4b_attn_prepkv writes for one token, from its own rows
