@@ -194,6 +194,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attn_decode_kernel(const Attn
     __shared__ float xacc[kAttnWarps][G][HD];   // every warp's partial, merged by all threads
     __shared__ float xm[kAttnWarps][G], xl[kAttnWarps][G];
     const int s = blockIdx.x, kvh = blockIdx.y, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    // launched as a programmatic dependent: scheduled while the kernel before it (the chain that wrote
+    // q|k|v) finishes; nothing is read before that kernel has completed
+    pdl_launch_dependents();
+    pdl_wait();
     const int pos = __ldg(a.pos_dev);
     const int T = min(a.window > 0 ? min(pos + 1, a.window) : pos + 1, a.stride);   // never past the cache
     const int k0 = (int)((long long)s * T / a.S), k1 = (int)((long long)(s + 1) * T / a.S);
@@ -389,12 +393,20 @@ static int attn_splits(int nkv, int max_T, int sms) {
     return std::max(1, std::min(std::min(by_keys, by_sms), kAttnMaxSplits));
 }
 
+// as a programmatic dependent of the previous kernel (the kernel waits for it before reading anything)
 template <int D, int G, bool PREP>
 static cudaError_t launch_decode(const AttnArgs& a, bool xf32, cudaStream_t s) {
-    const dim3 grid(a.S, a.nkv);
-    if (xf32) attn_decode_kernel<D, G, true, PREP><<<grid, kAttnThreads, 0, s>>>(a);
-    else attn_decode_kernel<D, G, false, PREP><<<grid, kAttnThreads, 0, s>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(a.S, a.nkv);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return xf32 ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, G, true, PREP>, a)
+                : cudaLaunchKernelEx(&cfg, attn_decode_kernel<D, G, false, PREP>, a);
 }
 
 template <int D, bool PREP>

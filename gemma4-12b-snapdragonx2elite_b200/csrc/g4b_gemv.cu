@@ -1291,6 +1291,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
     if (tid < 32) s_zero[tid] = 0u;
     if (tid < kStepWords) reinterpret_cast<uint32_t*>(&s_step[0])[tid] = __ldg(reinterpret_cast<const uint32_t*>(ch.steps) + tid);
     if (tid < ch.world && ch.peers) s_peers[tid] = ch.peers[tid];
+    // a programmatic dependent launched after this chain may be scheduled now (it waits for our completion)
+    pdl_launch_dependents();
     __syncthreads();
 
     if (warp == pw) {
@@ -1380,7 +1382,11 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
             }
         }
     } else if (warp == pw + 1) {
-        // x slices by plain loads (L2, not L1: x was written by other SMs during this launch)
+        // x slices by plain loads (L2, not L1: x was written by other SMs during this launch).  Launched as a
+        // programmatic dependent (G4B_CHAIN_RUN_PDL), the chain streams weights from its start, and only
+        // this warp -- whose loads are the first reads of anything an earlier kernel wrote -- waits for the
+        // kernel before it; every write of the chain follows these loads.
+        pdl_wait();
         int i = 0;
         bool stop = false;
         for (int j = 0; j < nsteps && !stop; j++) {
@@ -3194,28 +3200,30 @@ static int chain_prepare(bool xf32, int sfmt, bool yf32, size_t smem, int* resid
 }
 
 template <bool XF32, int SFMT, bool YF32>
-static cudaError_t chain_launch_kernel(const g4b_gemv_chain* c, const ChainArgs& ch, cudaStream_t s) {
+static cudaError_t chain_launch_kernel(const g4b_gemv_chain* c, const ChainArgs& ch, bool pdl, cudaStream_t s) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(c->grid);
     cfg.blockDim = dim3(kChainThreads);
     cfg.dynamicSmemBytes = c->smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the steps wait on one another
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, gemv_i4_chain_kernel<XF32, SFMT, YF32>, ch);
 }
 
-static cudaError_t chain_launch(const g4b_gemv_chain* c, const ChainArgs& ch, cudaStream_t s) {
+static cudaError_t chain_launch(const g4b_gemv_chain* c, const ChainArgs& ch, bool pdl, cudaStream_t s) {
     const bool xf32 = c->x_dtype == G4B_DT_F32, yf32 = c->y_dtype == G4B_DT_F32;
     if (xf32) {
-        if (c->scale_fmt == G4B_SCALE_F16) return yf32 ? chain_launch_kernel<true, G4B_SCALE_F16, true>(c, ch, s) : chain_launch_kernel<true, G4B_SCALE_F16, false>(c, ch, s);
-        return yf32 ? chain_launch_kernel<true, G4B_SCALE_E4M3, true>(c, ch, s) : chain_launch_kernel<true, G4B_SCALE_E4M3, false>(c, ch, s);
+        if (c->scale_fmt == G4B_SCALE_F16) return yf32 ? chain_launch_kernel<true, G4B_SCALE_F16, true>(c, ch, pdl, s) : chain_launch_kernel<true, G4B_SCALE_F16, false>(c, ch, pdl, s);
+        return yf32 ? chain_launch_kernel<true, G4B_SCALE_E4M3, true>(c, ch, pdl, s) : chain_launch_kernel<true, G4B_SCALE_E4M3, false>(c, ch, pdl, s);
     }
-    if (c->scale_fmt == G4B_SCALE_F16) return yf32 ? chain_launch_kernel<false, G4B_SCALE_F16, true>(c, ch, s) : chain_launch_kernel<false, G4B_SCALE_F16, false>(c, ch, s);
-    return yf32 ? chain_launch_kernel<false, G4B_SCALE_E4M3, true>(c, ch, s) : chain_launch_kernel<false, G4B_SCALE_E4M3, false>(c, ch, s);
+    if (c->scale_fmt == G4B_SCALE_F16) return yf32 ? chain_launch_kernel<false, G4B_SCALE_F16, true>(c, ch, pdl, s) : chain_launch_kernel<false, G4B_SCALE_F16, false>(c, ch, pdl, s);
+    return yf32 ? chain_launch_kernel<false, G4B_SCALE_E4M3, true>(c, ch, pdl, s) : chain_launch_kernel<false, G4B_SCALE_E4M3, false>(c, ch, pdl, s);
 }
 
 }  // namespace g4b
@@ -3535,7 +3543,13 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
 size_t g4b_gemv_chain_workspace_bytes(const g4b_gemv_chain* chain) { return chain ? chain->ws_bytes : 0; }
 
 int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_bytes, g4b_stream_t stream) {
+    return g4b_gemv_chain_run_ex(chain, workspace, ws_bytes, 0u, stream);
+}
+
+int g4b_gemv_chain_run_ex(const g4b_gemv_chain* chain, void* workspace, size_t ws_bytes, unsigned flags,
+                          g4b_stream_t stream) {
     G4B_ENTRY("gemv_chain_run");
+    G4B_REQUIRE((flags & ~G4B_CHAIN_RUN_PDL) == 0u, G4B_E_ARG, "gemv_chain_run: unknown flags 0x%x", flags);
     G4B_REQUIRE(chain && chain->plan, G4B_E_ARG, "gemv_chain_run: NULL chain");
     G4B_REQUIRE(workspace && ws_bytes >= chain->ws_bytes, G4B_E_WORKSPACE,
                 "gemv_chain_run: needs %zu bytes of workspace, got %zu", chain->ws_bytes, workspace ? ws_bytes : 0);
@@ -3562,7 +3576,7 @@ int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_b
     ch.rank = chain->rank;
     ch.world = chain->world;
     ch.pf_items = chain->pf_items;
-    cudaError_t e = chain_launch(chain, ch, reinterpret_cast<cudaStream_t>(stream));
+    cudaError_t e = chain_launch(chain, ch, (flags & G4B_CHAIN_RUN_PDL) != 0u, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemv_chain_run: launch: %s", cudaGetErrorString(e));
     count_launch();
     return launch_status("gemv_chain_run");

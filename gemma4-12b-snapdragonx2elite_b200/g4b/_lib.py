@@ -25,6 +25,7 @@ G4B_E_TIMEOUT = -8
 
 GEMV_PDL = 1
 CHAIN_ALLREDUCE = 1
+CHAIN_RUN_PDL = 1
 DT_F32 = 0
 DT_F16 = 1
 SCALE_F16 = 0
@@ -90,6 +91,7 @@ SIGNATURES = {
     "g4b_attn_prefill": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "g4b_gemv_chain_workspace_bytes": (_Z, [_P]),
     "g4b_gemv_chain_run": (_I, [_P, _P, _Z, _P]),
+    "g4b_gemv_chain_run_ex": (_I, [_P, _P, _Z, C.c_uint, _P]),
     "g4b_gemv_chain_destroy": (None, [_P]),
 }
 

@@ -197,11 +197,13 @@ class SegmentedDecodeToken:
     def logits(self) -> torch.Tensor:
         return self.bufs["logits"]
 
-    def run(self, stream: Optional[torch.cuda.Stream], attention) -> None:
+    def run(self, stream: Optional[torch.cuda.Stream], attention, pdl: bool = True) -> None:
+        """pdl: each segment after the first is a programmatic dependent of the attention before it, so
+        its weights start streaming while attention runs (G4B_CHAIN_RUN_PDL); the results are the same."""
         self.chains[0].run(stream)
         for li, ch in enumerate(self.chains[1:]):
             attention(li, stream)
-            ch.run(stream)
+            ch.run(stream, pdl=pdl)
 
     def close(self) -> None:
         for ch in self.chains:

@@ -272,12 +272,14 @@ class GemvChain:
         self.workspace_bytes = int(self.lib.g4b_gemv_chain_workspace_bytes(self.handle))
         self.workspace = torch.zeros(self.workspace_bytes + 256, dtype=torch.uint8, device=self.device)
 
-    def run(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+    def run(self, stream: Optional[torch.cuda.Stream] = None, pdl: bool = False) -> None:
+        """pdl: launch as a programmatic dependent of the previous kernel on the stream
+        (G4B_CHAIN_RUN_PDL): the weights stream while that kernel finishes."""
         if self.handle is None:
             raise RuntimeError("GemvChain: closed")
         sh = _stream_handle(stream, self.device)
-        L.check("g4b_gemv_chain_run", self.lib.g4b_gemv_chain_run(
-            self.handle, _ptr(self.workspace), self.workspace.numel(), sh))
+        L.check("g4b_gemv_chain_run", self.lib.g4b_gemv_chain_run_ex(
+            self.handle, _ptr(self.workspace), self.workspace.numel(), L.CHAIN_RUN_PDL if pdl else 0, sh))
 
     def close(self) -> None:
         if getattr(self, "handle", None) is not None:

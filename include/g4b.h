@@ -274,6 +274,18 @@ G4B_API int g4b_gemv_chain_create_fused(const g4b_gemv_chain_step* steps, const 
                                         int x_dtype, int scale_fmt, int y_dtype, g4b_gemv_chain** chain);
 G4B_API size_t g4b_gemv_chain_workspace_bytes(const g4b_gemv_chain* chain);
 G4B_API int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_bytes, g4b_stream_t stream);
+/* g4b_gemv_chain_run with launch flags:
+ *   G4B_CHAIN_RUN_PDL  programmatic dependent launch: the chain may start while
+ *                      the previous kernel in `stream` is still running and
+ *                      begins streaming its weights at once; it reads its first
+ *                      x, and writes anything, only after that kernel has
+ *                      completed.  For a decode token split at attention: the
+ *                      next layer's weights stream while attention runs.  The
+ *                      chain itself lets a programmatic dependent after it
+ *                      start early (g4b_attn_decode* is launched that way). */
+#define G4B_CHAIN_RUN_PDL 1u
+G4B_API int g4b_gemv_chain_run_ex(const g4b_gemv_chain* chain, void* workspace, size_t ws_bytes, unsigned flags,
+                                  g4b_stream_t stream);
 G4B_API void g4b_gemv_chain_destroy(g4b_gemv_chain* chain);
 
 /* Split-K partial reduction, vk/reduce.comp:8-12:

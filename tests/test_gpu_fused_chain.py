@@ -113,3 +113,40 @@ def test_fused_chain_rejects_a_norm_on_a_vector_the_step_before_did_not_write():
         ops.GemvChain(steps, xforms=xf, x_dtype=torch.float16)
     assert e.value.code == L.G4B_E_ARG and "NORMADD" in str(e.value)
     assert L.query(L.Q_LAUNCHES) == before
+
+
+@pytest.mark.parametrize("pdl", [False, True])
+def test_segmented_token_equals_the_fused_token(pdl):
+    """The token split at attention (one chain launch per layer, g4b.decode.SegmentedDecodeToken) with
+    an attention stand-in that hands q on (what the fused token's o step reads) gives the fused token's
+    bits: each step's partition and arithmetic are the same.  pdl: the segments are programmatic
+    dependents of the kernel before them (G4B_CHAIN_RUN_PDL), eager and in a graph."""
+    host, dev, dnorms, lm, finw, h0 = _model(False, seed=5)
+    lmd = ops.to_device(lm, "cuda")
+    fw = torch.from_numpy(finw).cuda()
+    fused = decode.FusedDecodeToken(dev, dnorms, lmd, fw, dtype=torch.float16)
+    seg = decode.SegmentedDecodeToken(dev, dnorms, lmd, fw, dtype=torch.float16)
+    fused.h0.copy_(torch.from_numpy(h0))
+    seg.h0.copy_(torch.from_numpy(h0))
+    s = torch.cuda.Stream()
+
+    def attention(li, stream):
+        with torch.cuda.stream(stream):
+            seg.bufs["attn"].copy_(seg.bufs["q"])
+
+    with torch.cuda.stream(s):
+        fused.run(s)
+        seg.run(s, attention, pdl=pdl)
+        eager = seg.logits.clone()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            seg.run(s, attention, pdl=pdl)
+        seg.logits.zero_()
+        g.replay()
+    s.synchronize()
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+    assert torch.equal(eager, fused.logits), (eager.float() - fused.logits.float()).abs().max()
+    assert torch.equal(seg.logits, fused.logits)
+    del g
+    fused.close()
+    seg.close()
