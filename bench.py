@@ -1212,10 +1212,12 @@ def measure_engine(c, args):
     and flash-decode attention in one launch (g4b_attn_decode_prepkv) over a
     synthetic f16 cache (GQA, 16 query and 8 KV heads of 256), timed as K
     graph replays at a fixed context (the reference grows it by 64 tokens).
-    Prefill runs the W4A16 GEMMs (and, as PREFILL_I8 does, cast_i8 + the W8A8
-    GEMMs) over the 2048-token prompt in one batch; its attention and its norms
-    and gelu*up over [T, H] rows are torch stand-ins (prefill attention,
-    vk/pre_attn.comp, is not built here).  The logits are for the last token."""
+    Prefill is all g4b too, over the 2048-token prompt in one batch: the row
+    norms and gelu*up (g4b_rows_*, g4b_gelumul), the W4A16 GEMMs (or, as
+    PREFILL_I8 does, cast_i8 + the W8A8 GEMMs), and the batched KV-cache write
+    and causal attention (g4b_attn_prefill_prepkv, g4b_attn_prefill); a third
+    key swaps torch's SDPA in for the attention, for comparison.  The logits
+    are for the last token."""
     torch = c.torch
     F = torch.nn.functional
     from g4b import decode
@@ -1238,8 +1240,8 @@ def measure_engine(c, args):
     nw = lambda: (1.0 + 0.1 * torch.randn((H,), generator=gen, device=c.device))  # noqa: E731
     norms = [decode.LayerNorms(inw=nw(), paw=nw(), pfw=nw(), ofw=nw(), scl=1.0) for _ in range(args.layers)]
     finw = nw()
-    out = {"attention": "decode: g4b_attn_decode_prepkv (GQA 16/8 heads of 256, f16 KV cache); "
-                        "prefill: torch scaled_dot_product_attention stand-in",
+    out = {"attention": "decode: g4b_attn_decode_prepkv; prefill: g4b_attn_prefill_prepkv + g4b_attn_prefill "
+                        "(GQA 16/8 heads of 256, f16 KV cache)",
            "steps": args.steps}
     # ---- decode
     tok = decode.SegmentedDecodeToken(layers_d, norms, lm, finw, dtype=torch.float16)
@@ -1277,9 +1279,6 @@ def measure_engine(c, args):
     sa = torch.empty((T,), dtype=torch.float32, device=c.device)
     lib = c.L.load()
 
-    def rms(x, w):
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + decode.EPS) * w
-
     def mm(x16, w, i8):
         if not i8:
             return c.ops.gemm_i4(x16, w, out_dtype=torch.float16, stream=c.stream)
@@ -1288,36 +1287,61 @@ def measure_engine(c, args):
                                                  c.sh))
         return c.ops.gemm_w8a8(A8.view(-1)[:M_ * K_].view(M_, K_), sa[:M_], w, stream=c.stream)
 
-    def prefill(i8):
-        h = X0
-        for dd, nm in zip(layers_w, norms):
-            x = rms(h, nm.inw).half()
-            q, k, v = mm(x, dd["q"], i8), mm(x, dd["k"], i8), mm(x, dd["v"], i8)
-            a = F.scaled_dot_product_attention(q.view(T, NH, HEAD_DIM).transpose(0, 1)[None],
-                                               k.view(T, NKV_HEADS, HEAD_DIM).transpose(0, 1)[None],
-                                               v.view(T, NKV_HEADS, HEAD_DIM).transpose(0, 1)[None],
-                                               is_causal=True, enable_gqa=True)
-            o = mm(a[0].transpose(0, 1).reshape(T, NQ).contiguous(), dd["o"], i8)
-            h = h + rms(o.float(), nm.paw)
-            x2 = rms(h, nm.pfw).half()
-            g, u = mm(x2, dd["gate"], i8), mm(x2, dd["up"], i8)
-            act = (F.gelu(g.float(), approximate="tanh") * u.float()).half()
-            h = (h + rms(mm(act, dd["down"], i8).float(), nm.ofw)) * nm.scl
-        c.ops.gemv_i4(rms(h[-1], finw).half(), lm, out=logits, stream=c.stream)
+    # the prompt's KV caches (one per layer, [KV heads, T, head_dim] f16) and rotation rows
+    kcs = [torch.empty((NKV_HEADS, T, HEAD_DIM), dtype=torch.float16, device=c.device) for _ in range(args.layers)]
+    vcs = [torch.empty_like(kc) for kc in kcs]
+    ang = torch.arange(T, device=c.device, dtype=torch.float64)[:, None] / \
+        10000.0 ** (torch.arange(0, HEAD_DIM, 2, device=c.device, dtype=torch.float64) / HEAD_DIM)
+    cosM, sinM = torch.cat([ang, ang], 1).cos().float(), torch.cat([ang, ang], 1).sin().float()
+    p0 = torch.zeros(1, dtype=torch.int32, device=c.device)
+    h = torch.empty((T, H), dtype=torch.float32, device=c.device)
+    a16 = torch.empty((T, NQ), dtype=torch.float16, device=c.device)
+    x16 = torch.empty((T, H), dtype=torch.float16, device=c.device)
+    hl16 = torch.empty((1, H), dtype=torch.float16, device=c.device)
+    st = c.stream
 
-    for i8 in (False, True):
+    def prefill(i8, torch_attention=False):
+        """vk_engine.py's per-layer prefill recording (src/vk_engine.py:413-424) on this stack: pre_norm,
+        q / k / v GEMMs, pre_prepkv + pre_attn, o GEMM, pre_na, pre_norm, gate / up GEMMs, gelumul, down
+        GEMM, pre_na; then the final norm and lm_head on the prompt's last token."""
+        h.copy_(X0)
+        for li, (dd, nm) in enumerate(zip(layers_w, norms)):
+            c.ops.rows_rmsnorm(h, nm.inw, out=x16, stream=st)
+            q, k, v = mm(x16, dd["q"], i8), mm(x16, dd["k"], i8), mm(x16, dd["v"], i8)
+            if torch_attention:
+                a = F.scaled_dot_product_attention(q.view(T, NH, HEAD_DIM).transpose(0, 1)[None],
+                                                   k.view(T, NKV_HEADS, HEAD_DIM).transpose(0, 1)[None],
+                                                   v.view(T, NKV_HEADS, HEAD_DIM).transpose(0, 1)[None],
+                                                   is_causal=True, enable_gqa=True)
+                a16.copy_(a[0].transpose(0, 1).reshape(T, NQ))
+            else:
+                c.ops.attn_prefill_prepkv(k, v, knw[li], cosM, sinM, kcs[li], vcs[li], p0, NKV_HEADS, HEAD_DIM,
+                                          stream=st)
+                c.ops.attn_prefill(q, qnw[li], cosM, sinM, kcs[li], vcs[li], p0, NH, NKV_HEADS, HEAD_DIM, out=a16,
+                                   stream=st)
+            c.ops.rows_normadd(mm(a16, dd["o"], i8), nm.paw, h, 1.0, stream=st)
+            c.ops.rows_rmsnorm(h, nm.pfw, out=x16, stream=st)
+            act = c.ops.gelumul(mm(x16, dd["gate"], i8), mm(x16, dd["up"], i8), stream=st)
+            c.ops.rows_normadd(mm(act, dd["down"], i8), nm.ofw, h, nm.scl, stream=st)
+        c.ops.rows_rmsnorm(h[-1:], finw, out=hl16, stream=st)
+        c.ops.gemv_i4(hl16.view(-1), lm, out=logits, stream=st)
+
+    runs = (("prefill prompt-tok/s (W4A16)", False, False),
+            ("prefill prompt-tok/s (PREFILL_I8: cast_i8 + W8A8)", True, False),
+            ("prefill prompt-tok/s (W4A16, torch SDPA in place of g4b_attn_prefill)", False, True))
+    for key, i8, ta in runs:
         with torch.cuda.stream(c.stream):
-            prefill(i8)                                       # warm-up
+            prefill(i8, ta)                                   # warm-up
             c.stream.synchronize()
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(c.stream)
-            prefill(i8)
+            prefill(i8, ta)
             e1.record(c.stream)
         c.stream.synchronize()
         ms = c.max(e0.elapsed_time(e1))
-        key = "prefill prompt-tok/s (PREFILL_I8: cast_i8 + W8A8)" if i8 else "prefill prompt-tok/s (W4A16)"
         out[key] = round(T / (ms / 1e3), 1)
+    del kcs, vcs
     del layers_w, layers_d, X0, A8
     torch.cuda.empty_cache()
     return out

@@ -87,6 +87,9 @@ SIGNATURES = {
     "g4b_attn_decode": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P]),
     "g4b_attn_decode_prepkv": (_I, [_P, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _I,
                                     _P, _P, _Z, _P]),
+    "g4b_rows_rmsnorm": (_I, [_P, _I, _P, _P, _I, _I, _I, _P]),
+    "g4b_rows_normadd": (_I, [_P, _I, _P, _P, _I, _I, _F, _P]),
+    "g4b_gelumul": (_I, [_P, _P, _I, _P, _I, _Z, _P]),
     "g4b_attn_prefill_prepkv": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "g4b_attn_prefill": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "g4b_gemv_chain_workspace_bytes": (_Z, [_P]),

@@ -523,3 +523,43 @@ def attn_prefill(q: torch.Tensor, qnw: torch.Tensor, cosM: torch.Tensor, sinM: t
         _ptr(q), _DT[q.dtype], q.stride(0), M, _ptr(qnw), _ptr(cosM), _ptr(sinM), _ptr(kc), _ptr(vc), _ptr(out),
         _DT[out.dtype], out.stride(0), nH, nkv, hd, kc.shape[1], window, _ptr(p0), sh))
     return out
+
+
+# ----------------------------------------------------------------- prefill element-wise rows
+def rows_rmsnorm(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 out_dtype: Optional[torch.dtype] = None, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """vk/pre_norm.comp over the rows of x [M, D]: x * rsqrt(mean(x^2) + 1e-6) * w."""
+    _need(x, "x")
+    _need(w, "w")
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    M, D = x.shape
+    L.check("g4b_rows_rmsnorm", L.load().g4b_rows_rmsnorm(
+        _ptr(x), _DT[x.dtype], _ptr(w), _ptr(out), _DT[out.dtype], M, D, _stream_handle(stream, x.device)))
+    return out
+
+
+def rows_normadd(x: torch.Tensor, w: torch.Tensor, h: torch.Tensor, scl: float = 1.0,
+                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """vk/pre_na.comp over the rows of x [M, D]: h = (h + rmsnorm(x) * w) * scl, in place (h f32)."""
+    for t, n in ((x, "x"), (w, "w"), (h, "h")):
+        _need(t, n)
+    M, D = x.shape
+    L.check("g4b_rows_normadd", L.load().g4b_rows_normadd(
+        _ptr(x), _DT[x.dtype], _ptr(w), _ptr(h), M, D, float(scl), _stream_handle(stream, x.device)))
+    return h
+
+
+def gelumul(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None,
+            out_dtype: Optional[torch.dtype] = None, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """vk/gelumul.comp: gelu_tanh(gate) * up, element-wise."""
+    _need(gate, "gate")
+    _need(up, "up")
+    if gate.dtype != up.dtype or gate.numel() != up.numel():
+        raise ValueError("gelumul: gate and up must match in dtype and size")
+    if out is None:
+        out = torch.empty(gate.shape, dtype=out_dtype or gate.dtype, device=gate.device)
+    L.check("g4b_gelumul", L.load().g4b_gelumul(
+        _ptr(gate), _ptr(up), _DT[gate.dtype], _ptr(out), _DT[out.dtype], gate.numel(),
+        _stream_handle(stream, gate.device)))
+    return out

@@ -460,6 +460,22 @@ G4B_API int g4b_attn_prefill(const void* q, int dtype, int q_stride, int M, cons
                              int out_stride, int nH, int nkv, int hd, int stride, int window, const int* p0_dev,
                              g4b_stream_t stream);
 
+/* ------------------------------------------------------------ prefill element-wise rows */
+/* The prefill layer's norm and activation dispatches over [M, D] token rows
+ * (src/vk_engine.py:413-424), one CTA per row for the norms:
+ *   g4b_rows_rmsnorm  vk/pre_norm.comp:8-13   y[m] = x[m] * rsqrt(mean(x[m]^2) + 1e-6) * w
+ *   g4b_rows_normadd  vk/pre_na.comp:9-15     h[m] = (h[m] + x[m] * rsqrt(mean(x[m]^2) + 1e-6) * w) * scl
+ *   g4b_gelumul       vk/gelumul.comp:7-8     out[i] = gelu_tanh(gate[i]) * up[i]   (n elements)
+ * x, y, gate, up, out are f32 or f16 (G4B_DT_*); w and the residual h are f32.  D and n are
+ * multiples of 4; every pointer 16-byte aligned.  (The decode token fuses the same work into the
+ * GEMV chain: g4b_gemv_chain_create_fused.) */
+G4B_API int g4b_rows_rmsnorm(const void* x, int x_dtype, const float* w, void* y, int y_dtype, int M, int D,
+                             g4b_stream_t stream);
+G4B_API int g4b_rows_normadd(const void* x, int x_dtype, const float* w, float* h, int M, int D, float scl,
+                             g4b_stream_t stream);
+G4B_API int g4b_gelumul(const void* gate, const void* up, int dtype, void* out, int out_dtype, size_t n,
+                        g4b_stream_t stream);
+
 /* ------------------------------------------------------------ tensor parallel */
 /* The all-reduce after the row-parallel o and down GEMVs of a tensor-parallel
  * decode -- the cross-GPU counterpart of vk/reduce.comp:8-12 (the reference
