@@ -22,7 +22,8 @@
 //               per element 2.5 ALU ops, exact f16((q-8)*s) (HSUB2 of the
 //               1024+q exponent trick, then HMUL2).
 //   warps 18-21 epilogue: tcgen05.ld of the f32 accumulator, convert, store.
-// TMEM: accumulator columns [0, 256), A stages at [256, 256 + 32*stages) (448 of 512).
+// TMEM: accumulator columns [0, 256), A stages at [256, 256 + 32*stages) (448 of 512); the 64-token
+// instance (batched decode): two accumulators [0, 128), 12 A stages up to column 512.
 // Shared-memory stage s and TMEM A stage s are recycled together: the MMA's
 // commit on empty[s] frees both.
 #include <algorithm>
@@ -45,18 +46,25 @@ constexpr int kW4BN = 128;      // weight columns per tile (TMEM lanes)
 constexpr int kW4BT = 256;      // tokens per tile (MMA N) for prefill
 constexpr int kW4BTSmall = 64;  // tokens per tile for M <= 64 (batched decode): no MMA work on padding rows
 constexpr int kW4BK = 64;       // K rows per stage
-constexpr int kW4Stages = 6;  // even: dequant warps alternate stages
 constexpr int kW4DqWarps = 16;
 constexpr int kW4Threads = (2 + kW4DqWarps + 4) * 32;
 constexpr int kW4WBytes = kW4BK * (kW4BN / 8) * 4;    // 4 KB
 constexpr int kW4SBytes = (kW4BK / 32) * kW4BN * 2;   // 512 B
 constexpr int kW4TmemCols = 512;
-static_assert(kW4Stages % 2 == 0 && 256 + 32 * kW4Stages <= kW4TmemCols, "TMEM budget");
-constexpr int kW4ACol = kW4BT;                         // first A column (after the widest accumulator)
 constexpr int kW4MaxSplit = 16;
+// Per instance: stages in flight (even: dequant warps alternate stages) and accumulator buffers.  The
+// 64-token instance (batched decode) is latency-bound on its small stages, so it keeps 12 in flight and
+// two 64-column accumulators (the epilogue of one tile overlaps the next tile's MMAs); TMEM holds the
+// accumulators, then 32 A columns per stage.
+__host__ __device__ constexpr int w4_stages(int bt) { return bt == kW4BTSmall ? 12 : 6; }
+__host__ __device__ constexpr int w4_nacc(int bt) { return bt == kW4BTSmall ? 2 : 1; }
+constexpr int kW4MaxStages = 12;
+static_assert(w4_stages(kW4BT) % 2 == 0 && w4_stages(kW4BTSmall) % 2 == 0, "dequant warps alternate stages");
+static_assert(w4_nacc(kW4BT) * kW4BT + 32 * w4_stages(kW4BT) <= kW4TmemCols, "TMEM budget (prefill)");
+static_assert(w4_nacc(kW4BTSmall) * kW4BTSmall + 32 * w4_stages(kW4BTSmall) <= kW4TmemCols, "TMEM budget (small M)");
 __host__ __device__ constexpr int w4_xbytes(int bt) { return bt * kW4BK * 2; }  // 32 KB / 8 KB
 __host__ __device__ constexpr size_t w4_smem(int bt) {
-    return 1024 + (size_t)kW4Stages * (w4_xbytes(bt) + kW4WBytes + kW4SBytes);
+    return 1024 + (size_t)w4_stages(bt) * (w4_xbytes(bt) + kW4WBytes + kW4SBytes);
 }
 
 // Split-K: tile t of the launch is (column tile, token tile) t / S with the K range of split t % S;
@@ -74,8 +82,15 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                                                                    const __grid_constant__ CUtensorMap wmap,
                                                                    const __grid_constant__ CUtensorMap smap) {
     constexpr int kW4XBytes = w4_xbytes(BT);
+    constexpr int kW4Stages = w4_stages(BT), kNAcc = w4_nacc(BT);
+    // dequant warps per stage: each of 8 warps takes one (lane quarter, 32-row scale block) of every
+    // other stage (giving the small-M instance's 4 warps a quarter's 64 rows of every fourth stage
+    // measured no faster)
+    constexpr int kPar = 2, kDqPerStage = kW4DqWarps / kPar;
+    static_assert(kW4Stages % kPar == 0, "stages a multiple of the dequant rotation");
+    constexpr int kW4ACol = kNAcc * BT;   // first A column (after the accumulators)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    __shared__ uint64_t bars[3 * kW4Stages + 3];
+    __shared__ uint64_t bars[3 * kW4MaxStages + 2 * 2 + 1];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -91,18 +106,21 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (kW4Stages + s); };
     auto afull_bar = [&](int s) { return bar0 + 8u * (2 * kW4Stages + s); };
-    const uint32_t dfull_bar = bar0 + 8u * (3 * kW4Stages);
-    const uint32_t dempty_bar = dfull_bar + 8u;
-    const uint32_t drain_bar = dfull_bar + 16u;
+    // accumulator buffer b: dfull(b) (MMA commit -> epilogue), dempty(b) (epilogue -> MMA)
+    auto dfull_bar = [&](int b) { return bar0 + 8u * (3 * kW4Stages + 2 * b); };
+    auto dempty_bar = [&](int b) { return bar0 + 8u * (3 * kW4Stages + 2 * b + 1); };
+    const uint32_t drain_bar = bar0 + 8u * (3 * kW4Stages + 2 * kNAcc);
 
     if (tid == 0) {
         for (int s = 0; s < kW4Stages; s++) {
             mbar_init(full_bar(s), 1);
-            mbar_init(empty_bar(s), 8 + 1);  // 8 dequant warps + the MMA commit
-            mbar_init(afull_bar(s), 8);
+            mbar_init(empty_bar(s), kDqPerStage + 1);  // the stage's dequant warps + the MMA commit
+            mbar_init(afull_bar(s), kDqPerStage);
         }
-        mbar_init(dfull_bar, 1);
-        mbar_init(dempty_bar, 4);
+        for (int b = 0; b < kNAcc; b++) {
+            mbar_init(dfull_bar(b), 1);
+            mbar_init(dempty_bar(b), 4);
+        }
         mbar_init(drain_bar, 1);
         s_abort = 0;
         fence_mbar_init();
@@ -158,7 +176,8 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
             int it = 0, tc_i = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x, tc_i++) {
-                if (!mbar_wait(dempty_bar, (tc_i & 1) ^ 1, abort_flag, &g_gemm_status)) break;
+                const int ab = tc_i % kNAcc;
+                if (!mbar_wait(dempty_bar(ab), ((tc_i / kNAcc) & 1) ^ 1, abort_flag, &g_gemm_status)) break;
                 tc::fence_after();
                 const int ks = SPLIT ? t % S : 0;
                 const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
@@ -174,11 +193,11 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                     const uint64_t bdesc = tc::sdesc_sw128(sm0 + s * kW4XBytes, 16, 1024);
 #pragma unroll
                     for (int kk = 0; kk < kW4BK / 16; kk++)
-                        tc::mma_f16_ts(tmem, tmem + kW4ACol + s * (kW4BK / 2) + kk * 8, bdesc + (uint64_t)(kk * 2),
+                        tc::mma_f16_ts(tmem + ab * BT, tmem + kW4ACol + s * (kW4BK / 2) + kk * 8, bdesc + (uint64_t)(kk * 2),
                                        idesc, SPLIT ? ((kb != kb0 || kk != 0) ? 1u : 0u) : (uint32_t)((kb | kk) != 0));
                     tc::commit(empty_bar(s));
                 }
-                if (ok) tc::commit(dfull_bar);
+                if (ok) tc::commit(dfull_bar(ab));
             }
             // drain: every MMA issued must be complete before TMEM is released
             tc::commit(drain_bar);
@@ -187,8 +206,9 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
     } else if (warp < 2 + kW4DqWarps) {
         // ------------------------------------------------------- dequant
         const int q = warp & 3;             // TMEM lane quarter this warp may access
-        const int kh = ((warp - 2) >> 2) & 1;  // which 32-row scale block of the stage
-        const int par = (warp - 2) >> 3;       // which stages: it % 2 == par
+        // the 32-row scale blocks of a stage this warp dequantises, and which stages: it % kPar == par
+        const int kh0 = kPar == 2 ? ((warp - 2) >> 2) & 1 : 0, nkh = kPar == 2 ? 1 : 2;
+        const int par = kPar == 2 ? (warp - 2) >> 3 : (warp - 2) >> 2;
         const int nl = q * 32 + lane;       // weight column within the tile
         const int g = nl >> 3, j = nl & 7;
         const uint32_t sel = (uint32_t)(j >> 1) | ((uint32_t)(4 + (j >> 1)) << 8);
@@ -200,26 +220,28 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
             const int ks = SPLIT ? t % S : 0;
             const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
             for (int kb = kb0; kb < kb1; kb++, it++) {
-                if ((it & 1) != par) continue;
+                if ((it % kPar) != par) continue;
                 const int s = it % kW4Stages;
                 if (!mbar_wait(full_bar(s), (it / kW4Stages) & 1, abort_flag, &g_gemm_status)) {
                     ok = false;
                     break;
                 }
                 tc::fence_after();
-                const uint32_t* wr = wsm + s * (kW4WBytes / 4) + kh * 32 * (kW4BN / 8) + g;
-                const uint32_t sc = ssm[s * (kW4SBytes / 2) + kh * kW4BN + nl];
-                const uint32_t s2 = sc | (sc << 16);
-                uint32_t v[16];
+                for (int kh = kh0; kh < kh0 + nkh; kh++) {
+                    const uint32_t* wr = wsm + s * (kW4WBytes / 4) + kh * 32 * (kW4BN / 8) + g;
+                    const uint32_t sc = ssm[s * (kW4SBytes / 2) + kh * kW4BN + nl];
+                    const uint32_t s2 = sc | (sc << 16);
+                    uint32_t v[16];
 #pragma unroll
-                for (int p = 0; p < 16; p++) {
-                    const uint32_t w0 = wr[(2 * p) * (kW4BN / 8)], w1 = wr[(2 * p + 1) * (kW4BN / 8)];
-                    uint32_t u = prmt(w0, w1, sel) >> sh;
-                    u = and_or(u, 0x000F000Fu, 0x64006400u);  // f16 pair (1024 + q_k, 1024 + q_k+1)
-                    u = hsub2_u(u, 0x64086408u);               // exact (q - 8)
-                    v[p] = hmul2_u(u, s2);                     // f16((q - 8) * s), one rounding
+                    for (int p = 0; p < 16; p++) {
+                        const uint32_t w0 = wr[(2 * p) * (kW4BN / 8)], w1 = wr[(2 * p + 1) * (kW4BN / 8)];
+                        uint32_t u = prmt(w0, w1, sel) >> sh;
+                        u = and_or(u, 0x000F000Fu, 0x64006400u);  // f16 pair (1024 + q_k, 1024 + q_k+1)
+                        u = hsub2_u(u, 0x64086408u);               // exact (q - 8)
+                        v[p] = hmul2_u(u, s2);                     // f16((q - 8) * s), one rounding
+                    }
+                    tc::st_32x32b_x16(tmem + lane_addr + kW4ACol + s * (kW4BK / 2) + kh * 16, v);
                 }
-                tc::st_32x32b_x16(tmem + lane_addr + kW4ACol + s * (kW4BK / 2) + kh * 16, v);
                 tc::wait_st();
                 tc::fence_before();
                 __syncwarp();
@@ -236,7 +258,8 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         int tc_i = 0;
         for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, tc_i++) {
-            if (!mbar_wait(dfull_bar, tc_i & 1, abort_flag, &g_gemm_status)) break;
+            const int ab = tc_i % kNAcc;
+            if (!mbar_wait(dfull_bar(ab), (tc_i / kNAcc) & 1, abort_flag, &g_gemm_status)) break;
             tc::fence_after();
             const int tb = SPLIT ? t / S : t, ks = SPLIT ? t % S : 0;
             const int nt = tb / a.ntm, mt = tb % a.ntm;
@@ -246,7 +269,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
 #pragma unroll 1
             for (int c = 0; c < BT / 32; c++) {
                 uint32_t r[32];
-                tc::ld_32x32b_x32(tmem + lane_addr + c * 32, r);
+                tc::ld_32x32b_x32(tmem + lane_addr + ab * BT + c * 32, r);
                 tc::wait_ld();
                 const int mb = m0 + c * 32;
                 // the f32 partials of a K split, or y; the row index is checked per element (M may end mid-tile)
@@ -271,7 +294,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
             }
             tc::fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(dempty_bar);
+            if (lane == 0) mbar_arrive(dempty_bar(ab));
         }
     }
 
