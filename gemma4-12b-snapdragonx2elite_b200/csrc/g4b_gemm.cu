@@ -23,7 +23,7 @@
 //               1024+q exponent trick, then HMUL2).
 //   warps 18-21 epilogue: tcgen05.ld of the f32 accumulator, convert, store.
 // TMEM: accumulator columns [0, 256), A stages at [256, 256 + 32*stages) (448 of 512); the 64-token
-// instance (batched decode): two accumulators [0, 128), 12 A stages up to column 512.
+// instance (batched decode): two accumulators [0, 128), 4 stages of 3 K blocks (96 A columns each).
 // Shared-memory stage s and TMEM A stage s are recycled together: the MMA's
 // commit on empty[s] frees both.
 #include <algorithm>
@@ -56,15 +56,20 @@ constexpr int kW4MaxSplit = 16;
 // 64-token instance (batched decode) is latency-bound on its small stages, so it keeps 12 in flight and
 // two 64-column accumulators (the epilogue of one tile overlaps the next tile's MMAs); TMEM holds the
 // accumulators, then 32 A columns per stage.
-__host__ __device__ constexpr int w4_stages(int bt) { return bt == kW4BTSmall ? 12 : 6; }
+// A stage carries w4_sub(bt) consecutive 64-row K blocks: the small-M instance's stages are otherwise too
+// small for their fixed hand-off (TMA landing, TMEM stores, MMA issue and commit) to hide behind.  Measured at
+// M = 8 on the lm_head shape: 1 block x 6 stages 350 us, 1 x 12 327-340 us, 2 x 6 274 us, 3 x 4 246-264 us.
+__host__ __device__ constexpr int w4_stages(int bt) { return bt == kW4BTSmall ? 4 : 6; }
+__host__ __device__ constexpr int w4_sub(int bt) { return bt == kW4BTSmall ? 3 : 1; }
 __host__ __device__ constexpr int w4_nacc(int bt) { return bt == kW4BTSmall ? 2 : 1; }
-constexpr int kW4MaxStages = 12;
+constexpr int kW4MaxStages = 6;
 static_assert(w4_stages(kW4BT) % 2 == 0 && w4_stages(kW4BTSmall) % 2 == 0, "dequant warps alternate stages");
-static_assert(w4_nacc(kW4BT) * kW4BT + 32 * w4_stages(kW4BT) <= kW4TmemCols, "TMEM budget (prefill)");
-static_assert(w4_nacc(kW4BTSmall) * kW4BTSmall + 32 * w4_stages(kW4BTSmall) <= kW4TmemCols, "TMEM budget (small M)");
-__host__ __device__ constexpr int w4_xbytes(int bt) { return bt * kW4BK * 2; }  // 32 KB / 8 KB
+static_assert(w4_nacc(kW4BT) * kW4BT + 32 * w4_sub(kW4BT) * w4_stages(kW4BT) <= kW4TmemCols, "TMEM budget (prefill)");
+static_assert(w4_nacc(kW4BTSmall) * kW4BTSmall + 32 * w4_sub(kW4BTSmall) * w4_stages(kW4BTSmall) <= kW4TmemCols,
+              "TMEM budget (small M)");
+__host__ __device__ constexpr int w4_xbytes(int bt) { return bt * kW4BK * 2; }  // 32 KB / 8 KB per K block
 __host__ __device__ constexpr size_t w4_smem(int bt) {
-    return 1024 + (size_t)w4_stages(bt) * (w4_xbytes(bt) + kW4WBytes + kW4SBytes);
+    return 1024 + (size_t)w4_stages(bt) * w4_sub(bt) * (w4_xbytes(bt) + kW4WBytes + kW4SBytes);
 }
 
 // Split-K: tile t of the launch is (column tile, token tile) t / S with the K range of split t % S;
@@ -82,13 +87,14 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                                                                    const __grid_constant__ CUtensorMap wmap,
                                                                    const __grid_constant__ CUtensorMap smap) {
     constexpr int kW4XBytes = w4_xbytes(BT);
-    constexpr int kW4Stages = w4_stages(BT), kNAcc = w4_nacc(BT);
+    constexpr int kW4Stages = w4_stages(BT), kNAcc = w4_nacc(BT), kSub = w4_sub(BT);
     // dequant warps per stage: each of 8 warps takes one (lane quarter, 32-row scale block) of every
     // other stage (giving the small-M instance's 4 warps a quarter's 64 rows of every fourth stage
     // measured no faster)
     constexpr int kPar = 2, kDqPerStage = kW4DqWarps / kPar;
     static_assert(kW4Stages % kPar == 0, "stages a multiple of the dequant rotation");
     constexpr int kW4ACol = kNAcc * BT;   // first A column (after the accumulators)
+    constexpr int kACols = kSub * (kW4BK / 2);   // A columns per stage
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[3 * kW4MaxStages + 2 * 2 + 1];
     __shared__ uint32_t s_tmem;
@@ -97,11 +103,12 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
     volatile int* abort_flag = &s_abort;
     const uint32_t raw0 = smem_u32(smem_raw);
     const uint32_t sm0 = (raw0 + 1023u) & ~1023u;          // X stages (1024-aligned for the swizzle)
-    const uint32_t smw = sm0 + kW4Stages * kW4XBytes;        // packed words
-    const uint32_t sms = smw + kW4Stages * kW4WBytes;        // scales
+    // stage s, K block j of the stage: X at sm0 + (s kSub + j) kW4XBytes, words and scales likewise
+    const uint32_t smw = sm0 + kW4Stages * kSub * kW4XBytes;   // packed words
+    const uint32_t sms = smw + kW4Stages * kSub * kW4WBytes;   // scales
     const uint8_t* gsm = smem_raw + (sm0 - raw0);
-    const uint32_t* wsm = reinterpret_cast<const uint32_t*>(gsm + kW4Stages * kW4XBytes);
-    const uint16_t* ssm = reinterpret_cast<const uint16_t*>(gsm + kW4Stages * (kW4XBytes + kW4WBytes));
+    const uint32_t* wsm = reinterpret_cast<const uint32_t*>(gsm + kW4Stages * kSub * kW4XBytes);
+    const uint16_t* ssm = reinterpret_cast<const uint16_t*>(gsm + kW4Stages * kSub * (kW4XBytes + kW4WBytes));
     const uint32_t bar0 = smem_u32(bars);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
     auto empty_bar = [&](int s) { return bar0 + 8u * (kW4Stages + s); };
@@ -152,17 +159,22 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                 const int tb = SPLIT ? t / S : t, ks = SPLIT ? t % S : 0;
                 const int nt = tb / a.ntm, mt = tb % a.ntm;
                 const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
-                for (int kb = kb0; kb < kb1; kb++, it++) {
-                    const int s = it % kW4Stages;
+                for (int kb = kb0; kb < kb1; kb += kSub, it++) {
+                    const int s = it % kW4Stages, sub = min(kSub, kb1 - kb);
                     if (it >= kW4Stages &&
                         !mbar_wait(empty_bar(s), ((it / kW4Stages) & 1) ^ 1, abort_flag, &g_gemm_status)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(full_bar(s), kW4XBytes + kW4WBytes + kW4SBytes);
-                    tma_load_2d(sm0 + s * kW4XBytes, &xmap, kb * kW4BK, mt * BT, full_bar(s), pol_x);
-                    tma_load_2d(smw + s * kW4WBytes, &wmap, nt * (kW4BN / 8), kb * kW4BK, full_bar(s), pol_w);
-                    tma_load_2d(sms + s * kW4SBytes, &smap, nt * kW4BN, kb * (kW4BK / 32), full_bar(s), pol_w);
+                    mbar_arrive_expect_tx(full_bar(s), (uint32_t)sub * (kW4XBytes + kW4WBytes + kW4SBytes));
+                    for (int j = 0; j < sub; j++) {
+                        const int sj = s * kSub + j;
+                        tma_load_2d(sm0 + sj * kW4XBytes, &xmap, (kb + j) * kW4BK, mt * BT, full_bar(s), pol_x);
+                        tma_load_2d(smw + sj * kW4WBytes, &wmap, nt * (kW4BN / 8), (kb + j) * kW4BK, full_bar(s),
+                                    pol_w);
+                        tma_load_2d(sms + sj * kW4SBytes, &smap, nt * kW4BN, (kb + j) * (kW4BK / 32), full_bar(s),
+                                    pol_w);
+                    }
                 }
             }
             // drain: the copies already issued must land before the CTA exits
@@ -181,8 +193,8 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                 tc::fence_after();
                 const int ks = SPLIT ? t % S : 0;
                 const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
-                for (int kb = kb0; kb < kb1; kb++, it++) {
-                    const int s = it % kW4Stages;
+                for (int kb = kb0; kb < kb1; kb += kSub, it++) {
+                    const int s = it % kW4Stages, sub = min(kSub, kb1 - kb);
                     const uint32_t ph = (it / kW4Stages) & 1;
                     if (!mbar_wait(full_bar(s), ph, abort_flag, &g_gemm_status) ||
                         !mbar_wait(afull_bar(s), ph, abort_flag, &g_gemm_status)) {
@@ -190,11 +202,14 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                         break;
                     }
                     tc::fence_after();
-                    const uint64_t bdesc = tc::sdesc_sw128(sm0 + s * kW4XBytes, 16, 1024);
+                    for (int j = 0; j < sub; j++) {
+                        const uint64_t bdesc = tc::sdesc_sw128(sm0 + (s * kSub + j) * kW4XBytes, 16, 1024);
 #pragma unroll
-                    for (int kk = 0; kk < kW4BK / 16; kk++)
-                        tc::mma_f16_ts(tmem + ab * BT, tmem + kW4ACol + s * (kW4BK / 2) + kk * 8, bdesc + (uint64_t)(kk * 2),
-                                       idesc, SPLIT ? ((kb != kb0 || kk != 0) ? 1u : 0u) : (uint32_t)((kb | kk) != 0));
+                        for (int kk = 0; kk < kW4BK / 16; kk++)
+                            tc::mma_f16_ts(tmem + ab * BT, tmem + kW4ACol + s * kACols + j * (kW4BK / 2) + kk * 8,
+                                           bdesc + (uint64_t)(kk * 2), idesc,
+                                           (kb + j != kb0 || kk != 0) ? 1u : 0u);
+                    }
                     tc::commit(empty_bar(s));
                 }
                 if (ok) tc::commit(dfull_bar(ab));
@@ -219,17 +234,18 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
         for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x) {
             const int ks = SPLIT ? t % S : 0;
             const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
-            for (int kb = kb0; kb < kb1; kb++, it++) {
+            for (int kb = kb0; kb < kb1; kb += kSub, it++) {
                 if ((it % kPar) != par) continue;
-                const int s = it % kW4Stages;
+                const int s = it % kW4Stages, sub = min(kSub, kb1 - kb);
                 if (!mbar_wait(full_bar(s), (it / kW4Stages) & 1, abort_flag, &g_gemm_status)) {
                     ok = false;
                     break;
                 }
                 tc::fence_after();
-                for (int kh = kh0; kh < kh0 + nkh; kh++) {
-                    const uint32_t* wr = wsm + s * (kW4WBytes / 4) + kh * 32 * (kW4BN / 8) + g;
-                    const uint32_t sc = ssm[s * (kW4SBytes / 2) + kh * kW4BN + nl];
+                for (int jk = 0; jk < sub * nkh; jk++) {
+                    const int j = jk / nkh, kh = kh0 + jk % nkh, sj = s * kSub + j;
+                    const uint32_t* wr = wsm + sj * (kW4WBytes / 4) + kh * 32 * (kW4BN / 8) + g;
+                    const uint32_t sc = ssm[sj * (kW4SBytes / 2) + kh * kW4BN + nl];
                     const uint32_t s2 = sc | (sc << 16);
                     uint32_t v[16];
 #pragma unroll
@@ -240,7 +256,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                         u = hsub2_u(u, 0x64086408u);               // exact (q - 8)
                         v[p] = hmul2_u(u, s2);                     // f16((q - 8) * s), one rounding
                     }
-                    tc::st_32x32b_x16(tmem + lane_addr + kW4ACol + s * (kW4BK / 2) + kh * 16, v);
+                    tc::st_32x32b_x16(tmem + lane_addr + kW4ACol + s * kACols + j * (kW4BK / 2) + kh * 16, v);
                 }
                 tc::wait_st();
                 tc::fence_before();
