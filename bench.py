@@ -896,7 +896,8 @@ def build_tp_model(c, fp8, layers):
 def measure_decode_batch(c, layers, lm, M, steps, warmup, full_bytes):
     """configs[4]'s batched decode: M tokens through the tensor-parallel stack,
     one W4A16 tensor-core GEMM per layer weight (64-token tiles, K split over
-    the SMs where the column tiles cannot fill them), an NCCL all-reduce after
+    the SMs where the column tiles cannot fill them; each GEMM launched as a
+    programmatic dependent of the kernel before it), an NCCL all-reduce after
     o and after down and a logits all-gather, captured as one CUDA graph.  Each
     layer's q/k/v read the same f16 N(0, 1) input block, so the unnormalised
     activations stay in f16 range.  value = the whole model's weight bytes /
@@ -917,7 +918,8 @@ def measure_decode_batch(c, layers, lm, M, steps, warmup, full_bytes):
     launches = [0]
 
     def mm(x, w, out):
-        ops.gemm_i4(x, w, out=out, stream=c.stream, workspace=ws)
+        # each GEMM a programmatic dependent of the kernel before it (G4B_GEMM_PDL)
+        ops.gemm_i4(x, w, out=out, stream=c.stream, workspace=ws, pdl=True)
         launches[0] += 1 + (1 if ops.gemm_i4_workspace_bytes(M, w.N, w.K) else 0)
 
     def ar(t):

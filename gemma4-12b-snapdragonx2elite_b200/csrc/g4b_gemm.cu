@@ -140,6 +140,7 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
     __syncthreads();
     tc::fence_after();
     const uint32_t tmem = s_tmem;
+    pdl_launch_dependents();   // a programmatic dependent may be scheduled now; it waits for this grid
     const int nks = a.nkb;  // K stages per tile
     // K splits: only the SPLIT instance (small M) reads a.S; the prefill instance keeps every tile whole
     const int S = SPLIT ? a.S : 1;
@@ -153,6 +154,17 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
             const uint64_t pol_w = l2_evict_first_policy();
             uint64_t pol_x;
             asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_x));
+            // launched as a programmatic dependent (G4B_GEMM_PDL): warm L2 with the first tile's first weight
+            // blocks while the kernel before finishes, then wait for it before the first X load
+            if (blockIdx.x < a.ntiles) {
+                const int t = blockIdx.x, tb = SPLIT ? t / S : t, ks = SPLIT ? t % S : 0;
+                const int nt = tb / a.ntm, kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
+                for (int kb = kb0; kb < std::min(kb1, kb0 + kW4Stages * kSub); kb++) {
+                    tma_prefetch_l2_2d(&wmap, nt * (kW4BN / 8), kb * kW4BK);
+                    tma_prefetch_l2_2d(&smap, nt * kW4BN, kb * (kW4BK / 32));
+                }
+            }
+            pdl_wait();
             int it = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x) {
@@ -623,6 +635,8 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
 template <bool YF32>
 __global__ void w4a16_splitk_reduce(const float* __restrict__ part, void* __restrict__ y, size_t n4, size_t stride,
                                     int S) {
+    pdl_launch_dependents();
+    pdl_wait();   // launched as a programmatic dependent of its GEMM: the partials are complete after this
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
         float4 v = __ldg(reinterpret_cast<const float4*>(part) + i);
         for (int s = 1; s < S; s++) {
@@ -683,7 +697,13 @@ size_t g4b_gemm_i4_workspace_bytes(int M, int N, int K, int x_dtype) {
 
 int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* scales_f16, void* Y, int y_dtype,
                 int M, int N, int K, void* workspace, size_t ws_bytes, g4b_stream_t stream) {
+    return g4b_gemm_i4_ex(X, x_dtype, wp, scales_f16, Y, y_dtype, M, N, K, workspace, ws_bytes, 0u, stream);
+}
+
+int g4b_gemm_i4_ex(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* scales_f16, void* Y, int y_dtype,
+                   int M, int N, int K, void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream) {
     G4B_ENTRY("gemm_i4");
+    G4B_REQUIRE((flags & ~G4B_GEMM_PDL) == 0u, G4B_E_ARG, "gemm_i4: unknown flags 0x%x", flags);
     G4B_REQUIRE(X && wp && scales_f16 && Y, G4B_E_ARG, "gemm_i4: NULL pointer");
     G4B_REQUIRE(x_dtype == G4B_DT_F32 || x_dtype == G4B_DT_F16, G4B_E_ARG, "gemm_i4: bad x_dtype %d", x_dtype);
     G4B_REQUIRE(y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16, G4B_E_ARG, "gemm_i4: bad y_dtype %d", y_dtype);
@@ -741,14 +761,34 @@ int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* 
         if (st != G4B_OK) return st;
     }
     const int grid = std::min(a.ntiles, sms);
-    kern<<<grid, kW4Threads, smem, s>>>(a, xmap, wmap, smap);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kW4Threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    // a GEMM after the f32 -> f16 cast (its own kernel) does not overlap it
+    cfg.numAttrs = (flags & G4B_GEMM_PDL) && x_dtype != G4B_DT_F32 ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, kern, a, xmap, wmap, smap);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemm_i4: launch: %s", cudaGetErrorString(e));
     count_launch();
     st = launch_status("gemm_i4");
     if (st != G4B_OK || p.S == 1) return st;
+    // the split sum, as a programmatic dependent of the GEMM (it waits for the partials)
     const size_t n4 = (size_t)M * N / 4;
     const int threads = 256, blocks = (int)std::min<size_t>((n4 + threads - 1) / threads, (size_t)sms * 8);
-    if (yf32) w4a16_splitk_reduce<true><<<blocks, threads, 0, s>>>(a.part, Y, n4, (size_t)M * N, p.S);
-    else w4a16_splitk_reduce<false><<<blocks, threads, 0, s>>>(a.part, Y, n4, (size_t)M * N, p.S);
+    cudaLaunchConfig_t rcfg{};
+    rcfg.gridDim = dim3(blocks);
+    rcfg.blockDim = dim3(threads);
+    rcfg.stream = s;
+    rcfg.attrs = attr;
+    rcfg.numAttrs = 1;
+    e = yf32 ? cudaLaunchKernelEx(&rcfg, w4a16_splitk_reduce<true>, (const float*)a.part, Y, n4, (size_t)M * N, p.S)
+             : cudaLaunchKernelEx(&rcfg, w4a16_splitk_reduce<false>, (const float*)a.part, Y, n4, (size_t)M * N, p.S);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemm_i4: split-sum launch: %s", cudaGetErrorString(e));
     count_launch();
     return launch_status("gemm_i4");
 }

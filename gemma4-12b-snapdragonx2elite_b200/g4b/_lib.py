@@ -26,6 +26,7 @@ G4B_E_TIMEOUT = -8
 GEMV_PDL = 1
 CHAIN_ALLREDUCE = 1
 CHAIN_RUN_PDL = 1
+GEMM_PDL = 1
 DT_F32 = 0
 DT_F16 = 1
 SCALE_F16 = 0
@@ -69,6 +70,7 @@ SIGNATURES = {
     "g4b_quant_w8a8": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
     "g4b_gemm_i4_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g4b_gemm_i4": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
+    "g4b_gemm_i4_ex": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, C.c_uint, _P]),
     "g4b_allreduce_buffer_bytes": (_Z, [_I, _I]),
     "g4b_allreduce_f32": (_I, [_P, _P, _I, _I, _I, _P, _P, C.c_uint, _P]),
     "g4b_comm_alloc": (_I, [_Z, C.POINTER(_P)]),

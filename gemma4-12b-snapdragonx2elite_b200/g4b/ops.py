@@ -301,9 +301,10 @@ def gemm_i4_workspace_bytes(M: int, N: int, K: int, x_dtype: torch.dtype = torch
 
 def gemm_i4(X: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None,
             out_dtype: torch.dtype = torch.float16, stream: Optional[torch.cuda.Stream] = None,
-            workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+            workspace: Optional[torch.Tensor] = None, pdl: bool = False) -> torch.Tensor:
     """W4A16 prefill GEMM: Y[M, N] = X[M, K] @ dequant(W) with f16 block scales
-    (gmm()'s f16 path: cast_dn -> coopgemm_i4h -> cast_up)."""
+    (gmm()'s f16 path: cast_dn -> coopgemm_i4h -> cast_up).  pdl: launch as a
+    programmatic dependent of the previous kernel (G4B_GEMM_PDL)."""
     _need(X, "X")
     M, K = X.shape
     if K != w.K:
@@ -317,9 +318,9 @@ def gemm_i4(X: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None
     ws = workspace
     if need and ws is None:
         ws = WORKSPACES.get(X.device, sh, need, use="gemm_i4")
-    L.check("g4b_gemm_i4", lib.g4b_gemm_i4(
+    L.check("g4b_gemm_i4", lib.g4b_gemm_i4_ex(
         _ptr(X), _DT[X.dtype], _ptr(w.wp), _ptr(w.scales16), _ptr(out), _DT[out.dtype], M, w.N, w.K,
-        _ptr(ws), ws.numel() if ws is not None else 0, sh))
+        _ptr(ws), ws.numel() if ws is not None else 0, L.GEMM_PDL if pdl else 0, sh))
     return out
 
 

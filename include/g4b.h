@@ -368,6 +368,18 @@ G4B_API size_t g4b_gemm_i4_workspace_bytes(int M, int N, int K, int x_dtype);
 G4B_API int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* scales_f16,
                         void* Y, int y_dtype, int M, int N, int K,
                         void* workspace, size_t ws_bytes, g4b_stream_t stream);
+/* g4b_gemm_i4 with launch flags:
+ *   G4B_GEMM_PDL  programmatic dependent launch: the GEMM may start while the
+ *                 previous kernel in `stream` is still running; it prefetches
+ *                 its first weight tiles into L2 and reads X, and writes Y or
+ *                 the workspace, only after that kernel has completed.  For a
+ *                 batched decode's chain of dependent GEMMs.  (The split-K sum
+ *                 is always launched that way after its GEMM.)
+ * flags == 0 behaves exactly as g4b_gemm_i4. */
+#define G4B_GEMM_PDL 1u
+G4B_API int g4b_gemm_i4_ex(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* scales_f16,
+                           void* Y, int y_dtype, int M, int N, int K,
+                           void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream);
 
 /* W8A8 prefill GEMM (PREFILL_I8), vk/coopgemm_w8a8.comp:18-37, dispatched by
  * gmm() after cast_i8 (src/vk_engine.py:391-397):

@@ -144,3 +144,44 @@ def test_gemm_i4_small_m_split_k(M, N, K):
     assert torch.equal(Y, Y2)                                                 # deterministic
     assert_close(Y.cpu().numpy(), ref, f"split-K M={M} N={N} K={K}", guard=LONG_K_GUARD)
     assert_close(Y1.cpu().numpy(), ref, f"one split M={M} N={N} K={K}", guard=LONG_K_GUARD)
+
+
+def test_gemm_pdl_chain_gives_the_same_bits():
+    """G4B_GEMM_PDL: a chain of dependent small-M GEMMs (each one's output the next one's input, the
+    split-K ones sharing one workspace) launched as programmatic dependents, eager and in a graph, gives
+    the bits of the same chain launched plainly."""
+    from g4b import quant_gpu as qz
+    g = torch.Generator(device="cuda").manual_seed(4)
+    shapes = [(512, 3840), (3840, 512), (2048, 3840), (3840, 2048)]
+    ws_ = [qz.quant_device(torch.randn((N, K), generator=g, device="cuda").mul_(0.02), pf=False, fp8=False,
+                           prefill_i8=False) for N, K in shapes]
+    x0 = torch.randn((8, 3840), generator=g, device="cuda").half()
+    need = max(ops.gemm_i4_workspace_bytes(8, w.N, w.K) for w in ws_)
+    outs = {p: [torch.empty((8, w.N), device="cuda", dtype=torch.float16) for w in ws_] for p in (False, True)}
+    wsp = {p: torch.zeros(need + 256, dtype=torch.uint8, device="cuda") for p in (False, True)}
+    s = torch.cuda.Stream()
+
+    def chain(pdl):
+        x = x0
+        for w, y in zip(ws_, outs[pdl]):
+            ops.gemm_i4(x, w, out=y, stream=s, workspace=wsp[pdl], pdl=pdl)
+            x = y
+
+    with torch.cuda.stream(s):
+        chain(False)
+        chain(True)
+    s.synchronize()
+    for a, b in zip(outs[False], outs[True]):
+        assert torch.equal(a, b)
+    ref = [o.clone() for o in outs[True]]
+    with torch.cuda.stream(s):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=s):
+            chain(True)
+        for o in outs[True]:
+            o.zero_()
+        gr.replay()
+    s.synchronize()
+    for a, b in zip(ref, outs[True]):
+        assert torch.equal(a, b)
+    del gr
