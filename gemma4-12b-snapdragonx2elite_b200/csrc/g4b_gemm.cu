@@ -75,17 +75,61 @@ __host__ __device__ constexpr size_t w4_smem(int bt) {
 // Split-K: tile t of the launch is (column tile, token tile) t / S with the K range of split t % S;
 // with S > 1 each split writes its f32 partial to part[split][M][N] and a second kernel sums the
 // splits in order into y.
+// Fused weights (the small-M instance only): up to 3 weights that share X run as one launch, segment g
+// owning column tiles [tile0[g], tile0[g + 1]) and writing ys[g] [M, Ns[g]]; N is then their total and the
+// split partials are laid out over it.
+constexpr int kW4MaxSeg = 3;
+struct W4Segs {
+    int nseg;
+    int tile0[kW4MaxSeg + 1];
+    void* ys[kW4MaxSeg];
+    int Ns[kW4MaxSeg];
+};
+
 struct W4Args {
     void* y;
     float* part;
     int M, N, K, nkb, ntm, ntiles, S;
+    W4Segs seg;
 };
+
+// the segment of global column tile nt
+__device__ __forceinline__ int w4_seg_of(const W4Segs& g, int nt) {
+    return nt >= g.tile0[1] ? (nt >= g.tile0[2] ? 2 : 1) : 0;
+}
+// segment sg's output, width and first column tile (constant indices: no local-memory copy of the params)
+__device__ __forceinline__ void w4_seg_out(const W4Segs& g, int sg, void*& y, int& N, int& tile0) {
+    y = sg == 0 ? g.ys[0] : (sg == 1 ? g.ys[1] : g.ys[2]);
+    N = sg == 0 ? g.Ns[0] : (sg == 1 ? g.Ns[1] : g.Ns[2]);
+    tile0 = sg == 0 ? g.tile0[0] : (sg == 1 ? g.tile0[1] : g.tile0[2]);
+}
 
 template <bool YF32, int BT, bool SPLIT>
 __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args a,
                                                                    const __grid_constant__ CUtensorMap xmap,
                                                                    const __grid_constant__ CUtensorMap wmap,
-                                                                   const __grid_constant__ CUtensorMap smap) {
+                                                                   const __grid_constant__ CUtensorMap smap,
+                                                                   const __grid_constant__ CUtensorMap wmap1,
+                                                                   const __grid_constant__ CUtensorMap smap1,
+                                                                   const __grid_constant__ CUtensorMap wmap2,
+                                                                   const __grid_constant__ CUtensorMap smap2) {
+    // the weight / scale maps and local column tile of global column tile nt (segments: SPLIT instance only)
+    auto seg_maps = [&](int nt, const CUtensorMap*& wm, const CUtensorMap*& smp, int& ntl) {
+        wm = &wmap;
+        smp = &smap;
+        ntl = nt;
+        if constexpr (SPLIT) {
+            const int sg = w4_seg_of(a.seg, nt);
+            if (sg == 1) {
+                wm = &wmap1;
+                smp = &smap1;
+            } else if (sg == 2) {
+                wm = &wmap2;
+                smp = &smap2;
+            }
+            ntl = nt - (sg == 0 ? a.seg.tile0[0] : (sg == 1 ? a.seg.tile0[1] : a.seg.tile0[2]));
+        }
+    };
     constexpr int kW4XBytes = w4_xbytes(BT);
     constexpr int kW4Stages = w4_stages(BT), kNAcc = w4_nacc(BT), kSub = w4_sub(BT);
     // dequant warps per stage: each of 8 warps takes one (lane quarter, 32-row scale block) of every
@@ -158,10 +202,13 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
             // blocks while the kernel before finishes, then wait for it before the first X load
             if (blockIdx.x < a.ntiles) {
                 const int t = blockIdx.x, tb = SPLIT ? t / S : t, ks = SPLIT ? t % S : 0;
-                const int nt = tb / a.ntm, kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
+                const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
+                const CUtensorMap *wm, *smp;
+                int ntl;
+                seg_maps(tb / a.ntm, wm, smp, ntl);
                 for (int kb = kb0; kb < std::min(kb1, kb0 + kW4Stages * kSub); kb++) {
-                    tma_prefetch_l2_2d(&wmap, nt * (kW4BN / 8), kb * kW4BK);
-                    tma_prefetch_l2_2d(&smap, nt * kW4BN, kb * (kW4BK / 32));
+                    tma_prefetch_l2_2d(wm, ntl * (kW4BN / 8), kb * kW4BK);
+                    tma_prefetch_l2_2d(smp, ntl * kW4BN, kb * (kW4BK / 32));
                 }
             }
             pdl_wait();
@@ -171,6 +218,9 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                 const int tb = SPLIT ? t / S : t, ks = SPLIT ? t % S : 0;
                 const int nt = tb / a.ntm, mt = tb % a.ntm;
                 const int kb0 = SPLIT ? ks * nks / S : 0, kb1 = SPLIT ? (ks + 1) * nks / S : nks;
+                const CUtensorMap *wm, *smp;
+                int ntl;
+                seg_maps(nt, wm, smp, ntl);
                 for (int kb = kb0; kb < kb1; kb += kSub, it++) {
                     const int s = it % kW4Stages, sub = min(kSub, kb1 - kb);
                     if (it >= kW4Stages &&
@@ -182,9 +232,9 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                     for (int j = 0; j < sub; j++) {
                         const int sj = s * kSub + j;
                         tma_load_2d(sm0 + sj * kW4XBytes, &xmap, (kb + j) * kW4BK, mt * BT, full_bar(s), pol_x);
-                        tma_load_2d(smw + sj * kW4WBytes, &wmap, nt * (kW4BN / 8), (kb + j) * kW4BK, full_bar(s),
+                        tma_load_2d(smw + sj * kW4WBytes, wm, ntl * (kW4BN / 8), (kb + j) * kW4BK, full_bar(s),
                                     pol_w);
-                        tma_load_2d(sms + sj * kW4SBytes, &smap, nt * kW4BN, (kb + j) * (kW4BK / 32), full_bar(s),
+                        tma_load_2d(sms + sj * kW4SBytes, smp, ntl * kW4BN, (kb + j) * (kW4BK / 32), full_bar(s),
                                     pol_w);
                     }
                 }
@@ -291,9 +341,17 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
             tc::fence_after();
             const int tb = SPLIT ? t / S : t, ks = SPLIT ? t % S : 0;
             const int nt = tb / a.ntm, mt = tb % a.ntm;
-            const int n = nt * kW4BN + nl;
+            const int n = nt * kW4BN + nl;   // over all segments: the partials' column
             const int m0 = mt * BT;
             float* const part = SPLIT && S > 1 ? a.part + (size_t)ks * a.M * a.N : nullptr;
+            // y of this tile's segment
+            void* yseg = a.y;
+            int nseg_col = n, Nseg = a.N;
+            if constexpr (SPLIT) {
+                int t0;
+                w4_seg_out(a.seg, w4_seg_of(a.seg, nt), yseg, Nseg, t0);
+                nseg_col = n - t0 * kW4BN;
+            }
 #pragma unroll 1
             for (int c = 0; c < BT / 32; c++) {
                 uint32_t r[32];
@@ -313,9 +371,9 @@ __global__ void __launch_bounds__(kW4Threads, 1) gemm_w4a16_kernel(const W4Args 
                         if (m < a.M) {
                             const float f = __uint_as_float(r[i]);
                             if (YF32)
-                                reinterpret_cast<float*>(a.y)[(size_t)m * a.N + n] = f;
+                                reinterpret_cast<float*>(yseg)[(size_t)m * Nseg + nseg_col] = f;
                             else
-                                reinterpret_cast<__half*>(a.y)[(size_t)m * a.N + n] = __float2half_rn(f);
+                                reinterpret_cast<__half*>(yseg)[(size_t)m * Nseg + nseg_col] = __float2half_rn(f);
                         }
                     }
                 }
@@ -633,11 +691,19 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
 
 // y[i] = sum over the splits s = 0 .. S-1 of part[s][i], in split order (deterministic)
 template <bool YF32>
-__global__ void w4a16_splitk_reduce(const float* __restrict__ part, void* __restrict__ y, size_t n4, size_t stride,
-                                    int S) {
+__global__ void w4a16_splitk_reduce(const float* __restrict__ part, const W4Segs g, size_t n4, size_t stride,
+                                    int S, int N) {
     pdl_launch_dependents();
     pdl_wait();   // launched as a programmatic dependent of its GEMM: the partials are complete after this
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        // element 4i of the [M, N] partials: row m, column ncol, in the segment holding it (segments start on
+        // 128-column tiles, so a group of 4 never straddles two)
+        const size_t m = 4 * i / N;
+        const int ncol = (int)(4 * i - m * N);
+        void* y;
+        int Ns, t0;
+        w4_seg_out(g, w4_seg_of(g, ncol / kW4BN), y, Ns, t0);
+        const size_t yo = (m * Ns + (ncol - t0 * kW4BN)) / 4;
         float4 v = __ldg(reinterpret_cast<const float4*>(part) + i);
         for (int s = 1; s < S; s++) {
             const float4 u = __ldg(reinterpret_cast<const float4*>(part + (size_t)s * stride) + i);
@@ -647,12 +713,12 @@ __global__ void w4a16_splitk_reduce(const float* __restrict__ part, void* __rest
             v.w += u.w;
         }
         if (YF32) {
-            reinterpret_cast<float4*>(y)[i] = v;
+            reinterpret_cast<float4*>(y)[yo] = v;
         } else {
             uint2 h;
             h.x = pack_half2(__float2half_rn(v.x), __float2half_rn(v.y));
             h.y = pack_half2(__float2half_rn(v.z), __float2half_rn(v.w));
-            reinterpret_cast<uint2*>(y)[i] = h;
+            reinterpret_cast<uint2*>(y)[yo] = h;
         }
     }
 }
@@ -700,18 +766,35 @@ int g4b_gemm_i4(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* 
     return g4b_gemm_i4_ex(X, x_dtype, wp, scales_f16, Y, y_dtype, M, N, K, workspace, ws_bytes, 0u, stream);
 }
 
-int g4b_gemm_i4_ex(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* scales_f16, void* Y, int y_dtype,
-                   int M, int N, int K, void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream) {
-    G4B_ENTRY("gemm_i4");
-    G4B_REQUIRE((flags & ~G4B_GEMM_PDL) == 0u, G4B_E_ARG, "gemm_i4: unknown flags 0x%x", flags);
-    G4B_REQUIRE(X && wp && scales_f16 && Y, G4B_E_ARG, "gemm_i4: NULL pointer");
-    G4B_REQUIRE(x_dtype == G4B_DT_F32 || x_dtype == G4B_DT_F16, G4B_E_ARG, "gemm_i4: bad x_dtype %d", x_dtype);
-    G4B_REQUIRE(y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16, G4B_E_ARG, "gemm_i4: bad y_dtype %d", y_dtype);
-    G4B_REQUIRE(M >= 1 && N >= kW4BN && K >= kW4BK && N % kW4BN == 0 && K % kW4BK == 0, G4B_E_SHAPE,
-                "gemm_i4: need M >= 1, N %% %d == 0, K %% %d == 0 (got M=%d N=%d K=%d)", kW4BN, kW4BK, M, N, K);
-    G4B_REQUIRE((long long)M * K < (1ll << 40) && (long long)M * N < (1ll << 40), G4B_E_SHAPE, "gemm_i4: too large");
-    G4B_REQUIRE(aligned16(X) && aligned16(wp) && aligned16(scales_f16) && aligned16(Y), G4B_E_ALIGN,
-                "gemm_i4: X, wp, scales and Y must be 16-byte aligned");
+}  // extern "C"
+
+// g4b_gemm_i4_ex (one weight) and g4b_gemm_i4_fused (2-3 weights sharing X, M <= 64): every check, then the
+// launches
+static int gemm_i4_impl(const char* op, const void* X, int x_dtype, int M, int K, int nseg, const g4b_gemm_seg* segs,
+                        int y_dtype, void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream) {
+    G4B_REQUIRE((flags & ~G4B_GEMM_PDL) == 0u, G4B_E_ARG, "%s: unknown flags 0x%x", op, flags);
+    G4B_REQUIRE(X && segs, G4B_E_ARG, "%s: NULL pointer", op);
+    G4B_REQUIRE(x_dtype == G4B_DT_F32 || x_dtype == G4B_DT_F16, G4B_E_ARG, "%s: bad x_dtype %d", op, x_dtype);
+    G4B_REQUIRE(y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16, G4B_E_ARG, "%s: bad y_dtype %d", op, y_dtype);
+    G4B_REQUIRE(nseg >= 1 && nseg <= kW4MaxSeg, G4B_E_ARG, "%s: 1 to %d weights, got %d", op, kW4MaxSeg, nseg);
+    G4B_REQUIRE(nseg == 1 || M <= kW4BTSmall, G4B_E_SHAPE, "%s: several weights in one launch need M <= %d (got %d)",
+                op, kW4BTSmall, M);
+    G4B_REQUIRE(M >= 1 && K >= kW4BK && K % kW4BK == 0, G4B_E_SHAPE, "%s: need M >= 1, K %% %d == 0 (got M=%d K=%d)",
+                op, kW4BK, M, K);
+    long long Ntot = 0;
+    for (int g = 0; g < nseg; g++) {
+        const g4b_gemm_seg& sg = segs[g];
+        G4B_REQUIRE(sg.wp && sg.scales_f16 && sg.y, G4B_E_ARG, "%s: NULL pointer in weight %d", op, g);
+        G4B_REQUIRE(sg.N >= kW4BN && sg.N % kW4BN == 0, G4B_E_SHAPE, "%s: weight %d: N %% %d == 0 (got N=%d)", op, g,
+                    kW4BN, sg.N);
+        G4B_REQUIRE(aligned16(sg.wp) && aligned16(sg.scales_f16) && aligned16(sg.y), G4B_E_ALIGN,
+                    "%s: weight %d: wp, scales and Y must be 16-byte aligned", op, g);
+        Ntot += sg.N;
+    }
+    G4B_REQUIRE(Ntot <= 0x7fffffffLL && (long long)M * K < (1ll << 40) && (long long)M * Ntot < (1ll << 40),
+                G4B_E_SHAPE, "%s: too large", op);
+    G4B_REQUIRE(aligned16(X), G4B_E_ALIGN, "%s: X must be 16-byte aligned", op);
+    const int N = (int)Ntot;
     int sms = 0;
     int st = check_device(&sms);
     if (st != G4B_OK) return st;
@@ -724,22 +807,24 @@ int g4b_gemm_i4_ex(const void* X, int x_dtype, const uint32_t* wp, const uint16_
     }
     const size_t need = w4a16_ws(p);
     G4B_REQUIRE(ws_bytes >= need && (need == 0 || workspace), G4B_E_WORKSPACE,
-                "gemm_i4: f32 X needs a %zu-byte workspace (got %zu)", need, ws_bytes);
-    G4B_REQUIRE(need == 0 || aligned16(workspace), G4B_E_ALIGN, "gemm_i4: workspace must be 16-byte aligned");
+                "%s: f32 X needs a %zu-byte workspace (got %zu)", op, need, ws_bytes);
+    G4B_REQUIRE(need == 0 || aligned16(workspace), G4B_E_ALIGN, "%s: workspace must be 16-byte aligned", op);
     // encode the tensor maps first: nothing is queued until every check has passed
     const void* X16 = x_dtype == G4B_DT_F32 ? workspace : X;
-    CUtensorMap xmap, wmap, smap;
+    CUtensorMap xmap, wmap[kW4MaxSeg], smap[kW4MaxSeg];
     st = tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, X16, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, kW4BK,
                        p.bt, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st == G4B_OK)
-        st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, wp, (uint64_t)N / 8, (uint64_t)K, (uint64_t)N / 2,
-                           kW4BN / 8, kW4BK, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (st == G4B_OK)
-        st = tensor_map_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales_f16, (uint64_t)N, (uint64_t)K / 32,
-                           (uint64_t)N * 2, kW4BN, kW4BK / 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+    for (int g = 0; g < kW4MaxSeg && st == G4B_OK; g++) {
+        const g4b_gemm_seg& sg = segs[g < nseg ? g : 0];   // unused maps repeat weight 0's
+        st = tensor_map_2d(&wmap[g], CU_TENSOR_MAP_DATA_TYPE_UINT32, sg.wp, (uint64_t)sg.N / 8, (uint64_t)K,
+                           (uint64_t)sg.N / 2, kW4BN / 8, kW4BK, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st == G4B_OK)
+            st = tensor_map_2d(&smap[g], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sg.scales_f16, (uint64_t)sg.N,
+                               (uint64_t)K / 32, (uint64_t)sg.N * 2, kW4BN, kW4BK / 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
     if (st != G4B_OK) return st;
-    W4Args a;
-    a.y = Y;
+    W4Args a{};
+    a.y = segs[0].y;
     a.part = p.part_bytes ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + p.xconv_bytes) : nullptr;
     a.M = M;
     a.N = N;
@@ -748,13 +833,26 @@ int g4b_gemm_i4_ex(const void* X, int x_dtype, const uint32_t* wp, const uint16_
     a.ntm = p.ntm;
     a.S = p.S;
     a.ntiles = p.base * p.S;
+    a.seg.nseg = nseg;
+    for (int g = 0, t0 = 0; g <= kW4MaxSeg; g++) {
+        a.seg.tile0[g] = g < nseg ? t0 : (g == nseg ? t0 : 0x3fffffff);
+        if (g < nseg) {
+            a.seg.ys[g] = segs[g].y;
+            a.seg.Ns[g] = segs[g].N;
+            t0 += segs[g].N / kW4BN;
+        }
+    }
+    for (int g = nseg; g < kW4MaxSeg; g++) {
+        a.seg.ys[g] = segs[0].y;
+        a.seg.Ns[g] = segs[0].N;
+    }
     const bool yf32 = y_dtype == G4B_DT_F32;
     auto kern = p.bt == kW4BT ? (yf32 ? gemm_w4a16_kernel<true, kW4BT, false> : gemm_w4a16_kernel<false, kW4BT, false>)
                               : (yf32 ? gemm_w4a16_kernel<true, kW4BTSmall, true>
                                       : gemm_w4a16_kernel<false, kW4BTSmall, true>);
     const size_t smem = w4_smem(p.bt);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemm_i4: cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "%s: cudaFuncSetAttribute: %s", op, cudaGetErrorString(e));
     if (x_dtype == G4B_DT_F32) {
         st = cast_f32_to_f16_async(reinterpret_cast<const float*>(X), reinterpret_cast<__half*>(workspace),
                                    (size_t)M * K, s);
@@ -772,10 +870,10 @@ int g4b_gemm_i4_ex(const void* X, int x_dtype, const uint32_t* wp, const uint16_
     cfg.attrs = attr;
     // a GEMM after the f32 -> f16 cast (its own kernel) does not overlap it
     cfg.numAttrs = (flags & G4B_GEMM_PDL) && x_dtype != G4B_DT_F32 ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, kern, a, xmap, wmap, smap);
-    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemm_i4: launch: %s", cudaGetErrorString(e));
+    e = cudaLaunchKernelEx(&cfg, kern, a, xmap, wmap[0], smap[0], wmap[1], smap[1], wmap[2], smap[2]);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "%s: launch: %s", op, cudaGetErrorString(e));
     count_launch();
-    st = launch_status("gemm_i4");
+    st = launch_status(op);
     if (st != G4B_OK || p.S == 1) return st;
     // the split sum, as a programmatic dependent of the GEMM (it waits for the partials)
     const size_t n4 = (size_t)M * N / 4;
@@ -786,11 +884,28 @@ int g4b_gemm_i4_ex(const void* X, int x_dtype, const uint32_t* wp, const uint16_
     rcfg.stream = s;
     rcfg.attrs = attr;
     rcfg.numAttrs = 1;
-    e = yf32 ? cudaLaunchKernelEx(&rcfg, w4a16_splitk_reduce<true>, (const float*)a.part, Y, n4, (size_t)M * N, p.S)
-             : cudaLaunchKernelEx(&rcfg, w4a16_splitk_reduce<false>, (const float*)a.part, Y, n4, (size_t)M * N, p.S);
-    if (e != cudaSuccess) return fail(G4B_E_CUDA, "gemm_i4: split-sum launch: %s", cudaGetErrorString(e));
+    e = yf32 ? cudaLaunchKernelEx(&rcfg, w4a16_splitk_reduce<true>, (const float*)a.part, a.seg, n4, (size_t)M * N,
+                                  p.S, N)
+             : cudaLaunchKernelEx(&rcfg, w4a16_splitk_reduce<false>, (const float*)a.part, a.seg, n4, (size_t)M * N,
+                                  p.S, N);
+    if (e != cudaSuccess) return fail(G4B_E_CUDA, "%s: split-sum launch: %s", op, cudaGetErrorString(e));
     count_launch();
-    return launch_status("gemm_i4");
+    return launch_status(op);
+}
+
+extern "C" {
+
+int g4b_gemm_i4_ex(const void* X, int x_dtype, const uint32_t* wp, const uint16_t* scales_f16, void* Y, int y_dtype,
+                   int M, int N, int K, void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream) {
+    G4B_ENTRY("gemm_i4");
+    const g4b_gemm_seg one{wp, scales_f16, Y, N};
+    return gemm_i4_impl("gemm_i4", X, x_dtype, M, K, 1, &one, y_dtype, workspace, ws_bytes, flags, stream);
+}
+
+int g4b_gemm_i4_fused(const void* X, int x_dtype, int M, int K, const g4b_gemm_seg* segs, int nseg, int y_dtype,
+                      void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream) {
+    G4B_ENTRY("gemm_i4_fused");
+    return gemm_i4_impl("gemm_i4_fused", X, x_dtype, M, K, nseg, segs, y_dtype, workspace, ws_bytes, flags, stream);
 }
 
 }  // extern "C"

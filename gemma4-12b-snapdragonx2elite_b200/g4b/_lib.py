@@ -50,6 +50,11 @@ _P = C.c_void_p
 _I = C.c_int
 _F = C.c_float
 _Z = C.c_size_t
+class GemmSeg(C.Structure):
+    """g4b_gemm_seg: one weight of g4b_gemm_i4_fused."""
+    _fields_ = [("wp", C.c_void_p), ("scales_f16", C.c_void_p), ("y", C.c_void_p), ("N", C.c_int)]
+
+
 SIGNATURES = {
     "g4b_last_error": (C.c_char_p, []),
     "g4b_version": (_I, []),
@@ -71,6 +76,7 @@ SIGNATURES = {
     "g4b_gemm_i4_workspace_bytes": (_Z, [_I, _I, _I, _I]),
     "g4b_gemm_i4": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, _P]),
     "g4b_gemm_i4_ex": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _P, _Z, C.c_uint, _P]),
+    "g4b_gemm_i4_fused": (_I, [_P, _I, _I, _I, _P, _I, _I, _P, _Z, C.c_uint, _P]),
     "g4b_allreduce_buffer_bytes": (_Z, [_I, _I]),
     "g4b_allreduce_f32": (_I, [_P, _P, _I, _I, _I, _P, _P, C.c_uint, _P]),
     "g4b_comm_alloc": (_I, [_Z, C.POINTER(_P)]),

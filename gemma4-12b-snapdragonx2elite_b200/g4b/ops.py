@@ -324,6 +324,34 @@ def gemm_i4(X: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None
     return out
 
 
+def gemm_i4_fused(X: torch.Tensor, ws_: list, outs: Optional[list] = None, out_dtype: torch.dtype = torch.float16,
+                  stream: Optional[torch.cuda.Stream] = None, workspace: Optional[torch.Tensor] = None,
+                  pdl: bool = False) -> list:
+    """2-3 W4A16 GEMMs on one X [M <= 64, K] as one launch (a decode batch's q|k|v or gate|up):
+    returns [X @ dequant(W_g)] for the weights in ws_."""
+    _need(X, "X")
+    M, K = X.shape
+    if not 1 <= len(ws_) <= 3 or any(w.K != K for w in ws_):
+        raise ValueError("gemm_i4_fused: 1 to 3 weights with X's K")
+    if outs is None:
+        outs = [torch.empty((M, w.N), dtype=out_dtype, device=X.device) for w in ws_]
+    for o in outs:
+        _need(o, "out")
+    segs = (L.GemmSeg * len(ws_))()
+    for g, (w, o) in enumerate(zip(ws_, outs)):
+        segs[g].wp, segs[g].scales_f16, segs[g].y, segs[g].N = _ptr(w.wp), _ptr(w.scales16), _ptr(o), w.N
+    sh = _stream_handle(stream, X.device)
+    lib = L.load()
+    need = lib.g4b_gemm_i4_workspace_bytes(M, sum(w.N for w in ws_), K, _DT[X.dtype])
+    ws = workspace
+    if need and ws is None:
+        ws = WORKSPACES.get(X.device, sh, need, use="gemm_i4")
+    L.check("g4b_gemm_i4_fused", lib.g4b_gemm_i4_fused(
+        _ptr(X), _DT[X.dtype], M, K, ctypes.cast(segs, ctypes.c_void_p), len(ws_), _DT[outs[0].dtype], _ptr(ws),
+        ws.numel() if ws is not None else 0, L.GEMM_PDL if pdl else 0, sh))
+    return outs
+
+
 def gemm_w8a8(A8: torch.Tensor, sa: torch.Tensor, w: DeviceWeight, out: Optional[torch.Tensor] = None,
               out_dtype: torch.dtype = torch.float16, acc: Optional[torch.Tensor] = None,
               stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:

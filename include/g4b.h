@@ -381,6 +381,22 @@ G4B_API int g4b_gemm_i4_ex(const void* X, int x_dtype, const uint32_t* wp, const
                            void* Y, int y_dtype, int M, int N, int K,
                            void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream);
 
+/* 2 or 3 W4A16 GEMMs on one X as one launch, for batched decode (M <= 64): a
+ * layer's q, k and v, or gate and up -- the gemm_ds() calls the engine records
+ * back to back on the same input (src/vk_engine.py:369-379).  Weight g writes
+ * Y_g = X @ dequant(W_g) to segs[g].y [M, segs[g].N]; the column tiles of all
+ * weights share the SMs and one split-K plan, whose workspace is
+ * g4b_gemm_i4_workspace_bytes(M, sum of N, K, x_dtype).  Otherwise as
+ * g4b_gemm_i4_ex (flags, dtypes, alignment). */
+typedef struct {
+    const uint32_t* wp;            /* packed words [K, N/8] */
+    const uint16_t* scales_f16;    /* f16 block scales [K/32, N] */
+    void* y;                       /* [M, N], y_dtype */
+    int N;                         /* a multiple of 128 */
+} g4b_gemm_seg;
+G4B_API int g4b_gemm_i4_fused(const void* X, int x_dtype, int M, int K, const g4b_gemm_seg* segs, int nseg,
+                              int y_dtype, void* workspace, size_t ws_bytes, unsigned flags, g4b_stream_t stream);
+
 /* W8A8 prefill GEMM (PREFILL_I8), vk/coopgemm_w8a8.comp:18-37, dispatched by
  * gmm() after cast_i8 (src/vk_engine.py:391-397):
  *     C[m, n] = sum_k A8[m, k] * W8[k, n]                 (exact int32)

@@ -185,3 +185,30 @@ def test_gemm_pdl_chain_gives_the_same_bits():
     for a, b in zip(ref, outs[True]):
         assert torch.equal(a, b)
     del gr
+
+
+@pytest.mark.parametrize("M", [1, 8, 64])
+@pytest.mark.parametrize("shapes", [[(512, 3840), (256, 3840), (256, 3840)], [(1024, 512), (1024, 512)]])
+def test_gemm_i4_fused_weights(M, shapes):
+    """g4b_gemm_i4_fused: 2-3 weights on one X in one launch (a decode batch's q|k|v, gate|up), each output
+    against the fp64 product of the same f16 operands and against its own g4b_gemm_i4 call."""
+    K = shapes[0][1]
+    pws = [_dw(N, K, seed=M + N + g) for g, (N, _) in enumerate(shapes)]
+    X16 = torch.from_numpy(activations(M, K, seed=9).astype(np.float16)).to(DEV)
+    outs = ops.gemm_i4_fused(X16, [dw for _, dw in pws], out_dtype=torch.float32, pdl=True)
+    again = ops.gemm_i4_fused(X16, [dw for _, dw in pws], out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+    for g, ((pw, dw), y, y2) in enumerate(zip(pws, outs, again)):
+        assert torch.equal(y, y2)
+        ref = (X16.double() @ ops.dequant_i4(dw, out_dtype=torch.float16).double()).cpu().numpy()
+        assert_close(y.cpu().numpy(), ref, f"fused weight {g} M={M}", guard=LONG_K_GUARD)
+        single = ops.gemm_i4(X16, dw, out_dtype=torch.float32)
+        assert_close(y.cpu().numpy(), single.cpu().numpy(), f"fused vs single, weight {g} M={M}", guard=LONG_K_GUARD)
+
+
+def test_gemm_i4_fused_rejects_large_m():
+    pws = [_dw(256, 512, seed=g) for g in range(2)]
+    X16 = torch.zeros((65, 512), dtype=torch.float16, device=DEV)
+    with pytest.raises(Exception, match="M <= 64"):
+        ops.gemm_i4_fused(X16, [dw for _, dw in pws])
