@@ -1107,6 +1107,15 @@ struct ChainStep {
     // run's epoch, into slot [rank] of region yreg of every rank's exchange buffer; xreg >= 0: x is
     // the rank-order sum of the world slots of region xreg (the all-reduce of the previous step's y)
     int xreg, yreg;
+    // forwarded x (one GPU): yfw >= 0: every written y value of segment 0 is also stored, tagged with
+    // the run's epoch, at word yfw + n of the chain's forward area; xfw >= 0: x is the previous step's
+    // segment-0 output read from those words (each x slice waits only for its own words, not for the
+    // whole previous step)
+    int xfw, yfw;
+    // the activation warp's step wait covers the counts of steps wlo .. j-1 (wlo < j-1 when the steps
+    // in between read forwarded x and so never waited on a count themselves); xind: none of the chain's
+    // steps writes x, so its first slice may be loaded before the wait
+    int wlo, xind;
     // completion count of the step: its tiles, plus the slices of h_out its loads write (NORMADD)
     int done;
     // fused element-wise work on x (g4b_chain_xform; one rank only): kind, an RMSNORM over a vector
@@ -1136,6 +1145,7 @@ struct ChainArgs {
     unsigned long long* partial;  // [2][2 * G][kStTN] {f32 bits, step tag} words: CTA c's partials of its
                                   // first and its last tile, by step parity
     unsigned long long* const* peers;  // [world] exchange buffers (this rank's own at [rank]); null if world 1
+    unsigned long long* fwd;           // the forward area: {f32 bits, epoch} words of forwarded outputs
     int nsteps, stage_bytes, s_bytes, maxtiles, G, rank, world;
     int pf_items;             // L2 prefetch distance: items ahead of the TMA producer (0 = off)
 };
@@ -1159,17 +1169,40 @@ __device__ __forceinline__ void load8(const void* p, int r0, float (&v)[8]) {
     }
 }
 
-// A chain stage's f16 x slice: 32-row block b at bytes [128 b, 128 b + 64), repeated at +64, so the
-// consumers read a block's words from any rotation without wrapping.  Lane l holds rows 8l .. 8l+7.
+// A chain stage's x slice, 1 KB either way, then the slice's 8 block sums (f32):
+//   f16 x: 32-row block b at bytes [128 b, 128 b + 64), repeated at +64, so the consumers read a
+//          block's words from any rotation without wrapping;
+//   f32 x: block b at [128 b, 128 b + 128): 16 words f16x2(hi) of its row pairs, then the 16 words
+//          f16x2(lo), hi = f16(x) and lo = f16(x - hi) -- the split the tensor cores take f32 x in,
+//          made once here instead of by every consumer lane.
+// Lane l holds rows 8l .. 8l+7 (block l/4).
+constexpr int kChainXBytes = kM1Rows * 4;
+constexpr int kChainXSumBytes = 32;
 __device__ __forceinline__ int chain_xoff16(int lane) { return (lane >> 2) * 128 + (lane & 3) * 16; }
 
-// a lane's 8 activations into a stage's x slice (rows 8*lane .. +8), in the chain's x dtype
+// a lane's 8 activations into a stage's x slice (rows 8*lane .. +8), in the chain's x dtype; for f32 x
+// also the slice's block sums (a block's 32 values added in a fixed order: a lane's 8 in row order,
+// then lanes l^1, l^2) for the -8 X correction -- f16 x leaves them to the consumers, which read the
+// 32 values anyway
 template <bool F32>
 __device__ __forceinline__ void store8(uint8_t* dst, int lane, const float (&v)[8]) {
     if constexpr (F32) {
-        float4* d4 = reinterpret_cast<float4*>(dst + 32 * lane);
-        d4[0] = make_float4(v[0], v[1], v[2], v[3]);
-        d4[1] = make_float4(v[4], v[5], v[6], v[7]);
+        uint4 hi, lo;
+        uint32_t* hw = &hi.x;
+        uint32_t* lw = &lo.x;
+        #pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const __half ha = __float2half_rn(v[2 * k]), hb = __float2half_rn(v[2 * k + 1]);
+            hw[k] = pack_half2(ha, hb);
+            lw[k] = pack_half2(__float2half_rn(v[2 * k] - __half2float(ha)),
+                               __float2half_rn(v[2 * k + 1] - __half2float(hb)));
+        }
+        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane)) = hi;
+        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane) + 64) = lo;
+        float s = ((((((v[0] + v[1]) + v[2]) + v[3]) + v[4]) + v[5]) + v[6]) + v[7];
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if ((lane & 3) == 0) reinterpret_cast<float*>(dst + kChainXBytes)[lane >> 2] = s;
     } else {
         uint4 h;
         h.x = pack_half2(__float2half_rn(v[0]), __float2half_rn(v[1]));
@@ -1178,6 +1211,20 @@ __device__ __forceinline__ void store8(uint8_t* dst, int lane, const float (&v)[
         h.w = pack_half2(__float2half_rn(v[6]), __float2half_rn(v[7]));
         *reinterpret_cast<uint4*>(dst + chain_xoff16(lane)) = h;
         *reinterpret_cast<uint4*>(dst + chain_xoff16(lane) + 64) = h;
+    }
+}
+
+// a lane's 8 consecutive activations (rows 8*lane .. +8) of an f32 or f16 slice as f32
+template <bool F32>
+__device__ __forceinline__ void unpack8(const uint4 (&u)[F32 ? 2 : 1], float (&v)[8]) {
+    if constexpr (F32) {
+        v[0] = __uint_as_float(u[0].x); v[1] = __uint_as_float(u[0].y);
+        v[2] = __uint_as_float(u[0].z); v[3] = __uint_as_float(u[0].w);
+        v[4] = __uint_as_float(u[1].x); v[5] = __uint_as_float(u[1].y);
+        v[6] = __uint_as_float(u[1].z); v[7] = __uint_as_float(u[1].w);
+    } else {
+        v[0] = h_lo(u[0].x); v[1] = h_hi(u[0].x); v[2] = h_lo(u[0].y); v[3] = h_hi(u[0].y);
+        v[4] = h_lo(u[0].z); v[5] = h_hi(u[0].z); v[6] = h_lo(u[0].w); v[7] = h_hi(u[0].w);
     }
 }
 
@@ -1370,7 +1417,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         tma_prefetch_l2_2d(&sm[sg], lt * (kStTN * ssz / 8), o * 8);
                         // the item's x slice too, so that its load after the step boundary hits L2 (the
                         // lines stay coherent with whatever an earlier step writes to them later)
-                        if (d.x && d.xreg < 0 && d.xf_kind == kXfNone)
+                        if (d.x && d.xreg < 0 && d.xfw < 0 && d.xf_kind == kXfNone)
                             bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(d.x) + (size_t)o * kM1Rows * esz,
                                              kM1Rows * esz);
                     }
@@ -1391,16 +1438,33 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
         bool stop = false;
         for (int j = 0; j < nsteps && !stop; j++) {
             const ChainStep* dj = ch.steps + j;
-            const int noct = dj->noct, K = dj->K, xreg = dj->xreg;
+            const int noct = dj->noct, K = dj->K, xreg = dj->xreg, xfw = dj->xfw;
             const uint8_t* x = reinterpret_cast<const uint8_t*>(dj->x);
             int ibeg, iend;
             my_range(*dj, ibeg, iend);
-            // an all-reduce input carries its own readiness (the epoch in every word): no step wait
-            if (iend > ibeg && j > 0 && xreg < 0) {
-                const bool ok = chain_wait_count(&ch.sync[j - 1], (unsigned)ch.steps[j - 1].done, gabort, abort_flag);
-                if (!__all_sync(0xffffffffu, ok)) break;
-            }
             const int xk = dj->xf_kind;
+            // an x that no step writes: its first slice is loaded before the step wait, so that the
+            // wait's end is followed by shared-memory stores only
+            constexpr int kPreVecs = kM1Rows * esz / 512;  // 16-byte loads per lane for one slice
+            uint4 pre[kPreVecs];
+            const bool hoist = dj->xind && xk == kXfNone && xreg < 0 && xfw < 0 && iend > ibeg;
+            if (hoist) {
+                const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)(ibeg % noct) * kM1Rows * esz);
+                #pragma unroll
+                for (int b = 0; b < kPreVecs; b++) pre[b] = __ldcg(src + kPreVecs * lane + b);
+            }
+            // an all-reduce input and a forwarded x carry their own readiness (the epoch in every word):
+            // no step wait.  Otherwise wait for the counts of steps wlo .. j-1 at once, a lane per step.
+            if (iend > ibeg && j > 0 && xreg < 0 && xfw < 0) {
+                bool ok = true;
+                for (int k0 = dj->wlo; k0 < j && ok; k0 += 32) {
+                    const int k = k0 + lane;
+                    const bool okl = k < j ? chain_wait_count(&ch.sync[k], (unsigned)ch.steps[k].done, gabort, abort_flag)
+                                           : true;
+                    ok = __all_sync(0xffffffffu, okl);
+                }
+                if (!ok) break;
+            }
             // the step's norm scales, once per step: from the producer's tile sums (summed in a fixed
             // lane order) or, for a vector the chain did not write, from the vector itself.  The sums'
             // loads are issued here and only reduced after the first slice's loads are in flight, so
@@ -1505,16 +1569,58 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         }
                     }
                     store8<XF32>(dst, lane, v);
+                } else if (xfw >= 0) {
+                    // rows o*256 + 8*lane .. +8 of the previous step's first output: its words, polled
+                    // until they carry this run's epoch (bounded); only words still without it are
+                    // loaded again
+                    const unsigned long long* src = ch.fwd + xfw + (size_t)o * kM1Rows + 8 * lane;
+                    unsigned long long w[8];
+                    #pragma unroll
+                    for (int e = 0; e < 8; e++) w[e] = ld_relaxed_gpu_u64(src + e);
+                    bool ok = true;
+                    uint64_t t0 = 0;
+                    for (;;) {
+                        bool all = true;
+                        #pragma unroll
+                        for (int e = 0; e < 8; e++) all = all && (unsigned)(w[e] >> 32) == epoch;
+                        if (all) break;
+                        if (t0 == 0) t0 = global_ns();
+                        if (*abort_flag || *(volatile unsigned*)gabort) {
+                            ok = false;
+                            break;
+                        }
+                        if (global_ns() - t0 > kWaitLimitNs) {
+                            atomicOr(&g_gemv_status, kStatusTimeout);
+                            atomicExch(gabort, 1u);
+                            ok = false;
+                            break;
+                        }
+                        #pragma unroll
+                        for (int e = 0; e < 8; e++)
+                            if ((unsigned)(w[e] >> 32) != epoch) w[e] = ld_relaxed_gpu_u64(src + e);
+                    }
+                    if (!__all_sync(0xffffffffu, ok)) {
+                        if (lane == 0) *abort_flag = 1;
+                        stop = true;
+                        break;
+                    }
+                    float v[8];
+                    #pragma unroll
+                    for (int e = 0; e < 8; e++) v[e] = __uint_as_float((unsigned)w[e]);
+                    store8<XF32>(dst, lane, v);
                 } else if (xreg < 0) {
                     const uint8_t* src = x + (size_t)o * kM1Rows * esz;
+                    uint4 u[kPreVecs];
+                    #pragma unroll
+                    for (int b = 0; b < kPreVecs; b++)
+                        u[b] = hoist && it == ibeg ? pre[b] : __ldcg(reinterpret_cast<const uint4*>(src) + kPreVecs * lane + b);
                     if constexpr (XF32) {
-                        #pragma unroll
-                        for (int b = lane * 16; b < kM1Rows * esz; b += 512)
-                            *reinterpret_cast<uint4*>(dst + b) = __ldcg(reinterpret_cast<const uint4*>(src + b));
+                        float v[8];
+                        unpack8<XF32>(u, v);
+                        store8<XF32>(dst, lane, v);
                     } else {
-                        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(src + lane * 16));
-                        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane)) = v;
-                        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane) + 64) = v;
+                        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane)) = u[0];
+                        *reinterpret_cast<uint4*>(dst + chain_xoff16(lane) + 64) = u[0];
                     }
                 } else {
                     // rows o*256 + 8*lane .. +8: the world ranks' words, polled until they carry this
@@ -1621,6 +1727,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         const size_t at = (size_t)d.yreg + (size_t)ch.rank * sgm.N + n;
                         for (int p = 0; p < ch.world; p++) st_relaxed_sys_u64(s_peers[p] + at, w);
                     }
+                    // the next step reads segment 0 as forwarded words (segment 1's first tile is
+                    // 1 << 30 when the step has one segment)
+                    if (d.yfw >= 0 && t < d.seg1.tile0)
+                        st_relaxed_gpu_u64(ch.fwd + d.yfw + n, ((unsigned long long)epoch << 32) | __float_as_uint(y));
                 }
             };
             // the tile sums a segment-0 tile of this step hands to the next step's norm: every thread
@@ -1744,19 +1854,17 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                     const uint8_t* st = smem + (size_t)s * stage_bytes;
                     const uint8_t* sc = st + kM1WBytes;
                     const uint8_t* xs = sc + s_bytes;
-                    // block sums X[b] of the stage's 8 blocks: lane l sums rows 8l..8l+7
-                    float xsum;
-                    if constexpr (XF32) {
-                        const float4 v0 = *reinterpret_cast<const float4*>(xs + lane * 32);
-                        const float4 v1 = *reinterpret_cast<const float4*>(xs + lane * 32 + 16);
-                        xsum = ((((((v0.x + v0.y) + v0.z) + v0.w) + v1.x) + v1.y) + v1.z) + v1.w;
-                    } else {
+                    // block sums X[b] of the slice: stored with it by the activation warp (f32 x), or
+                    // summed here, lane l over rows 8l..8l+7 (f16 x)
+                    const float* xss = reinterpret_cast<const float*>(xs + kChainXBytes);
+                    float xsum = 0.f;
+                    if constexpr (!XF32) {
                         const uint4 v = *reinterpret_cast<const uint4*>(xs + chain_xoff16(lane));
                         xsum = ((((((h_lo(v.x) + h_hi(v.x)) + h_lo(v.y)) + h_hi(v.y)) + h_lo(v.z)) + h_hi(v.z)) + h_lo(v.w)) +
                                h_hi(v.w);
+                        xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
+                        xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
                     }
-                    xsum += __shfl_xor_sync(0xffffffffu, xsum, 1);
-                    xsum += __shfl_xor_sync(0xffffffffu, xsum, 2);
                     #pragma unroll 1
                     for (int pass = 0; pass < NPASS; pass++) {
                         // ldmatrix row of this lane: block and rotated row (swizzle phase differs per lane)
@@ -1776,9 +1884,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         uint32_t xb0, xb1, xoff;
                         if constexpr (XF32) {
                             const bool mine = (g >> 1) == q;
-                            xb0 = mine ? smem_u32(xs) + (uint32_t)((4 * pass + q) * 128) : smem_u32(s_zero);
+                            xb0 = (mine ? smem_u32(xs) + (uint32_t)((4 * pass + q) * 128) : smem_u32(s_zero)) +
+                                  ((g & 1) ? 64u : 0u);
                             xb1 = xb0;
-                            xoff = (uint32_t)(8 * q);
+                            xoff = (uint32_t)(4 * q);
                         } else {
                             // each 32-row block of x sits twice in a row (128 bytes), so the rotated
                             // word (q + pp) is read at a constant offset from here: no wrap to compute
@@ -1801,13 +1910,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                                 const int pp = p + ss;
                                 uint32_t b0, b1;
                                 if constexpr (XF32) {
-                                    const uint32_t o0 = (xoff + 16u * pp) & 127u, o1 = (xoff + 16u * pp + 8u) & 127u;
-                                    float2 xa, xb;
-                                    asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(xa.x), "=f"(xa.y) : "r"(xb0 + o0));
-                                    asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(xb.x), "=f"(xb.y) : "r"(xb1 + o1));
-                                    const bool lo = (g & 1) != 0;
-                                    b0 = split_pair(xa.x, xa.y, lo);
-                                    b1 = split_pair(xb.x, xb.y, lo);
+                                    // the pre-split f16 words of row pairs (q + 2pp) and (q + 2pp + 1) mod 16
+                                    // of the block: hi words for even g, lo words (at +64) for odd g
+                                    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(xb0 + ((xoff + 8u * pp) & 63u)));
+                                    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(xb1 + ((xoff + 8u * pp + 4u) & 63u)));
                                 } else {
                                     asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b0) : "r"(xb0 + 4u * pp));
                                     asm volatile("ld.shared.b32 %0, [%1];" : "=r"(b1) : "r"(xb1 + 4u * pp));
@@ -1820,8 +1926,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
                         // per-block scale, 2^E and -8 X correction, in f32
                         int blk0, blk1;
                         if constexpr (XF32) { blk0 = 4 * pass + q; blk1 = blk0; } else { blk0 = 2 * q; blk1 = 2 * q + 1; }
-                        const float X0 = __shfl_sync(0xffffffffu, xsum, 4 * blk0);
-                        const float X1 = __shfl_sync(0xffffffffu, xsum, 4 * blk1);
+                        float X0, X1;
+                        if constexpr (XF32) {
+                            X0 = xss[blk0];
+                            X1 = xss[blk1];
+                        } else {
+                            X0 = __shfl_sync(0xffffffffu, xsum, 4 * blk0);
+                            X1 = __shfl_sync(0xffffffffu, xsum, 4 * blk1);
+                        }
                         // scales of columns colA .. colA+3 in blocks blk0 / blk1
                         float s0[4], s1[4];
                         if constexpr (SFMT == G4B_SCALE_F16) {
@@ -3127,6 +3239,7 @@ struct g4b_gemv_chain {
     int grid = 0, stage_bytes = 0, s_bytes = 0, maxtiles = 0, rank = 0, world = 1;
     int pf_items = 0;              // L2 prefetch distance in items (G4B_CHAIN_PREFETCH at create time)
     size_t smem = 0, sync_bytes = 0, ws_bytes = 0;
+    size_t fwd_at = 0;             // workspace offset of the forward area (forwarded outputs' words)
     void* const* peers = nullptr;  // device array of the world exchange buffers (tensor parallel)
     // device: [nsteps][6] CUtensorMap, then [nsteps] ChainStep, then the steps' range / cspan tables
     void* plan = nullptr;
@@ -3385,6 +3498,14 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
     size_t sums_words = 0;
     int grid = 1, maxtiles = 0;
     long long region = 0;  // next free exchange word
+    // Forwarded x: a step whose x is the step before's first output (same dtype, no element-wise work,
+    // no all-reduce between them) reads it as epoch-tagged words in the workspace, each 256-row slice
+    // as soon as its own words are stored.  G4B_CHAIN_FORWARD=0 at creation turns it off (and the early
+    // load of an x no step writes).
+    const char* fwd_env = getenv("G4B_CHAIN_FORWARD");
+    const bool fwd_on = x_dtype == y_dtype && !(fwd_env && atoi(fwd_env) == 0);
+    const bool early_on = !(fwd_env && atoi(fwd_env) == 0);
+    long long fwd_words = 0;
     for (int j = 0; j < nsteps; j++) {
         const g4b_gemv_chain_step& cs = steps[j];
         ChainStep& d = hsteps[j];
@@ -3392,10 +3513,22 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
         d.x = cs.x;
         d.xreg = -1;
         d.yreg = -1;
+        d.xfw = -1;
+        d.yfw = -1;
+        d.wlo = j > 0 ? j - 1 : 0;
         if (j > 0 && (steps[j - 1].flags & G4B_CHAIN_ALLREDUCE)) d.xreg = hsteps[j - 1].yreg;
         if (cs.flags & G4B_CHAIN_ALLREDUCE) {
             d.yreg = (int)region;
             region += (long long)world * cs.seg[0].N;
+        }
+        if (fwd_on && j > 0 && cs.x && cs.x == steps[j - 1].seg[0].y && !(xf && xf[j].kind != G4B_XF_NONE) &&
+            !(steps[j - 1].flags & G4B_CHAIN_ALLREDUCE) && cs.K <= steps[j - 1].seg[0].N) {
+            ChainStep& pd = hsteps[j - 1];
+            if (pd.yfw < 0) {
+                pd.yfw = (int)fwd_words;
+                fwd_words += (steps[j - 1].seg[0].N + 31) & ~31;  // 256-byte aligned regions
+            }
+            d.xfw = pd.yfw;
         }
         TcSeg* dst[kTcMaxSeg] = {&d.seg0, &d.seg1, &d.seg2};
         const uint32_t* wps[kTcMaxSeg];
@@ -3480,8 +3613,34 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
             if (st != G4B_OK) return st;
         }
     }
-    // x slice: f32, or f16 stored twice over (each block repeated, see chain_xoff16): 1 KB either way
-    const int stage_bytes = (kM1WBytes + 8 * kStTN * ssz + kM1Rows * 4 + 1023) & ~1023;
+    G4B_REQUIRE(fwd_words < (1LL << 31), G4B_E_SHAPE, "gemv_chain_create: the forwarded outputs are too long");
+    // the step waits: back over the steps that read forwarded x (they waited on no count), so that a
+    // waiting step still covers every step before it
+    const int ysz = y_dtype == G4B_DT_F32 ? 4 : 2, xsz = xf32 ? 4 : 2;
+    for (int j = 1; j < nsteps; j++) {
+        int lo = j - 1;
+        while (lo > 0 && hsteps[lo].xfw >= 0) lo--;
+        hsteps[j].wlo = lo;
+        // an x no step writes (no output or h_out range overlaps it) may be loaded before the wait
+        const ChainStep& d = hsteps[j];
+        if (!early_on || !d.x || d.xreg >= 0 || d.xfw >= 0 || d.xf_kind != kXfNone) continue;
+        const uintptr_t x0 = reinterpret_cast<uintptr_t>(d.x), x1 = x0 + (uintptr_t)d.K * xsz;
+        bool written = false;
+        for (int k = 0; k < nsteps && !written; k++) {
+            for (int i = 0; i < steps[k].nseg && !written; i++) {
+                const uintptr_t y0 = reinterpret_cast<uintptr_t>(steps[k].seg[i].y);
+                written = y0 < x1 && x0 < y0 + (uintptr_t)steps[k].seg[i].N * ysz;
+            }
+            if (!written && hsteps[k].xf_kind == kXfNormAdd) {
+                const uintptr_t h0 = reinterpret_cast<uintptr_t>(hsteps[k].xf_hout);
+                written = h0 < x1 && x0 < h0 + (uintptr_t)hsteps[k].K * 4;
+            }
+        }
+        hsteps[j].xind = written ? 0 : 1;
+    }
+    // x slice: f32 as f16 hi | lo words, or f16 stored twice over (see chain_xoff16): 1 KB either way,
+    // then (f32 x) its 8 block sums
+    const int stage_bytes = (kM1WBytes + 8 * kStTN * ssz + kChainXBytes + (xf32 ? kChainXSumBytes : 0) + 1023) & ~1023;
     const size_t smem = (size_t)kM1Stages * stage_bytes + 1024;
     int resident = 0;
     st = chain_prepare(xf32, scale_fmt, y_dtype == G4B_DT_F32, smem, &resident);
@@ -3529,7 +3688,8 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
     c->maxtiles = maxtiles;
     c->smem = smem;
     c->sync_bytes = ((size_t)(nsteps + 3) * sizeof(unsigned) + 255) & ~(size_t)255;
-    c->ws_bytes = c->sync_bytes + (size_t)2 * 2 * grid * kStTN * sizeof(unsigned long long);
+    c->fwd_at = c->sync_bytes + (size_t)2 * 2 * grid * kStTN * sizeof(unsigned long long);
+    c->ws_bytes = c->fwd_at + (size_t)fwd_words * sizeof(unsigned long long);
     c->plan = plan;
     c->peers = peers_dev;
     c->rank = rank;
@@ -3567,6 +3727,7 @@ int g4b_gemv_chain_run_ex(const g4b_gemv_chain* chain, void* workspace, size_t w
     uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
     ch.sync = reinterpret_cast<unsigned*>(ws);
     ch.partial = reinterpret_cast<unsigned long long*>(ws + chain->sync_bytes);
+    ch.fwd = reinterpret_cast<unsigned long long*>(ws + chain->fwd_at);
     ch.peers = reinterpret_cast<unsigned long long* const*>(chain->peers);
     ch.nsteps = chain->nsteps;
     ch.stage_bytes = chain->stage_bytes;

@@ -147,6 +147,48 @@ def test_chain_repeat_and_graph_replay_are_identical():
     chain.close()
 
 
+@pytest.mark.parametrize("dt", [torch.float32, torch.float16])
+def test_forwarded_x_gives_the_bits_of_the_whole_step_wait(dt, monkeypatch):
+    """A step whose x is the step before's first output reads that output as
+    epoch-tagged words, each 256-row slice as soon as its own words are stored
+    (forwarded x); with G4B_CHAIN_FORWARD=0 at creation every step instead
+    waits for the whole step before it and loads x from memory.  Both give the
+    same bits, run after run.  Two extra steps: one reading an output from two
+    steps back after a run of forwarded steps (its wait then covers every step
+    before it), and one forwarded from that."""
+    steps, packed, _ = _layer_chain(2, dt, H=512, Q=1024, F=2048, V=4096, fp8=False, seed=13)
+    down = steps[-2][2][0]
+    e_w = _packed(768, down.numel(), seed=901, std=down.numel() ** -0.5)
+    e_out = torch.empty(768, dtype=dt, device=DEV)
+    f_w = _packed(512, 768, seed=902, std=768 ** -0.5)
+    f_out = torch.empty(512, dtype=dt, device=DEV)
+    steps = steps + [(down, [e_w[1]], [e_out]), (e_out, [f_w[1]], [f_out])]
+    outs = [o for _, _, oo in steps for o in oo]
+    runs = []
+    for fwd in ("1", "0"):
+        monkeypatch.setenv("G4B_CHAIN_FORWARD", fwd)
+        chain = ops.GemvChain(steps)
+        got = []
+        for _ in range(2):
+            for o in outs:
+                o.fill_(float("nan"))
+            chain.run()
+            torch.cuda.synchronize()
+            got.append([o.clone() for o in outs])
+        assert all(torch.equal(a, b) for a, b in zip(*got)), f"forward={fwd}: runs differ"
+        assert L.query(L.Q_KERNEL_STATUS) == 0
+        chain.close()
+        runs.append(got[0])
+    for k, (a, b) in enumerate(zip(*runs)):
+        assert torch.equal(a, b), f"output {k}: forwarded x differs from the whole-step wait"
+    sep = _run_separately(steps[-2:], dt)
+    tag = "f16" if dt == torch.float16 else "f32"
+    _assert_same_up_to_order(e_out, sep[0][0], f"two steps back {tag}")
+    _assert_same_up_to_order(f_out, sep[1][0], f"forwarded from it {tag}")
+    x32 = down.float().cpu().numpy()
+    assert_close(e_out.float().cpu().numpy(), _oracle(e_w[0], x32).astype(np.float32), f"two steps back {tag}")
+
+
 @pytest.mark.parametrize("fp8", [False, True])
 def test_chain_config2_shapes(fp8):
     """Two full-size layers of the configs[1] stack and the full lm_head, f16
