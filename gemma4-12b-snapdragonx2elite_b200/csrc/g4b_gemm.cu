@@ -27,6 +27,7 @@
 // Shared-memory stage s and TMEM A stage s are recycled together: the MMA's
 // commit on empty[s] frees both.
 #include <algorithm>
+#include <cstdlib>
 
 #include "g4b_tcgen05.cuh"
 
@@ -438,18 +439,38 @@ static_assert(256 + 32 * kS8Stages <= 512, "TMEM budget");
 // Tile t is (token tile t / ntn, column tile t % ntn): the CTAs resident at once share a few
 // activation panels and sweep every column tile, so the whole int8 weight (59 MB at config 4)
 // stays in L2 across waves and each activation panel is read from DRAM about once.
+//
+// Work units: the first nfull units are whole tiles; when the tiles leave a last wave that fills at most a
+// quarter of the CTAs (W8A8), each tile of that wave runs as four units of 64 tokens instead (unit
+// nfull + 4 i + sub: token rows sub * 64 .. +64 of tile nfull + i), so the last wave ends in about a
+// quarter of a tile's time instead of a whole one.  Every unit still owns its outputs: no partial sums.
+constexpr int kS8Sub = 4;
+constexpr int kS8SubT = kS8BT / kS8Sub;                 // tokens per quarter unit
 struct S8Args {
     void* y;
     int32_t* c;           // nullable raw accumulators
     const float* sa;      // [M]
     const uint16_t* sw;   // [N] f16
-    int M, N, K, nkb, ntm, ntiles;
+    int M, N, K, nkb, ntm, ntiles, nfull, nunits;
 };
+
+// unit u -> token tile, column tile and quarter (-1: the whole tile)
+__device__ __forceinline__ void s8_unit(const S8Args& a, int u, int& mt, int& nt, int& sub) {
+    int t = u;
+    sub = -1;
+    if (u >= a.nfull) {
+        t = a.nfull + (u - a.nfull) / kS8Sub;
+        sub = (u - a.nfull) % kS8Sub;
+    }
+    const int ntn = a.ntiles / a.ntm;
+    mt = t / ntn;
+    nt = t % ntn;
+}
 
 template <bool W4, bool YF32>
 __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
     gemm_s8_kernel(const S8Args a, const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap wmap,
-                   const __grid_constant__ CUtensorMap rmap) {
+                   const __grid_constant__ CUtensorMap rmap, const __grid_constant__ CUtensorMap amap_q) {
     using Cfg = S8Cfg<W4>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t bars[3 * kS8Stages + 5];
@@ -500,6 +521,7 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
             prefetch_tensor_map(&amap);
             prefetch_tensor_map(&wmap);
             if (W4) prefetch_tensor_map(&rmap);
+            if (a.nunits > a.nfull) prefetch_tensor_map(&amap_q);
             // the weights are swept again by every wave of tiles: keep them in L2; an activation panel
             // is read by the CTAs of one wave only (token-tile-major order), so it may go first
             uint64_t pol_keep;
@@ -507,8 +529,9 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
             const uint64_t pol_once = l2_evict_first_policy();
             int it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x) {
-                const int ntn = a.ntiles / a.ntm, mt = t / ntn, nt = t % ntn;  // token-tile major: see S8Args
+            for (int u = blockIdx.x; ok && u < a.nunits; u += gridDim.x) {
+                int mt, nt, sub;
+                s8_unit(a, u, mt, nt, sub);  // token-tile major: see S8Args
                 for (int kb = 0; kb < nks; kb++, it++) {
                     const int s = it % kS8Stages;
                     if (it >= kS8Stages &&
@@ -516,8 +539,14 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(full_bar(s), Cfg::kStageBytes);
-                    tma_load_2d(sm0 + s * kS8ABytes, &amap, kb * kS8BK, mt * kS8BT, full_bar(s), pol_once);
+                    if (sub < 0) {
+                        mbar_arrive_expect_tx(full_bar(s), Cfg::kStageBytes);
+                        tma_load_2d(sm0 + s * kS8ABytes, &amap, kb * kS8BK, mt * kS8BT, full_bar(s), pol_once);
+                    } else {
+                        mbar_arrive_expect_tx(full_bar(s), Cfg::kStageBytes - kS8ABytes + kS8ABytes / kS8Sub);
+                        tma_load_2d(sm0 + s * kS8ABytes, &amap_q, kb * kS8BK, mt * kS8BT + sub * kS8SubT, full_bar(s),
+                                    pol_once);
+                    }
                     if (W4) {
                         const uint32_t dst = smw + s * Cfg::kWBytes;
                         tma_load_2d(dst, &wmap, nt * (kS8BN / 8), kb * kS8BK, full_bar(s), pol_keep);
@@ -534,10 +563,12 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
         // ------------------------------------------------------- MMA issuer
         if (lane == 0) {
             // D s32, A/B s8; A MN-major from shared memory (W8A8) or K-major from TMEM (W4A8)
-            constexpr uint32_t idesc = tc::idesc(2, 1, 1, W4 ? 0 : 1, 0, kS8BT, kS8BN);
+            constexpr uint32_t idesc_full = tc::idesc(2, 1, 1, W4 ? 0 : 1, 0, kS8BT, kS8BN);
+            constexpr uint32_t idesc_q = tc::idesc(2, 1, 1, W4 ? 0 : 1, 0, kS8SubT, kS8BN);
             int it = 0, tc_i = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x, tc_i++) {
+            for (int u = blockIdx.x; ok && u < a.nunits; u += gridDim.x, tc_i++) {
+                const uint32_t idesc = u < a.nfull ? idesc_full : idesc_q;
                 const int buf = tc_i % Cfg::kAccBufs;
                 const uint32_t use = (uint32_t)(tc_i / Cfg::kAccBufs);
                 if (!mbar_wait(dempty_bar(buf), (use & 1) ^ 1, abort_flag, &g_gemm_status)) break;
@@ -583,7 +614,7 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         int it = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < a.ntiles; t += gridDim.x) {
+        for (int u = blockIdx.x; ok && u < a.nunits; u += gridDim.x) {
             for (int kb = 0; kb < nks; kb++, it++) {
                 const int s = it % kS8Stages;
                 if (!mbar_wait(full_bar(s), (it / kS8Stages) & 1, abort_flag, &g_gemm_status)) {
@@ -643,18 +674,20 @@ __global__ void __launch_bounds__(S8Cfg<W4>::kThreads, 1)
         const int nl = q * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         int tc_i = 0;
-        for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, tc_i++) {
+        for (int u = blockIdx.x; u < a.nunits; u += gridDim.x, tc_i++) {
             const int buf = tc_i % Cfg::kAccBufs;
             const uint32_t use = (uint32_t)(tc_i / Cfg::kAccBufs);
             if (!mbar_wait(dfull_bar(buf), use & 1, abort_flag, &g_gemm_status)) break;
             tc::fence_after();
-            const int ntn = a.ntiles / a.ntm, mt = t / ntn, nt = t % ntn;  // token-tile major: see S8Args
+            int mt, nt, sub;
+            s8_unit(a, u, mt, nt, sub);  // token-tile major: see S8Args
             const int n = nt * kS8BN + nl;
             const bool nok = n < a.N;
             const float swf = nok ? __half2float(__ushort_as_half(a.sw[n])) : 0.0f;
-            const int m0 = mt * kS8BT;
+            const int m0 = mt * kS8BT + (sub < 0 ? 0 : sub * kS8SubT);
+            const int nchunk = (sub < 0 ? kS8BT : kS8SubT) / 32;
 #pragma unroll 1
-            for (int c = 0; c < kS8BT / 32; c++) {
+            for (int c = 0; c < nchunk; c++) {
                 const int mb = m0 + c * 32;
                 if (mb >= a.M) break;
                 uint32_t r[32];
@@ -919,9 +952,12 @@ static int launch_s8(const char* op, const int8_t* A8, const void* W, const uint
     int sms = 0;
     int st = check_device(&sms);
     if (st != G4B_OK) return st;
-    CUtensorMap amap, wmap, rmap;
+    CUtensorMap amap, wmap, rmap, amap_q;
     st = tensor_map_2d(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, A8, (uint64_t)K, (uint64_t)M, (uint64_t)K, kS8BK, kS8BT,
                        CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st == G4B_OK)
+        st = tensor_map_2d(&amap_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, A8, (uint64_t)K, (uint64_t)M, (uint64_t)K, kS8BK,
+                           kS8SubT, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st == G4B_OK) {
         if (W4)
             st = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, W, (uint64_t)N / 8, (uint64_t)K, (uint64_t)N / 2,
@@ -946,11 +982,19 @@ static int launch_s8(const char* op, const int8_t* A8, const void* W, const uint
     a.nkb = (K + kS8BK - 1) / kS8BK;
     a.ntm = (M + kS8BT - 1) / kS8BT;
     a.ntiles = ((N + kS8BN - 1) / kS8BN) * a.ntm;
+    // the last wave's tiles as quarter units when that wave fills at most a quarter of the SMs (W8A8: the
+    // W4A8 requant costs the same per stage whatever the token count, so a quarter unit would not be faster)
+    const int tail = a.ntiles % sms;
+    // G4B_S8_QUARTER_TAIL=0 in the environment keeps whole tiles throughout
+    const char* qenv = std::getenv("G4B_S8_QUARTER_TAIL");
+    const bool quarter = !W4 && !(qenv && std::atoi(qenv) == 0) && tail > 0 && kS8Sub * tail <= sms;
+    a.nfull = quarter ? a.ntiles - tail : a.ntiles;
+    a.nunits = quarter ? a.nfull + kS8Sub * tail : a.ntiles;
     auto kern = y_dtype == G4B_DT_F32 ? gemm_s8_kernel<W4, true> : gemm_s8_kernel<W4, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::kSmem);
     if (e != cudaSuccess) return fail(G4B_E_CUDA, "%s: cudaFuncSetAttribute: %s", op, cudaGetErrorString(e));
-    const int grid = std::min(a.ntiles, sms);
-    kern<<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(a, amap, wmap, rmap);
+    const int grid = std::min(a.nunits, sms);
+    kern<<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(a, amap, wmap, rmap, amap_q);
     count_launch();
     return launch_status(op);
 }

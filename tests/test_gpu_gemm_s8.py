@@ -57,6 +57,25 @@ def test_w8a8_matches_oracle(M, N, K, ydt):
         assert np.array_equal(Y.cpu().numpy(), _epilogue(Cref, sa, pw.sw8)), "f32 outputs differ"
 
 
+@pytest.mark.parametrize("M,N,K", [(300, 384, 160), (2048, 1280, 256)])
+def test_w8a8_quarter_units_give_the_whole_tiles_bits(M, N, K, monkeypatch):
+    """When the last wave of tiles fills at most a quarter of the SMs, each of
+    its tiles runs as four 64-token units; G4B_S8_QUARTER_TAIL=0 keeps whole
+    tiles.  Both give the oracle's bits.  (300, 384, 160): every tile split,
+    the second token tile ragged; (2048, 1280, 256): 80 tiles, a last wave too
+    full to split on a 148-SM part."""
+    pw, dw, A8, sa = _prep(M, N, K, seed=7)
+    Cref, Yref = O.gemm_w8a8(A8, pw.w8, sa, pw.sw8.view(np.uint16))
+    for q in ("1", "0"):
+        monkeypatch.setenv("G4B_S8_QUARTER_TAIL", q)
+        acc = torch.empty((M, N), dtype=torch.int32, device=DEV)
+        Y = ops.gemm_w8a8(torch.from_numpy(A8).to(DEV), torch.from_numpy(sa).to(DEV), dw, acc=acc)
+        torch.cuda.synchronize()
+        assert L.query(L.Q_KERNEL_STATUS) == 0
+        assert np.array_equal(acc.cpu().numpy(), Cref), f"int32 accumulators differ (quarter units {q})"
+        assert np.array_equal(Y.cpu().numpy().view(np.uint16), Yref), f"f16 outputs differ (quarter units {q})"
+
+
 @pytest.mark.parametrize("M,N,K", [s for s in SHAPES if s[1] % 32 == 0])
 def test_w4a8_matches_oracle(M, N, K):
     pw, dw, A8, sa = _prep(M, N, K, seed=2 * M + N + K)
