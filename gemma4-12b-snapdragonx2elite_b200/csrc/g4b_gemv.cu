@@ -1696,10 +1696,18 @@ __global__ void __launch_bounds__(kChainThreads, 1) gemv_i4_chain_kernel(const _
         unsigned ndone = 0;  // ctid 0: tiles of the current step whose y this CTA wrote
 
         for (int j = 0; j < nsteps; j++) {
-            // step j's partial slots are step j-2's: every tile of step j-2 (its reductions
-            // included) is written before they are reused (normally long since)
-            if (j >= 2 && ctid == 0)
-                chain_wait_count(&ch.sync[j - 2], (unsigned)ch.steps[j - 2].done, gabort, abort_flag);
+            // Steps j-2 and j-3 complete (acquire, two threads at once), normally long since:
+            //  - step j's partial slots are step j-2's, so every tile of step j-2 (its reductions
+            //    included) is written before they are reused;
+            //  - a step that reads forwarded or all-reduced x waits on no count before its loads, so
+            //    this is what orders its writes after every read and write of the steps before j-1
+            //    (by induction over the steps: j-2 and j-3 waited the same way) -- a later layer
+            //    overwriting a buffer an earlier step still reads or writes.  The host refuses
+            //    forwarded x where step j's outputs overlap what step j-1 reads or writes.
+            if (j >= 2 && (ctid == 0 || (ctid == 32 && j >= 3))) {
+                const int k = ctid == 0 ? j - 2 : j - 3;
+                chain_wait_count(&ch.sync[k], (unsigned)ch.steps[k].done, gabort, abort_flag);
+            }
             // every consumer is done with step j-1, whose descriptor slot now takes step j+1's
             named_bar_sync(1, kM1Consumers);
             if (j + 1 < nsteps && ctid < kStepWords)
@@ -3421,6 +3429,36 @@ static int chain_check_xform(const g4b_gemv_chain_step* steps, const g4b_chain_x
     return G4B_OK;
 }
 
+// Step j's outputs (every segment's y) against what step j-1 reads from memory (its x, its
+// element-wise inputs) or writes (its outputs, its h_out).  A step that reads forwarded x does not wait
+// for step j-1 to finish, so an overlap there must keep the whole-step wait.
+static bool ranges_overlap(const void* a, size_t na, const void* b, size_t nb) {
+    if (!a || !b || !na || !nb) return false;
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+    return a0 < b0 + nb && b0 < a0 + na;
+}
+static bool chain_outputs_touch_prev(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xf, int j, int x_dtype,
+                                     int y_dtype, bool prev_x_in_memory) {
+    const size_t ysz = y_dtype == G4B_DT_F32 ? 4 : 2, xsz = x_dtype == G4B_DT_F32 ? 4 : 2;
+    const g4b_gemv_chain_step& p = steps[j - 1];
+    for (int i = 0; i < steps[j].nseg; i++) {
+        const void* y = steps[j].seg[i].y;
+        const size_t ny = (size_t)steps[j].seg[i].N * ysz;
+        // (step j-1's own x only when it loads it from memory, not as forwarded or all-reduced words)
+        if (prev_x_in_memory && ranges_overlap(y, ny, p.x, (size_t)p.K * xsz)) return true;
+        for (int q = 0; q < p.nseg; q++)
+            if (ranges_overlap(y, ny, p.seg[q].y, (size_t)p.seg[q].N * ysz)) return true;
+        if (xf && xf[j - 1].kind != G4B_XF_NONE) {
+            const g4b_chain_xform& f = xf[j - 1];
+            const size_t nk = (size_t)p.K;
+            if (ranges_overlap(y, ny, f.a, nk * 4) || ranges_overlap(y, ny, f.b, nk * 4) ||
+                ranges_overlap(y, ny, f.h_out, nk * 4))
+                return true;
+        }
+    }
+    return false;
+}
+
 static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xf, int nsteps, int x_dtype,
                              int scale_fmt, int y_dtype, void* const* peers_dev, int rank, int world,
                              size_t exchange_bytes, g4b_gemv_chain** chain) {
@@ -3522,7 +3560,9 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
             region += (long long)world * cs.seg[0].N;
         }
         if (fwd_on && j > 0 && cs.x && cs.x == steps[j - 1].seg[0].y && !(xf && xf[j].kind != G4B_XF_NONE) &&
-            !(steps[j - 1].flags & G4B_CHAIN_ALLREDUCE) && cs.K <= steps[j - 1].seg[0].N) {
+            !(steps[j - 1].flags & G4B_CHAIN_ALLREDUCE) && cs.K <= steps[j - 1].seg[0].N &&
+            !chain_outputs_touch_prev(steps, xf, j, x_dtype, y_dtype,
+                                      hsteps[j - 1].xfw < 0 && hsteps[j - 1].xreg < 0)) {
             ChainStep& pd = hsteps[j - 1];
             if (pd.yfw < 0) {
                 pd.yfw = (int)fwd_words;

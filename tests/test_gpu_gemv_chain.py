@@ -189,6 +189,36 @@ def test_forwarded_x_gives_the_bits_of_the_whole_step_wait(dt, monkeypatch):
     assert_close(e_out.float().cpu().numpy(), _oracle(e_w[0], x32).astype(np.float32), f"two steps back {tag}")
 
 
+def test_step_overwriting_the_input_of_the_step_before():
+    """Step 1 reads step 0's first output and writes its result over step 0's
+    own input h, which step 0's second segment may still be reading: the chain
+    keeps the whole-step wait there instead of forwarding x.  Step 2 reads the
+    new h (forwarded).  Every output is what the steps give one at a time."""
+    K = 512
+    h0 = torch.from_numpy(activations(1, K, seed=61)[0]).to(DEV)
+    h = h0.clone()
+    a = [_packed(512, K, seed=62, std=K ** -0.5), _packed(768, K, seed=63, std=K ** -0.5)]
+    b = _packed(K, 512, seed=64, std=512 ** -0.5)
+    c = _packed(256, K, seed=65, std=K ** -0.5)
+    ya, yb, yc = (torch.empty(n, dtype=torch.float32, device=DEV) for n in (512, 768, 256))
+    steps = [(h, [a[0][1], a[1][1]], [ya, yb]), (ya, [b[1]], [h]), (h, [c[1]], [yc])]
+    chain = ops.GemvChain(steps)
+    for _ in range(2):
+        h.copy_(h0)
+        chain.run()
+        torch.cuda.synchronize()
+        ra = ops.gemv_i4_fused(h0, [a[0][1], a[1][1]], out_dtype=torch.float32)
+        rb = ops.gemv_i4(ra[0], b[1], out_dtype=torch.float32)
+        rc = ops.gemv_i4(rb, c[1], out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        _assert_same_up_to_order(ya, ra[0], "step 0 segment 0 f32")
+        _assert_same_up_to_order(yb, ra[1], "step 0 segment 1 f32")
+        _assert_same_up_to_order(h, rb, "step 1 (over h) f32")
+        _assert_same_up_to_order(yc, rc, "step 2 f32")
+    assert L.query(L.Q_KERNEL_STATUS) == 0
+    chain.close()
+
+
 @pytest.mark.parametrize("fp8", [False, True])
 def test_chain_config2_shapes(fp8):
     """Two full-size layers of the configs[1] stack and the full lm_head, f16
