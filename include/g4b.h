@@ -200,7 +200,12 @@ G4B_API int g4b_gemv_i4_fused(const void* x, int x_dtype, int nseg, const g4b_ge
  *   run      one launch on `stream` (cooperative: every CTA resident); the
  *            workspace (g4b_gemv_chain_workspace_bytes, 16-byte aligned) is
  *            zero-filled once before first use.  Never allocates or
- *            synchronises; capturable in a CUDA graph.
+ *            synchronises; capturable in a CUDA graph.  A step whose x is the
+ *            step before's first output (same dtype, no element-wise work)
+ *            receives it slice by slice as forwarded words in the workspace
+ *            instead of waiting for the whole step; the results are the same
+ *            bits (G4B_CHAIN_FORWARD=0 in the environment at create turns it
+ *            off).
  *   destroy  frees the plan.
  *
  * Tensor parallel (create_tp): a step flagged G4B_CHAIN_ALLREDUCE (one
@@ -406,7 +411,9 @@ G4B_API int g4b_gemm_i4_fused(const void* X, int x_dtype, int M, int K, const g4
  *            (src/vk_engine.py:152-157) -- used as they are, no repacking
  *   Y        [M, N] f16 or f32 (y_dtype; f32 skips the final f16 rounding)
  *   C_debug  nullable [M, N] int32: the raw accumulators, for exact checks
- * M >= 1, N % 16 == 0, K % 32 == 0. */
+ * M >= 1, N % 16 == 0, K % 32 == 0.  A last wave of tiles that fills at most a
+ * quarter of the SMs runs as quarter-height tiles (the same bits;
+ * G4B_S8_QUARTER_TAIL=0 in the environment keeps whole tiles). */
 G4B_API int g4b_gemm_w8a8(const int8_t* A8, const int8_t* W8, const float* sa, const uint16_t* sw_f16,
                           void* Y, int y_dtype, int32_t* C_debug, int M, int N, int K, g4b_stream_t stream);
 
