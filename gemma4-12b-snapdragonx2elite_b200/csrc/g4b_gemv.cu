@@ -1089,7 +1089,10 @@ __global__ void __launch_bounds__(kM1Threads, 1) gemv_i4_m1_kernel(const M1Args 
 // the engine's recorded command buffer of gemv() dispatches with a barrier
 // after each (src/vk_engine.py:254-290, bar() at :261).  Step j reads x only
 // after every column tile of step j-1 has been written (a per-step count of
-// written tiles); the weight stream runs on from one step into the next.
+// written tiles) -- or, when x is step j-1's first output, each 256-row slice
+// as soon as that slice's tile is (forwarded words) -- and writes only after
+// steps j-2 and j-3 are complete; the weight stream runs on from one step into
+// the next.
 //
 // Each step carries its own partition of (tile, k-chunk) items over the CTAs,
 // chosen on the host: CTA c owns the contiguous items [range[c], range[c+1]).
