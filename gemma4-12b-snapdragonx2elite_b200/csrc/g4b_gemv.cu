@@ -1155,6 +1155,9 @@ struct ChainArgs {
 
 // element-wise work fused into a chain step's activation load (G4B_XF_*)
 constexpr int kXfNone = 0, kXfRmsNorm = 1, kXfNormAdd = 2, kXfGeluMul = 3;
+static_assert(kXfNone == G4B_XF_NONE && kXfRmsNorm == G4B_XF_RMSNORM && kXfNormAdd == G4B_XF_NORMADD &&
+                  kXfGeluMul == G4B_XF_GELU_MUL,
+              "the kernel's element-wise kinds are the header's");
 
 // elements [r0, r0 + 8) of an f32 (F32) or f16 vector as f32, through L2 (the vector may have
 // been written by other SMs during the launch)
@@ -3462,6 +3465,54 @@ static bool chain_outputs_touch_prev(const g4b_gemv_chain_step* steps, const g4b
     return false;
 }
 
+// Where each step's x comes from -- the decisions chain creation makes, on the host only:
+//   fwd[j]    x is step j-1's first output (same dtype, no element-wise work, no all-reduce between them,
+//             no overlap that the whole-step wait would have to order), read as forwarded words;
+//   wlo[j]    the first step whose completion count step j's activation load waits for (it waits for
+//             wlo .. j-1 unless its x is forwarded or all-reduced): back over the forwarded steps, which
+//             waited on no count themselves;
+//   early[j]  x written by no step (no output or h_out range overlaps it): its first slice is loaded
+//             before that wait.
+// G4B_CHAIN_FORWARD=0 in the environment turns forwarding and the early load off.
+struct ChainXPlan {
+    std::vector<int> fwd, wlo, early;
+};
+static ChainXPlan chain_plan_x(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xf, int nsteps, int x_dtype,
+                               int y_dtype) {
+    const char* env = getenv("G4B_CHAIN_FORWARD");
+    const bool off = env && atoi(env) == 0;
+    const bool fwd_on = x_dtype == y_dtype && !off;
+    const size_t ysz = y_dtype == G4B_DT_F32 ? 4 : 2, xsz = x_dtype == G4B_DT_F32 ? 4 : 2;
+    ChainXPlan p;
+    p.fwd.assign(nsteps, 0);
+    p.wlo.assign(nsteps, 0);
+    p.early.assign(nsteps, 0);
+    auto xreg = [&](int j) { return j > 0 && (steps[j - 1].flags & G4B_CHAIN_ALLREDUCE) != 0; };
+    auto xform = [&](int j) { return xf && xf[j].kind != G4B_XF_NONE; };
+    for (int j = 1; j < nsteps; j++) {
+        const g4b_gemv_chain_step& cs = steps[j];
+        p.fwd[j] = fwd_on && cs.x && cs.x == steps[j - 1].seg[0].y && !xform(j) &&
+                   !(steps[j - 1].flags & G4B_CHAIN_ALLREDUCE) && cs.K <= steps[j - 1].seg[0].N &&
+                   !chain_outputs_touch_prev(steps, xf, j, x_dtype, y_dtype, !p.fwd[j - 1] && !xreg(j - 1));
+    }
+    for (int j = 1; j < nsteps; j++) {
+        int lo = j - 1;
+        while (lo > 0 && p.fwd[lo]) lo--;
+        p.wlo[j] = lo;
+        if (off || !steps[j].x || xreg(j) || p.fwd[j] || xform(j)) continue;
+        bool written = false;
+        for (int k = 0; k < nsteps && !written; k++) {
+            for (int i = 0; i < steps[k].nseg && !written; i++)
+                written = ranges_overlap(steps[j].x, (size_t)steps[j].K * xsz, steps[k].seg[i].y,
+                                         (size_t)steps[k].seg[i].N * ysz);
+            if (!written && xf && xf[k].kind == G4B_XF_NORMADD)
+                written = ranges_overlap(steps[j].x, (size_t)steps[j].K * xsz, xf[k].h_out, (size_t)steps[k].K * 4);
+        }
+        p.early[j] = written ? 0 : 1;
+    }
+    return p;
+}
+
 static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xf, int nsteps, int x_dtype,
                              int scale_fmt, int y_dtype, void* const* peers_dev, int rank, int world,
                              size_t exchange_bytes, g4b_gemv_chain** chain) {
@@ -3539,13 +3590,9 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
     size_t sums_words = 0;
     int grid = 1, maxtiles = 0;
     long long region = 0;  // next free exchange word
-    // Forwarded x: a step whose x is the step before's first output (same dtype, no element-wise work,
-    // no all-reduce between them) reads it as epoch-tagged words in the workspace, each 256-row slice
-    // as soon as its own words are stored.  G4B_CHAIN_FORWARD=0 at creation turns it off (and the early
-    // load of an x no step writes).
-    const char* fwd_env = getenv("G4B_CHAIN_FORWARD");
-    const bool fwd_on = x_dtype == y_dtype && !(fwd_env && atoi(fwd_env) == 0);
-    const bool early_on = !(fwd_env && atoi(fwd_env) == 0);
+    // Forwarded x (chain_plan_x): a step whose x is the step before's first output reads it as
+    // epoch-tagged words in the workspace, each 256-row slice as soon as its own words are stored.
+    const ChainXPlan xp = chain_plan_x(steps, xf, nsteps, x_dtype, y_dtype);
     long long fwd_words = 0;
     for (int j = 0; j < nsteps; j++) {
         const g4b_gemv_chain_step& cs = steps[j];
@@ -3556,16 +3603,12 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
         d.yreg = -1;
         d.xfw = -1;
         d.yfw = -1;
-        d.wlo = j > 0 ? j - 1 : 0;
         if (j > 0 && (steps[j - 1].flags & G4B_CHAIN_ALLREDUCE)) d.xreg = hsteps[j - 1].yreg;
         if (cs.flags & G4B_CHAIN_ALLREDUCE) {
             d.yreg = (int)region;
             region += (long long)world * cs.seg[0].N;
         }
-        if (fwd_on && j > 0 && cs.x && cs.x == steps[j - 1].seg[0].y && !(xf && xf[j].kind != G4B_XF_NONE) &&
-            !(steps[j - 1].flags & G4B_CHAIN_ALLREDUCE) && cs.K <= steps[j - 1].seg[0].N &&
-            !chain_outputs_touch_prev(steps, xf, j, x_dtype, y_dtype,
-                                      hsteps[j - 1].xfw < 0 && hsteps[j - 1].xreg < 0)) {
+        if (xp.fwd[j]) {
             ChainStep& pd = hsteps[j - 1];
             if (pd.yfw < 0) {
                 pd.yfw = (int)fwd_words;
@@ -3657,29 +3700,9 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
         }
     }
     G4B_REQUIRE(fwd_words < (1LL << 31), G4B_E_SHAPE, "gemv_chain_create: the forwarded outputs are too long");
-    // the step waits: back over the steps that read forwarded x (they waited on no count), so that a
-    // waiting step still covers every step before it
-    const int ysz = y_dtype == G4B_DT_F32 ? 4 : 2, xsz = xf32 ? 4 : 2;
-    for (int j = 1; j < nsteps; j++) {
-        int lo = j - 1;
-        while (lo > 0 && hsteps[lo].xfw >= 0) lo--;
-        hsteps[j].wlo = lo;
-        // an x no step writes (no output or h_out range overlaps it) may be loaded before the wait
-        const ChainStep& d = hsteps[j];
-        if (!early_on || !d.x || d.xreg >= 0 || d.xfw >= 0 || d.xf_kind != kXfNone) continue;
-        const uintptr_t x0 = reinterpret_cast<uintptr_t>(d.x), x1 = x0 + (uintptr_t)d.K * xsz;
-        bool written = false;
-        for (int k = 0; k < nsteps && !written; k++) {
-            for (int i = 0; i < steps[k].nseg && !written; i++) {
-                const uintptr_t y0 = reinterpret_cast<uintptr_t>(steps[k].seg[i].y);
-                written = y0 < x1 && x0 < y0 + (uintptr_t)steps[k].seg[i].N * ysz;
-            }
-            if (!written && hsteps[k].xf_kind == kXfNormAdd) {
-                const uintptr_t h0 = reinterpret_cast<uintptr_t>(hsteps[k].xf_hout);
-                written = h0 < x1 && x0 < h0 + (uintptr_t)hsteps[k].K * 4;
-            }
-        }
-        hsteps[j].xind = written ? 0 : 1;
+    for (int j = 0; j < nsteps; j++) {
+        hsteps[j].wlo = xp.wlo[j];
+        hsteps[j].xind = xp.early[j];
     }
     // x slice: f32 as f16 hi | lo words, or f16 stored twice over (see chain_xoff16): 1 KB either way,
     // then (f32 x) its 8 block sums
@@ -3740,6 +3763,27 @@ static int chain_create_impl(const g4b_gemv_chain_step* steps, const g4b_chain_x
     c->pf_items = kChainPrefetchItems;
     if (const char* pf = getenv("G4B_CHAIN_PREFETCH")) c->pf_items = std::max(0, std::min(64, atoi(pf)));
     *chain = c;
+    return G4B_OK;
+}
+
+int g4b_gemv_chain_plan(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xforms, int nsteps, int x_dtype,
+                        int y_dtype, g4b_chain_step_plan* out) {
+    G4B_ENTRY("gemv_chain_plan");
+    G4B_REQUIRE(steps && out, G4B_E_ARG, "gemv_chain_plan: NULL pointer argument");
+    G4B_REQUIRE(nsteps >= 1 && nsteps <= kChainMaxSteps, G4B_E_ARG, "gemv_chain_plan: nsteps=%d (1..%d)", nsteps,
+                kChainMaxSteps);
+    G4B_REQUIRE((x_dtype == G4B_DT_F32 || x_dtype == G4B_DT_F16) && (y_dtype == G4B_DT_F32 || y_dtype == G4B_DT_F16),
+                G4B_E_ARG, "gemv_chain_plan: bad dtype %d / %d", x_dtype, y_dtype);
+    for (int j = 0; j < nsteps; j++)
+        G4B_REQUIRE(steps[j].nseg >= 1 && steps[j].nseg <= kTcMaxSeg && steps[j].K > 0, G4B_E_ARG,
+                    "gemv_chain_plan: step %d nseg=%d K=%d", j, steps[j].nseg, steps[j].K);
+    const ChainXPlan xp = chain_plan_x(steps, xforms, nsteps, x_dtype, y_dtype);
+    for (int j = 0; j < nsteps; j++) {
+        out[j].x_forwarded = xp.fwd[j];
+        out[j].wait_from = xp.wlo[j];
+        out[j].x_early = xp.early[j];
+        out[j].reserved = 0;
+    }
     return G4B_OK;
 }
 

@@ -101,6 +101,7 @@ SIGNATURES = {
     "g4b_attn_prefill_prepkv": (_I, [_P, _P, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "g4b_attn_prefill": (_I, [_P, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "g4b_gemv_chain_workspace_bytes": (_Z, [_P]),
+    "g4b_gemv_chain_plan": (_I, [_P, _P, _I, _I, _I, _P]),
     "g4b_gemv_chain_run": (_I, [_P, _P, _Z, _P]),
     "g4b_gemv_chain_run_ex": (_I, [_P, _P, _Z, C.c_uint, _P]),
     "g4b_gemv_chain_destroy": (None, [_P]),
@@ -128,6 +129,11 @@ class ChainXform(C.Structure):
     """struct g4b_chain_xform (include/g4b.h)."""
     _fields_ = [("kind", C.c_int), ("a", C.c_void_p), ("b", C.c_void_p), ("w", C.c_void_p), ("w_post", C.c_void_p),
                 ("h_out", C.c_void_p), ("scale", C.c_float), ("eps", C.c_float)]
+
+
+class ChainStepPlan(C.Structure):
+    """struct g4b_chain_step_plan (include/g4b.h)."""
+    _fields_ = [("x_forwarded", C.c_int), ("wait_from", C.c_int), ("x_early", C.c_int), ("reserved", C.c_int)]
 
 
 class G4BError(RuntimeError):

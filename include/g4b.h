@@ -277,6 +277,28 @@ typedef struct g4b_chain_xform {
  * work between them as one launch. */
 G4B_API int g4b_gemv_chain_create_fused(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xforms, int nsteps,
                                         int x_dtype, int scale_fmt, int y_dtype, g4b_gemv_chain** chain);
+
+/* The chain's plan for where each step's x comes from, as g4b_gemv_chain_create*
+ * decides it, on the host only (no device, nothing allocated; no counterpart in
+ * the reference -- it exposes the barrier decisions for tests and tooling):
+ *   x_forwarded  x is the step before's first output read as forwarded words
+ *                (same dtype, no element-wise work, no all-reduce between them,
+ *                and the step's outputs overlap nothing the step before reads
+ *                from memory or writes);
+ *   wait_from    the first step whose completion its x load waits for (it
+ *                waits for wait_from .. j-1 unless x is forwarded or
+ *                all-reduced);
+ *   x_early      x is written by no step, and its first slice is loaded
+ *                before that wait.
+ * xforms may be NULL.  out has nsteps entries. */
+typedef struct g4b_chain_step_plan {
+    int x_forwarded;
+    int wait_from;
+    int x_early;
+    int reserved;
+} g4b_chain_step_plan;
+G4B_API int g4b_gemv_chain_plan(const g4b_gemv_chain_step* steps, const g4b_chain_xform* xforms, int nsteps,
+                                int x_dtype, int y_dtype, g4b_chain_step_plan* out);
 G4B_API size_t g4b_gemv_chain_workspace_bytes(const g4b_gemv_chain* chain);
 G4B_API int g4b_gemv_chain_run(const g4b_gemv_chain* chain, void* workspace, size_t ws_bytes, g4b_stream_t stream);
 /* g4b_gemv_chain_run with launch flags:
